@@ -1,0 +1,226 @@
+"""Generate the committed golden fixtures under tests/golden/.
+
+Run in a container that has the reference checkout at /root/reference:
+
+    python tests/golden/make_golden.py
+
+Outputs (compressed .npz, raw bit patterns: bf16 as uint16, fp8/e8m0 as uint8):
+
+* act_quant_goldens.npz -- all 36 reference golden cases
+  (QCAU/QCAU_inference/framework/test_vectors/*): c_q and the FP8 codes / E8M0
+  scales that linear() -> act_quant(c_q, 128, "ue8m0") produced on the GPU
+  (model.py:117; the TileLang kernel kernel.py:40-102).
+* attn_goldens.npz -- the same 36 cases' attention inputs (q after query-up,
+  kv, topk_idxs, attn_sink, freqs_cis) and TileLang outputs
+  (qcau_o_after_inverse_rope, and the rope tail of sparse_o_before_inverse_rope).
+  To keep the fixture small, sequence-length-4 cases keep 16 of the 64 heads
+  and sequence-length-16 cases keep 4 (heads are independent in the MQA core,
+  kernel.py:301-343, so a head subset is an exact sub-problem); length-1 cases
+  keep all 64.
+* ref_synthetic.npz -- seeded synthetic inputs run through the reference's
+  own PyTorch CPU path, imported here by file path:
+  kernel_fallback.act_quant / fp8_gemm (QCAU/QCAU_inference/inference/
+  kernel_fallback.py:48-113) and check/QCAU.py (_sparse_attention_online with
+  prob_dtype=bf16, and the whole QCAU() with a callable FP8 Linear).
+"""
+from __future__ import annotations
+
+import importlib.util
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REF = Path("/root/reference")
+FW = REF / "QCAU/QCAU_inference/framework"
+VEC = FW / "test_vectors"
+INF = REF / "QCAU/QCAU_inference/inference"
+OUT = Path(__file__).resolve().parent
+
+
+def load_module(name: str, path: Path):
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def read_shape(case: Path, name: str):
+    return tuple(int(x) for x in (case / f"{name}.shape.txt").read_text().split())
+
+
+def read_hex(case: Path, fname: str, dtype) -> np.ndarray:
+    vals = [int(line, 16) for line in (case / fname).read_text().split()]
+    return np.asarray(vals, dtype=dtype)
+
+
+def read_text(case: Path, fname: str, dtype) -> np.ndarray:
+    return np.asarray((case / fname).read_text().split(), dtype=np.float64).astype(dtype)
+
+
+def head_subset(seq: int, n_heads: int) -> np.ndarray:
+    if seq == 1:
+        return np.arange(n_heads)
+    if seq == 4:
+        return np.arange(0, n_heads, n_heads // 16)
+    return np.arange(0, n_heads, n_heads // 4)
+
+
+def goldens():
+    manifest = json.loads((FW / "manifest.json").read_text())
+    cases = manifest["cases"]
+    aq = {}
+    at = {}
+    for name in cases:
+        case = VEC / name
+        meta = json.loads((case / "metadata.json").read_text())
+        S = meta["seq_len"]
+        H = meta["n_local_heads"]
+        D = meta["head_dim"]
+        cq = read_hex(case, "c_q.bf16_hex.txt", np.uint16).reshape(read_shape(case, "c_q"))
+        x = read_hex(case, "linear_x_after_act_quant.fp8_e4m3_hex.txt", np.uint8)
+        s = read_hex(case, "linear_s_after_act_quant.e8m0_hex.txt", np.uint8)
+        aq[f"{name}/c_q"] = cq.reshape(S, -1)
+        aq[f"{name}/x"] = x.reshape(S, -1)
+        aq[f"{name}/s"] = s.reshape(S, -1)
+
+        hs = head_subset(S, H)
+        q = read_hex(case, "q_after_query_up_rope.bf16_hex.txt", np.uint16).reshape(1, S, H, D)
+        kv_shape = read_shape(case, "kv_after_rope_quant_compress")
+        kv = read_hex(case, "kv_after_rope_quant_compress.bf16_hex.txt", np.uint16).reshape(kv_shape)
+        idx = np.loadtxt(case / "topk_idxs.int.txt", dtype=np.int64).astype(np.int32)
+        idx = idx.reshape(read_shape(case, "topk_idxs"))
+        sink = read_text(case, "attn_sink.fp32.txt", np.float32)
+        fr = read_text(case, "freqs_cis_real.fp32.txt", np.float32).reshape(S, -1)
+        fi = read_text(case, "freqs_cis_imag.fp32.txt", np.float32).reshape(S, -1)
+        o = read_hex(case, "qcau_o_after_inverse_rope.bf16_hex.txt", np.uint16).reshape(1, S, H, D)
+        so = read_hex(case, "sparse_o_before_inverse_rope.bf16_hex.txt", np.uint16).reshape(1, S, H, D)
+        at[f"{name}/heads"] = hs.astype(np.int32)
+        at[f"{name}/q"] = np.ascontiguousarray(q[:, :, hs])
+        at[f"{name}/kv"] = kv
+        at[f"{name}/idx"] = idx
+        at[f"{name}/sink"] = sink[hs]
+        at[f"{name}/freqs"] = np.stack([fr, fi], axis=-1).astype(np.float32)
+        at[f"{name}/qcau_o"] = np.ascontiguousarray(o[:, :, hs])
+        at[f"{name}/sparse_o_tail"] = np.ascontiguousarray(so[:, :, hs, D - 64:])
+        at[f"{name}/scale"] = np.float32(meta["softmax_scale"])
+    aq["cases"] = np.asarray(cases)
+    at["cases"] = np.asarray(cases)
+    np.savez_compressed(OUT / "act_quant_goldens.npz", **aq)
+    np.savez_compressed(OUT / "attn_goldens.npz", **at)
+
+
+def u16(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def u8(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.uint8).numpy()
+
+
+def synthetic():
+    fb = load_module("ref_kernel_fallback", INF / "kernel_fallback.py")
+    cq_mod = load_module("ref_check_qcau", INF / "check" / "QCAU.py")
+    g = torch.Generator().manual_seed(0)
+    out = {}
+
+    # act_quant: fp32 scales (scale_fmt=None), UE8M0 scales, and the in-place
+    # block-64 UE8M0 round trip used on the KV rows (model.py:506).
+    x = (torch.randn(64, 1536, generator=g) * torch.logspace(-3, 2, 64).unsqueeze(1)).bfloat16()
+    x[3, 128:256] = 0  # all-zero block -> amax floor 1e-4
+    y32, s32 = fb.act_quant(x, 128, None, torch.float32)
+    y8, s8 = fb.act_quant(x, 128, "ue8m0", torch.float8_e8m0fnu)
+    kvx = x[:, :448].clone()
+    fb.act_quant(kvx, 64, "ue8m0", torch.float8_e8m0fnu, inplace=True)
+    out["aq/x"] = u16(x)
+    out["aq/y_f32"] = u8(y32)
+    out["aq/s_f32"] = s32.numpy()
+    out["aq/y_ue8m0"] = u8(y8)
+    out["aq/s_ue8m0"] = u8(s8)
+    out["aq/inplace64"] = u16(kvx)
+
+    # fp8_gemm with fp32 block scales, output in the model's default dtype bf16
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        a = (torch.randn(32, 1536, generator=g) * 3).bfloat16()
+        aq_, as_ = fb.act_quant(a, 128, None, torch.float32)
+        w = torch.randn(384, 1536, generator=g) * 0.02
+        # weight scales are per 128x128 block
+        wblk = w.view(3, 128, 12, 128).abs().amax(dim=(1, 3)).clamp_min(1e-4) / 448.0
+        wq_ = (w.view(3, 128, 12, 128) / wblk[:, None, :, None]).clamp(-448, 448).view(384, 1536)
+        wq_ = wq_.to(torch.float8_e4m3fn)
+        c = fb.fp8_gemm(aq_, as_, wq_, wblk.float())
+        out["gemm/a"] = u8(aq_)
+        out["gemm/sa"] = as_.numpy()
+        out["gemm/b"] = u8(wq_)
+        out["gemm/sb"] = wblk.float().numpy()
+        out["gemm/c_bf16"] = u16(c)
+    finally:
+        torch.set_default_dtype(torch.float32)
+
+    # attention core (bf16 P), V4 widths, with -1 holes, an all-invalid tile
+    # and an out-of-range index
+    B, S, H, D, N, K = 1, 3, 16, 512, 300, 200
+    q = torch.randn(B, S, H, D, generator=g).bfloat16()
+    kv = torch.randn(B, N, D, generator=g).bfloat16()
+    idx = torch.randint(0, N, (B, S, K), generator=g, dtype=torch.int64)
+    idx[:, :, 5::7] = -1
+    idx[:, 1, 64:128] = -1
+    idx[:, 2, 0] = N + 5
+    sink = torch.randn(H, generator=g)
+    scale = D ** -0.5
+    o = cq_mod._sparse_attention_online(q, kv, sink, idx, scale, 64, torch.bfloat16)
+    out["attn/q"] = u16(q)
+    out["attn/kv"] = u16(kv)
+    out["attn/idx"] = idx.int().numpy()
+    out["attn/sink"] = sink.numpy()
+    out["attn/scale"] = np.float32(scale)
+    out["attn/o"] = u16(o)
+
+    # whole QCAU (V4 mode) with a callable FP8 projector: act_quant(ue8m0) ->
+    # fp8_gemm, per-head RMSNorm (bf16), RoPE, attention, inverse RoPE
+    Dc, H2, S2, N2, K2 = 1024, 2, 2, 96, 80
+    c_q = torch.randn(1, S2, Dc, generator=g).bfloat16()
+    w2 = torch.randn(H2 * D, Dc, generator=g) * 0.02
+    blk = w2.view(H2 * D // 128, 128, Dc // 128, 128).abs().amax(dim=(1, 3)).clamp_min(1e-4) / 448.0
+    blk = torch.exp2(torch.ceil(torch.log2(blk)))
+    w2q = (w2.view(H2 * D // 128, 128, Dc // 128, 128) / blk[:, None, :, None]).clamp(-448, 448)
+    w2q = w2q.view(H2 * D, Dc).to(torch.float8_e4m3fn)
+
+    def projector(x):
+        xq, xs = fb.act_quant(x, 128, "ue8m0", torch.float8_e8m0fnu)
+        return fb.fp8_gemm(xq, xs, w2q, blk.to(torch.float8_e8m0fnu), torch.float8_e8m0fnu)
+
+    kv2 = torch.randn(1, N2, D, generator=g).bfloat16()
+    idx2 = torch.randint(0, N2, (1, S2, K2), generator=g, dtype=torch.int64)
+    idx2[:, :, 3::5] = -1
+    sink2 = torch.randn(H2, generator=g)
+    ang = torch.randn(S2, 32, generator=g)
+    freqs = torch.polar(torch.ones_like(ang), ang)
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        o2 = cq_mod.QCAU(c_q=c_q, w_uq=projector, kv=kv2, topk_idxs=idx2, attn_sink=sink2,
+                         freqs_cis=freqs, n_local_heads=H2, head_dim=D, rope_head_dim=64,
+                         prob_dtype=torch.bfloat16)
+    finally:
+        torch.set_default_dtype(torch.float32)
+    out["qcau/c_q"] = u16(c_q)
+    out["qcau/w"] = u8(w2q)
+    out["qcau/w_scale_e8m0"] = u8(blk.to(torch.float8_e8m0fnu))
+    out["qcau/kv"] = u16(kv2)
+    out["qcau/idx"] = idx2.int().numpy()
+    out["qcau/sink"] = sink2.numpy()
+    out["qcau/freqs"] = torch.view_as_real(freqs).numpy().astype(np.float32)
+    out["qcau/o"] = u16(o2)
+    np.savez_compressed(OUT / "ref_synthetic.npz", **out)
+
+
+if __name__ == "__main__":
+    if not VEC.exists():
+        sys.exit("reference test vectors not found under /root/reference")
+    goldens()
+    synthetic()
+    for f in sorted(OUT.glob("*.npz")):
+        print(f.name, f.stat().st_size)
