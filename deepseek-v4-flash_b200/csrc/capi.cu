@@ -1,0 +1,543 @@
+// capi.cu -- the C ABI (include/qcau_b200.h): argument validation, error
+// reporting, workspace layout and the orchestration of the multi-kernel
+// entry points.  No entry point synchronises the host or allocates device
+// memory; qcau_device_error() is the only call that synchronises.
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace qcau;
+
+// ---------------------------------------------------------------- errors
+
+static thread_local std::string g_last_error;
+
+static int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+static int fail_cuda(cudaError_t e, const char* what) {
+  if (e == cudaErrorNotSupported)
+    return fail(QCAU_ERR_UNSUPPORTED, std::string(what) + ": shape not supported by any kernel");
+  return fail(QCAU_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define QCAU_CHECK_ARG(cond, msg)                          \
+  do {                                                     \
+    if (!(cond)) return fail(QCAU_ERR_INVALID, (msg));     \
+  } while (0)
+
+#define QCAU_CHECK_CUDA(expr)                              \
+  do {                                                     \
+    cudaError_t e_ = (expr);                               \
+    if (e_ != cudaSuccess) return fail_cuda(e_, #expr);    \
+  } while (0)
+
+// ---------------------------------------------------------------- device error word
+
+__device__ int g_qcau_device_error;
+
+namespace qcau {
+
+int* device_error_word() {
+  static std::mutex mu;
+  static int* addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (addr[dev]) return addr[dev];
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_qcau_device_error) == cudaSuccess) addr[dev] = (int*)p;
+  }
+  return addr[dev];
+}
+
+// ---------------------------------------------------------------- TMA descriptors
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+bool make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+               const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+               CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; i++) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; i++) s[i] = strides_bytes[i];
+  CUresult r = fn(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, s, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+}  // namespace qcau
+
+// ---------------------------------------------------------------- helpers
+
+static inline cudaStream_t to_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+static inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+namespace {
+
+constexpr int kNumSms = 148;
+
+// Number of KV splits of the general split-KV kernel: enough CTAs for two
+// waves over the SMs, at least 4 tiles of 64 keys per split, at most 64.
+int general_splits(int64_t b, int64_t h, int64_t max_len) {
+  const int64_t ctas = b * ((h + 15) / 16);
+  int64_t want = (2 * kNumSms + ctas - 1) / (ctas > 0 ? ctas : 1);
+  const int64_t cap = (max_len + 255) / 256;
+  if (want > cap) want = cap;
+  if (want < 1) want = 1;
+  if (want > 64) want = 64;
+  return (int)want;
+}
+
+// Splits of the tcgen05 two-CTA decode kernel (one CTA pair per 64 heads).
+int sm100_splits(int64_t b, int64_t h, int64_t max_len) {
+  const int64_t pairs = b * (h / 64 > 0 ? h / 64 : 1);
+  const int64_t pair_slots = kNumSms / 2;
+  int64_t want = (4 * pair_slots + pairs - 1) / (pairs > 0 ? pairs : 1);
+  const int64_t cap = (max_len + 511) / 512;
+  if (want > cap) want = cap;
+  if (want < 2) want = 2;
+  if (want > 64) want = 64;
+  return (int)want;
+}
+
+size_t attn_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int splits) {
+  if (splits <= 1) return 0;
+  return align256((size_t)rows * splits * h * d_v * 4) + align256((size_t)rows * splits * h * 2 * 4);
+}
+
+// Runs paged decode attention with partials in `ws` (size checked by caller).
+int run_decode_attn(AttnArgs a, void* ws, cudaStream_t st) {
+  const bool sm100 = decode_attn_sm100_supported(a);
+  a.splits = sm100 ? sm100_splits(a.b, a.h, a.max_len) : general_splits(a.b, a.h, a.max_len);
+  if (a.splits > 1) {
+    a.part_o = reinterpret_cast<float*>(ws);
+    a.part_ml = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) +
+                                         align256((size_t)a.b * a.splits * a.h * a.d_v * 4));
+  }
+  if (sm100) {
+    QCAU_CHECK_CUDA(launch_decode_attn_sm100(a, st));
+  } else {
+    QCAU_CHECK_CUDA(launch_attn_general(a, st));
+  }
+  if (a.splits > 1) QCAU_CHECK_CUDA(launch_attn_combine(a, st));
+  return QCAU_OK;
+}
+
+size_t decode_ws_bytes(int64_t b, int64_t h, int64_t d_v, int64_t max_len) {
+  const size_t w1 = attn_ws_bytes(b, h, d_v, general_splits(b, h, max_len));
+  const size_t w2 = attn_ws_bytes(b, h, d_v, sm100_splits(b, h, max_len));
+  return w1 > w2 ? w1 : w2;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- ABI
+
+extern "C" {
+
+int qcau_version(void) { return 100; }
+
+const char* qcau_last_error(void) { return g_last_error.c_str(); }
+
+int qcau_device_error(void* stream) {
+  QCAU_CHECK_CUDA(cudaStreamSynchronize(to_stream(stream)));
+  int v = 0;
+  QCAU_CHECK_CUDA(cudaMemcpyFromSymbol(&v, g_qcau_device_error, sizeof(int)));
+  if (v) {
+    const int zero = 0;
+    QCAU_CHECK_CUDA(cudaMemcpyToSymbol(g_qcau_device_error, &zero, sizeof(int)));
+  }
+  return v;
+}
+
+int qcau_act_quant(const void* x, void* y, void* s, int64_t m, int64_t n, int32_t block_size,
+                   int32_t round_scale, int32_t scale_dtype, int32_t inplace, void* stream) {
+  QCAU_CHECK_ARG(x != nullptr, "act_quant: x is NULL");
+  QCAU_CHECK_ARG(m >= 0 && n > 0, "act_quant: bad shape");
+  QCAU_CHECK_ARG(block_size == 32 || block_size == 64 || block_size == 128 || block_size == 256,
+                 "act_quant: block_size must be 32, 64, 128 or 256");
+  QCAU_CHECK_ARG(n % block_size == 0, "act_quant: last dimension must be divisible by block_size");
+  QCAU_CHECK_ARG(scale_dtype == QCAU_SCALE_F32 || scale_dtype == QCAU_SCALE_E8M0,
+                 "act_quant: bad scale dtype");
+  QCAU_CHECK_ARG(scale_dtype == QCAU_SCALE_F32 || round_scale,
+                 "act_quant: E8M0 scales require round_scale (scale_fmt='ue8m0')");
+  QCAU_CHECK_ARG(inplace || (y != nullptr && s != nullptr), "act_quant: y/s are NULL");
+  QCAU_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0, "act_quant: x must be 16-byte aligned");
+  QCAU_CHECK_CUDA(launch_act_quant(x, y, s, m, n, block_size, round_scale,
+                                   scale_dtype == QCAU_SCALE_E8M0, inplace, to_stream(stream)));
+  return QCAU_OK;
+}
+
+int qcau_fp8_gemm(const void* a, const void* a_s, const void* b, const void* b_s, void* c,
+                  int64_t m, int64_t n, int64_t k, int32_t scale_dtype, int32_t out_dtype,
+                  void* stream) {
+  QCAU_CHECK_ARG(a && a_s && b && b_s && c, "fp8_gemm: NULL pointer");
+  QCAU_CHECK_ARG(m >= 0 && n > 0 && k > 0, "fp8_gemm: bad shape");
+  QCAU_CHECK_ARG(k % 128 == 0, "fp8_gemm: K must be a multiple of 128");
+  QCAU_CHECK_ARG(n % 128 == 0, "fp8_gemm: N must be a multiple of 128");
+  QCAU_CHECK_ARG(scale_dtype == QCAU_SCALE_F32 || scale_dtype == QCAU_SCALE_E8M0,
+                 "fp8_gemm: bad scale dtype");
+  QCAU_CHECK_ARG(out_dtype == QCAU_OUT_BF16 || out_dtype == QCAU_OUT_F32, "fp8_gemm: bad out dtype");
+  QCAU_CHECK_ARG(((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                   reinterpret_cast<uintptr_t>(c)) & 15) == 0,
+                 "fp8_gemm: operands must be 16-byte aligned");
+  const int e8 = scale_dtype == QCAU_SCALE_E8M0;
+  QCAU_CHECK_CUDA(launch_fp8_gemm(a, a_s, b, b_s, c, m, n, k, e8, e8, out_dtype == QCAU_OUT_F32,
+                                  to_stream(stream)));
+  return QCAU_OK;
+}
+
+int qcau_head_norm_rope(void* q, const void* gamma, const float* freqs, int64_t b, int64_t s,
+                        int64_t h, int64_t d, int64_t row_stride, int64_t rope_dim, int64_t npos,
+                        int64_t pos0, float eps, int32_t do_norm, void* stream) {
+  QCAU_CHECK_ARG(q != nullptr, "head_norm_rope: q is NULL");
+  QCAU_CHECK_ARG(b >= 0 && s >= 0 && h >= 0 && d > 0 && d <= 1024 && d % 2 == 0,
+                 "head_norm_rope: bad shape");
+  QCAU_CHECK_ARG(rope_dim >= 0 && rope_dim % 2 == 0 && rope_dim <= d,
+                 "head_norm_rope: rope_dim must be even and <= head_dim");
+  QCAU_CHECK_ARG(rope_dim == 0 || (freqs != nullptr && pos0 >= 0 && pos0 + s <= npos),
+                 "head_norm_rope: freqs_cis does not cover the query positions");
+  QCAU_CHECK_ARG(row_stride >= d && row_stride % 2 == 0, "head_norm_rope: bad row stride");
+  QCAU_CHECK_CUDA(launch_head_norm_rope(q, gamma, freqs, nullptr, b, s, h, (int)d, row_stride,
+                                        (int)rope_dim, pos0, eps, do_norm, rope_dim > 0, 0,
+                                        to_stream(stream)));
+  return QCAU_OK;
+}
+
+int qcau_rope(void* x, const float* freqs, int64_t b, int64_t s, int64_t h, int64_t d,
+              int64_t row_stride, int64_t rope_dim, int64_t npos, int64_t pos0, int32_t inverse,
+              void* stream) {
+  QCAU_CHECK_ARG(x != nullptr && freqs != nullptr, "rope: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && s >= 0 && h >= 0 && d > 0 && d <= 1024 && d % 2 == 0, "rope: bad shape");
+  QCAU_CHECK_ARG(rope_dim > 0 && rope_dim % 2 == 0 && rope_dim <= d,
+                 "rope: rope_dim must be even and <= head_dim");
+  QCAU_CHECK_ARG(pos0 >= 0 && pos0 + s <= npos, "rope: freqs_cis does not cover the positions");
+  QCAU_CHECK_ARG(row_stride >= d && row_stride % 2 == 0, "rope: bad row stride");
+  QCAU_CHECK_CUDA(launch_head_norm_rope(x, nullptr, freqs, nullptr, b, s, h, (int)d, row_stride,
+                                        (int)rope_dim, pos0, 0.f, 0, 1, inverse,
+                                        to_stream(stream)));
+  return QCAU_OK;
+}
+
+static int check_attn_widths(int64_t d_qk, int64_t d_v, int64_t d_kv, const char* who) {
+  if (!((d_qk == 512 && d_v == 512) || (d_qk == 576 && d_v == 512)))
+    return fail(QCAU_ERR_UNSUPPORTED,
+                std::string(who) + ": supported (d_qk, d_v) are (512, 512) and (576, 512)");
+  if (d_kv < d_qk || d_kv % 8 != 0)
+    return fail(QCAU_ERR_INVALID, std::string(who) + ": kv row width must be >= d_qk and a multiple of 8");
+  return QCAU_OK;
+}
+
+int qcau_sparse_attn(const void* q, const void* kv, const float* attn_sink,
+                     const int32_t* topk_idxs, void* o, int64_t b, int64_t s, int64_t h,
+                     int64_t d_qk, int64_t d_v, int64_t d_kv, int64_t n_kv, int64_t topk,
+                     float softmax_scale, int32_t inv_rope, const float* freqs, int64_t rope_dim,
+                     int64_t npos, int64_t pos0, void* stream) {
+  QCAU_CHECK_ARG(q && kv && topk_idxs && o, "sparse_attn: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && s >= 0 && h > 0 && topk >= 0, "sparse_attn: bad shape");
+  QCAU_CHECK_ARG(n_kv > 0, "sparse_attn: kv must contain at least one latent row");
+  int rc = check_attn_widths(d_qk, d_v, d_kv, "sparse_attn");
+  if (rc) return rc;
+  if (inv_rope) {
+    QCAU_CHECK_ARG(freqs != nullptr && rope_dim > 0 && rope_dim % 4 == 0 && rope_dim <= d_v,
+                   "sparse_attn: bad inverse-RoPE arguments");
+    QCAU_CHECK_ARG(pos0 >= 0 && pos0 + s <= npos, "sparse_attn: freqs_cis does not cover the positions");
+  }
+  AttnArgs a{};
+  a.q = q;
+  a.q_row_stride = d_qk;
+  a.kv = kv;
+  a.idx = topk_idxs;
+  a.sink = attn_sink;
+  a.o = o;
+  a.b = b; a.s = s; a.h = h; a.d_qk = d_qk; a.d_v = d_v; a.d_kv = d_kv; a.n_kv = n_kv;
+  a.topk = topk;
+  a.max_len = topk;
+  a.splits = 1;
+  a.scale = softmax_scale;
+  a.freqs = freqs;
+  a.inv_rope = inv_rope;
+  a.rope_dim = (int)rope_dim;
+  a.pos0 = pos0;
+  QCAU_CHECK_CUDA(launch_attn_general(a, to_stream(stream)));
+  return QCAU_OK;
+}
+
+size_t qcau_forward_workspace_size(int64_t b, int64_t s, int64_t h, int64_t d, int64_t dc) {
+  const size_t rows = (size_t)(b * s);
+  return align256(rows * dc) + align256(rows * (dc / 128) * 4) + align256(rows * h * d * 2);
+}
+
+int qcau_forward(const void* c_q, const void* wq_b, const void* wq_b_scale, int32_t w_scale_dtype,
+                 int32_t act_round_scale, const void* gamma, const void* kv,
+                 const int32_t* topk_idxs, const float* attn_sink, const float* freqs, void* o,
+                 int64_t b, int64_t s, int64_t h, int64_t d, int64_t dc, int64_t n_kv,
+                 int64_t topk, int64_t rope_dim, int64_t npos, int64_t pos0, float norm_eps,
+                 float softmax_scale, void* workspace, size_t workspace_bytes, void* stream) {
+  QCAU_CHECK_ARG(c_q && wq_b && wq_b_scale && kv && topk_idxs && freqs && o,
+                 "qcau_forward: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && s >= 0 && h > 0 && d > 0 && dc > 0, "qcau_forward: bad shape");
+  QCAU_CHECK_ARG(dc % 128 == 0, "qcau_forward: D_C must be a multiple of 128");
+  QCAU_CHECK_ARG((h * d) % 128 == 0, "qcau_forward: H*Dh must be a multiple of 128");
+  QCAU_CHECK_ARG(n_kv > 0, "qcau_forward: kv must contain at least one latent row");
+  QCAU_CHECK_ARG(rope_dim > 0 && rope_dim % 4 == 0 && rope_dim <= d, "qcau_forward: bad rope_dim");
+  QCAU_CHECK_ARG(pos0 >= 0 && pos0 + s <= npos, "qcau_forward: freqs_cis does not cover the positions");
+  QCAU_CHECK_ARG(w_scale_dtype == QCAU_SCALE_F32 || w_scale_dtype == QCAU_SCALE_E8M0,
+                 "qcau_forward: bad scale dtype");
+  int rc = check_attn_widths(d, d, d, "qcau_forward");
+  if (rc) return rc;
+  const size_t need = qcau_forward_workspace_size(b, s, h, d, dc);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(QCAU_ERR_WORKSPACE, "qcau_forward: workspace too small (need " +
+                                        std::to_string(need) + " bytes)");
+  if (b * s == 0) return QCAU_OK;
+  cudaStream_t st = to_stream(stream);
+  const int64_t rows = b * s;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  uint8_t* xq = ws;
+  void* sq = ws + align256(rows * dc);
+  void* q = ws + align256(rows * dc) + align256(rows * (dc / 128) * 4);
+  const int a_e8 = act_round_scale ? 1 : 0;
+  QCAU_CHECK_CUDA(launch_act_quant(c_q, xq, sq, rows, dc, 128, act_round_scale, a_e8, 0, st));
+  QCAU_CHECK_CUDA(launch_fp8_gemm(xq, sq, wq_b, wq_b_scale, q, rows, h * d, dc, a_e8,
+                                  w_scale_dtype == QCAU_SCALE_E8M0, 0, st));
+  QCAU_CHECK_CUDA(launch_head_norm_rope(q, gamma, freqs, nullptr, b, s, h, (int)d, d,
+                                        (int)rope_dim, pos0, norm_eps, 1, 1, 0, st));
+  AttnArgs a{};
+  a.q = q;
+  a.q_row_stride = d;
+  a.kv = kv;
+  a.idx = topk_idxs;
+  a.sink = attn_sink;
+  a.o = o;
+  a.b = b; a.s = s; a.h = h; a.d_qk = d; a.d_v = d; a.d_kv = d; a.n_kv = n_kv; a.topk = topk;
+  a.max_len = topk;
+  a.splits = 1;
+  a.scale = softmax_scale;
+  a.freqs = freqs;
+  a.inv_rope = 1;
+  a.rope_dim = (int)rope_dim;
+  a.pos0 = pos0;
+  QCAU_CHECK_CUDA(launch_attn_general(a, st));
+  return QCAU_OK;
+}
+
+size_t qcau_decode_attn_workspace_size(int64_t b, int64_t h, int64_t d_v, int64_t max_seqlen) {
+  return decode_ws_bytes(b, h, d_v, max_seqlen);
+}
+
+int qcau_decode_attn_paged(const void* q, const void* cache, const int32_t* block_table,
+                           const int32_t* seqlens, const float* attn_sink, void* o, int64_t b,
+                           int64_t h, int64_t d_qk, int64_t d_v, int64_t d_kv, int64_t page_size,
+                           int64_t max_pages, int64_t num_pages, int64_t max_seqlen,
+                           float softmax_scale, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  QCAU_CHECK_ARG(q && cache && block_table && seqlens && o, "decode_attn_paged: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && h > 0 && page_size > 0 && max_pages > 0 && num_pages > 0,
+                 "decode_attn_paged: bad shape");
+  QCAU_CHECK_ARG(max_seqlen >= 0 && max_seqlen <= max_pages * page_size,
+                 "decode_attn_paged: max_seqlen exceeds the block table");
+  int rc = check_attn_widths(d_qk, d_v, d_kv, "decode_attn_paged");
+  if (rc) return rc;
+  const size_t need = qcau_decode_attn_workspace_size(b, h, d_v, max_seqlen);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(QCAU_ERR_WORKSPACE, "decode_attn_paged: workspace too small (need " +
+                                        std::to_string(need) + " bytes)");
+  if (b == 0) return QCAU_OK;
+  AttnArgs a{};
+  a.q = q;
+  a.q_row_stride = d_qk;
+  a.kv = cache;
+  a.block_table = block_table;
+  a.seqlens = seqlens;
+  a.sink = attn_sink;
+  a.o = o;
+  a.b = b; a.s = 1; a.h = h; a.d_qk = d_qk; a.d_v = d_v; a.d_kv = d_kv;
+  a.page_size = page_size;
+  a.max_pages = max_pages;
+  a.num_pages = num_pages;
+  a.max_len = max_seqlen;
+  a.scale = softmax_scale;
+  return run_decode_attn(a, workspace, to_stream(stream));
+}
+
+int qcau_dequant_fp8_weight(const void* w, const void* w_scale, int32_t scale_dtype, void* out_bf16,
+                            int64_t rows, int64_t cols, void* stream) {
+  QCAU_CHECK_ARG(w && w_scale && out_bf16, "dequant_fp8_weight: NULL pointer");
+  QCAU_CHECK_ARG(rows >= 0 && cols >= 0, "dequant_fp8_weight: bad shape");
+  QCAU_CHECK_ARG(scale_dtype == QCAU_SCALE_F32 || scale_dtype == QCAU_SCALE_E8M0,
+                 "dequant_fp8_weight: bad scale dtype");
+  QCAU_CHECK_CUDA(launch_dequant_fp8_weight(w, w_scale, scale_dtype == QCAU_SCALE_E8M0, out_bf16,
+                                            rows, cols, to_stream(stream)));
+  return QCAU_OK;
+}
+
+// Workspace layout of the absorbed decode layer.
+struct MlaWs {
+  size_t xq, sq, q, qabs, olat, ov, xo, so, attn, total;
+};
+
+static MlaWs mla_ws(const qcau_mla_dims* d) {
+  MlaWs w{};
+  const size_t B = (size_t)d->batch, H = (size_t)d->n_heads;
+  const size_t dq = (size_t)(d->d_nope + d->d_rope), dabs = (size_t)(d->kv_lora + d->d_rope);
+  size_t off = 0;
+  w.xq = off; off += align256(B * d->dc);
+  w.sq = off; off += align256(B * (d->dc / 128) * 4);
+  w.q = off; off += align256(B * H * dq * 2);
+  w.qabs = off; off += align256(B * H * dabs * 2);
+  w.olat = off; off += align256(B * H * d->kv_lora * 2);
+  w.ov = off; off += align256(B * H * d->d_v * 2);
+  w.xo = off; off += align256(B * H * d->d_v);
+  w.so = off; off += align256(B * ((H * d->d_v) / 128) * 4);
+  w.attn = off; off += decode_ws_bytes(d->batch, d->n_heads, d->kv_lora, d->max_seqlen);
+  w.total = off;
+  return w;
+}
+
+size_t qcau_mla_decode_workspace_size(const qcau_mla_dims* dims) {
+  return dims ? mla_ws(dims).total : 0;
+}
+
+int qcau_mla_decode(const qcau_mla_dims* d, const void* q_lora, const void* wq_b,
+                    const void* wq_b_scale, const void* wkv_b_bf16, const void* wo,
+                    const void* wo_scale, const void* cache, const int32_t* block_table,
+                    const int32_t* seqlens, const int32_t* positions, const float* freqs, void* y,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  QCAU_CHECK_ARG(d != nullptr, "mla_decode: dims is NULL");
+  QCAU_CHECK_ARG(q_lora && wq_b && wq_b_scale && wkv_b_bf16 && wo && wo_scale && cache &&
+                     block_table && seqlens && positions && freqs && y,
+                 "mla_decode: NULL pointer");
+  QCAU_CHECK_ARG(d->batch >= 0 && d->n_heads > 0 && d->dc > 0 && d->dim > 0,
+                 "mla_decode: bad shape");
+  QCAU_CHECK_ARG(d->d_nope == 128 && d->d_rope == 64 && d->kv_lora == 512 && d->d_v == 128,
+                 "mla_decode: supported head layout is d_nope 128, d_rope 64, kv_lora 512, d_v 128");
+  QCAU_CHECK_ARG(d->dc % 128 == 0 && d->dim % 128 == 0 && (d->n_heads * d->d_v) % 128 == 0 &&
+                     (d->n_heads * (d->d_nope + d->d_rope)) % 128 == 0,
+                 "mla_decode: widths must be multiples of 128");
+  QCAU_CHECK_ARG(d->max_seqlen >= 0 && d->max_seqlen <= d->max_pages * d->page_size,
+                 "mla_decode: max_seqlen exceeds the block table");
+  QCAU_CHECK_ARG(d->w_scale_dtype == QCAU_SCALE_F32 || d->w_scale_dtype == QCAU_SCALE_E8M0,
+                 "mla_decode: bad scale dtype");
+  const MlaWs w = mla_ws(d);
+  if (workspace_bytes < w.total || !workspace)
+    return fail(QCAU_ERR_WORKSPACE, "mla_decode: workspace too small (need " +
+                                        std::to_string(w.total) + " bytes)");
+  if (d->batch == 0) return QCAU_OK;
+  cudaStream_t st = to_stream(stream);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  const int64_t B = d->batch, H = d->n_heads;
+  const int64_t dq = d->d_nope + d->d_rope;
+  const int64_t dabs = d->kv_lora + d->d_rope;
+  const int a_e8 = d->act_round_scale ? 1 : 0;
+  const int w_e8 = d->w_scale_dtype == QCAU_SCALE_E8M0;
+
+  // q = wq_b(act_quant(q_lora))
+  QCAU_CHECK_CUDA(launch_act_quant(q_lora, ws + w.xq, ws + w.sq, B, d->dc, 128,
+                                   d->act_round_scale, a_e8, 0, st));
+  QCAU_CHECK_CUDA(launch_fp8_gemm(ws + w.xq, ws + w.sq, wq_b, wq_b_scale, ws + w.q, B, H * dq,
+                                  d->dc, a_e8, w_e8, 0, st));
+  // RoPE on q_rope (last 64 of each head) at each sequence's position
+  QCAU_CHECK_CUDA(launch_head_norm_rope(ws + w.q, nullptr, freqs, positions, B, 1, H, (int)dq, dq,
+                                        (int)d->d_rope, 0, 0.f, 0, 1, 0, st));
+  // q_abs[:, :, :512] = q_nope . W_UK ;  q_abs[:, :, 512:] = q_rope
+  {
+    BmmArgs m{};
+    m.a = ws + w.q;
+    m.a_bstride = dq;
+    m.a_rstride = H * dq;
+    m.b = wkv_b_bf16;
+    m.b_bstride = (d->d_nope + d->d_v) * d->kv_lora;
+    m.b_rstride = d->kv_lora;
+    m.b_kmajor = 0;
+    m.c = ws + w.qabs;
+    m.c_bstride = dabs;
+    m.c_rstride = H * dabs;
+    m.batch = H;
+    m.m = B;
+    m.n = d->kv_lora;
+    m.k = d->d_nope;
+    QCAU_CHECK_CUDA(launch_bf16_bmm(m, st));
+    QCAU_CHECK_CUDA(cudaMemcpy2DAsync(ws + w.qabs + d->kv_lora * 2, dabs * 2,
+                                      ws + w.q + d->d_nope * 2, dq * 2, d->d_rope * 2,
+                                      (size_t)(B * H), cudaMemcpyDeviceToDevice, st));
+  }
+  // o_lat = attention over the paged latent cache (V = first 512 of each row)
+  {
+    AttnArgs a{};
+    a.q = ws + w.qabs;
+    a.q_row_stride = dabs;
+    a.kv = cache;
+    a.block_table = block_table;
+    a.seqlens = seqlens;
+    a.sink = nullptr;
+    a.o = ws + w.olat;
+    a.b = B; a.s = 1; a.h = H; a.d_qk = dabs; a.d_v = d->kv_lora; a.d_kv = dabs;
+    a.page_size = d->page_size;
+    a.max_pages = d->max_pages;
+    a.num_pages = d->num_pages;
+    a.max_len = d->max_seqlen;
+    a.scale = d->softmax_scale;
+    int rc = run_decode_attn(a, ws + w.attn, st);
+    if (rc) return rc;
+  }
+  // o_v = o_lat . W_UV^T
+  {
+    BmmArgs m{};
+    m.a = ws + w.olat;
+    m.a_bstride = d->kv_lora;
+    m.a_rstride = H * d->kv_lora;
+    m.b = reinterpret_cast<const uint8_t*>(wkv_b_bf16) + d->d_nope * d->kv_lora * 2;
+    m.b_bstride = (d->d_nope + d->d_v) * d->kv_lora;
+    m.b_rstride = d->kv_lora;
+    m.b_kmajor = 1;
+    m.c = ws + w.ov;
+    m.c_bstride = d->d_v;
+    m.c_rstride = H * d->d_v;
+    m.batch = H;
+    m.m = B;
+    m.n = d->d_v;
+    m.k = d->kv_lora;
+    QCAU_CHECK_CUDA(launch_bf16_bmm(m, st));
+  }
+  // y = wo(act_quant(o_v))   (row-parallel partial; the caller all-reduces)
+  QCAU_CHECK_CUDA(launch_act_quant(ws + w.ov, ws + w.xo, ws + w.so, B, H * d->d_v, 128,
+                                   d->act_round_scale, a_e8, 0, st));
+  QCAU_CHECK_CUDA(launch_fp8_gemm(ws + w.xo, ws + w.so, wo, wo_scale, y, B, d->dim, H * d->d_v,
+                                  a_e8, w_e8, d->out_dtype == QCAU_OUT_F32, st));
+  return QCAU_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,90 @@
+// kernels.h -- internal launchers of the QCAU sm_100a kernels (host side).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qcau {
+
+// Host-side TMA descriptor builders (driver entry point resolved once).
+// dims/strides innermost first; strides in bytes for dims 1..rank-1.
+bool make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+               const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+               CUtensorMapSwizzle swizzle);
+
+// Device address of the error word of the current device: a file-scope
+// __device__ int in capi.cu (no allocation), resolved once per device.
+int* device_error_word();
+
+cudaError_t launch_act_quant(const void* x, void* y, void* s, int64_t m, int64_t n, int block,
+                             int round_scale, int scale_e8m0, int inplace, cudaStream_t st);
+
+cudaError_t launch_dequant_fp8_weight(const void* w, const void* s, int scale_e8m0, void* out,
+                                      int64_t rows, int64_t cols, cudaStream_t st);
+
+cudaError_t launch_head_norm_rope(void* q, const void* gamma, const float* freqs,
+                                  const int32_t* positions, int64_t b, int64_t s, int64_t h,
+                                  int d, int64_t row_stride, int rope_dim, int64_t pos0,
+                                  float eps, int do_norm, int do_rope, int inverse,
+                                  cudaStream_t st);
+
+// C[m,n] = two-level FP8 block-scaled GEMM (tcgen05).  out_f32: fp32 C.
+cudaError_t launch_fp8_gemm(const void* a, const void* a_s, const void* b, const void* b_s,
+                            void* c, int64_t m, int64_t n, int64_t k, int a_e8m0, int b_e8m0,
+                            int out_f32, cudaStream_t st);
+
+// Batched bf16 GEMM on tcgen05 for the absorbed-MLA projections:
+//   for each batch g:  C_g[m, n] = A_g[m, k] . B_g^T  with
+//   A_g row r at a + g*a_bstride + r*a_rstride (K contiguous),
+//   B_g given either K-major (row j = output column, K contiguous, b_kmajor=1)
+//   or MN-major (row t = K index, N contiguous, b_kmajor=0),
+//   C_g row r at c + g*c_bstride + r*c_rstride (bf16).  Strides in elements.
+struct BmmArgs {
+  const void* a;
+  int64_t a_bstride, a_rstride;
+  const void* b;
+  int64_t b_bstride, b_rstride;
+  int b_kmajor;
+  void* c;
+  int64_t c_bstride, c_rstride;
+  int64_t batch, m, n, k;
+};
+cudaError_t launch_bf16_bmm(const BmmArgs& args, cudaStream_t st);
+
+// Split-KV attention arguments (gather by index or dense paged).
+struct AttnArgs {
+  const void* q;         // [rows, h, d_qk] where rows = b*s queries
+  int64_t q_row_stride;  // elements between consecutive (query, head) rows
+  const void* kv;        // dense [b, n_kv, d_kv] or paged [pages, page, d_kv]
+  const int32_t* idx;    // [b*s, topk] indices (gather mode) or nullptr
+  const int32_t* block_table;  // [b, max_pages] (paged mode) or nullptr
+  const int32_t* seqlens;      // [b] (paged mode) or nullptr
+  const float* sink;     // [h] or nullptr
+  void* o;               // [rows, h, d_v] bf16
+  float* part_o;         // [rows, splits, h, d_v] fp32 partials (splits > 1)
+  float* part_ml;        // [rows, splits, h, 2] (max in log2 units, sum) partials
+  int64_t b, s, h, d_qk, d_v, d_kv, n_kv, topk;
+  int64_t page_size, max_pages, num_pages;
+  int64_t max_len;       // topk (gather) or max seqlen (paged)
+  int splits;
+  float scale;
+  // inverse RoPE epilogue (V4 QCAU): freqs [npos, rope/2, 2], pos = pos0 + t
+  const float* freqs;
+  int inv_rope;
+  int rope_dim;
+  int64_t pos0;
+};
+
+// General split-KV kernel, mma.sync 16-head tiles (attn_general.cu).
+cudaError_t launch_attn_general(const AttnArgs& args, cudaStream_t st);
+
+// Merge split-KV partials into bf16 outputs (+ optional inverse RoPE).
+cudaError_t launch_attn_combine(const AttnArgs& args, cudaStream_t st);
+
+// tcgen05 two-CTA paged decode attention (h % 64 == 0, d_qk 576, d_v 512,
+// page 64).  Writes partials for the combine kernel.
+cudaError_t launch_decode_attn_sm100(const AttnArgs& args, cudaStream_t st);
+bool decode_attn_sm100_supported(const AttnArgs& args);
+
+}  // namespace qcau

@@ -1,0 +1,223 @@
+"""Absorbed-MLA decode layer on the QCAU kernels, head-sharded over ranks.
+
+One decode step for `batch` sequences (one new token each):
+
+    q      = wq_b(act_quant(q_lora))                 FP8 block-scaled GEMM
+    q_rope = RoPE(q[..., 128:192], position)         freqs_cis at each position
+    q_lat  = q_nope . W_UK[h]                        absorption into the latent space
+    o_lat  = softmax(q_abs . cache^T * scale) . cache[..., :512]   paged decode attention
+    o_v    = o_lat . W_UV[h]^T                       v-up
+    y      = wo(act_quant(o_v))                      row-parallel FP8 GEMM
+    y      = all_reduce(y) over the head shards      NCCL over NVLink
+
+Heads are sharded like the reference's tensor parallelism: wq_b / wkv_b are
+column-parallel (this rank's heads, ColumnParallelLinear model.py:155-163),
+wo is row-parallel with an all-reduce of the partial outputs
+(RowParallelLinear model.py:166-180).  The latent cache is shared by all heads
+(MQA), so every rank reads all of it.
+
+The reference's V4 attention has no wkv_b; this layer serves the absorbed-MLA
+decode configuration (kv_lora 512 + rope 64 cache rows, d_nope 128, d_v 128).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from ._lib import check, lib, stream_ptr
+
+
+@dataclass
+class MLAConfig:
+    n_heads: int = 128          # total heads (all ranks)
+    dc: int = 1536              # q_lora_rank
+    d_nope: int = 128
+    d_rope: int = 64
+    kv_lora: int = 512
+    d_v: int = 128
+    dim: int = 7168
+    page_size: int = 64
+    rope_theta: float = 10000.0
+    act_round_scale: bool = False   # True: UE8M0 activation scales (scale_fmt="ue8m0")
+
+    @property
+    def softmax_scale(self) -> float:
+        return (self.d_nope + self.d_rope) ** -0.5
+
+
+def quantize_weight_fp8(w: torch.Tensor, e8m0: bool = False):
+    """FP8 e4m3 weight with one scale per 128 x 128 block (s = amax/448).
+
+    Weight preparation (not on the decode path).  Rows and columns must be
+    multiples of 128.
+    """
+    R, C = w.shape
+    blk = w.float().view(R // 128, 128, C // 128, 128)
+    s = blk.abs().amax(dim=(1, 3)).clamp_min(1e-4) / 448.0
+    if e8m0:
+        s = torch.exp2(torch.ceil(torch.log2(s)))
+    q = (blk / s[:, None, :, None]).clamp(-448, 448).view(R, C).to(torch.float8_e4m3fn)
+    return q, (s.to(torch.float8_e8m0fnu) if e8m0 else s.contiguous())
+
+
+def precompute_freqs_cis(rope_dim: int, npos: int, theta: float, device) -> torch.Tensor:
+    """RoPE table [npos, rope_dim/2, 2] fp32 (re, im), model.py:198-228 without YaRN."""
+    freqs = 1.0 / (theta ** (torch.arange(0, rope_dim, 2, dtype=torch.float32) / rope_dim))
+    t = torch.arange(npos, dtype=torch.float32)
+    ang = torch.outer(t, freqs)
+    return torch.view_as_real(torch.polar(torch.ones_like(ang), ang)).contiguous().to(device)
+
+
+class MLADecodeLayer:
+    """Holds this rank's weight shards and runs one decode step per call."""
+
+    def __init__(self, cfg: MLAConfig, device, rank: int = 0, world_size: int = 1,
+                 process_group=None):
+        if cfg.n_heads % world_size:
+            raise ValueError("n_heads must be divisible by the number of ranks")
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.rank, self.world_size = rank, world_size
+        self.group = process_group
+        self.n_local = cfg.n_heads // world_size
+        self.wq_b = self.wq_b_scale = None
+        self.wkv_b_bf16 = None
+        self.wo = self.wo_scale = None
+        self._ws = None
+
+    # ------------------------------------------------------------ weights
+    def load_weights(self, wq_b, wq_b_scale, wkv_b, wkv_b_scale, wo, wo_scale,
+                     sharded: bool = False):
+        """Load FP8 weights with 128x128 block scales.
+
+        Unsharded tensors (sharded=False) are sliced to this rank's heads:
+        wq_b [H*(d_nope+d_rope), dc], wkv_b [H*(d_nope+d_v), kv_lora],
+        wo [dim, H*d_v].  Scales are fp32 or float8_e8m0fnu.
+        """
+        c, r, hl = self.cfg, self.rank, self.n_local
+        dq, dkv = c.d_nope + c.d_rope, c.d_nope + c.d_v
+        if not sharded and self.world_size > 1:
+            wq_b = wq_b[r * hl * dq:(r + 1) * hl * dq]
+            wq_b_scale = wq_b_scale[r * hl * dq // 128:(r + 1) * hl * dq // 128]
+            wkv_b = wkv_b[r * hl * dkv:(r + 1) * hl * dkv]
+            wkv_b_scale = wkv_b_scale[r * hl * dkv // 128:(r + 1) * hl * dkv // 128]
+            wo = wo[:, r * hl * c.d_v:(r + 1) * hl * c.d_v]
+            wo_scale = wo_scale[:, r * hl * c.d_v // 128:(r + 1) * hl * c.d_v // 128]
+        dev = self.device
+        self.wq_b = wq_b.to(dev).contiguous()
+        self.wq_b_scale = wq_b_scale.to(dev).contiguous()
+        self.wo = wo.to(dev).contiguous()
+        self.wo_scale = wo_scale.to(dev).contiguous()
+        if self.wq_b_scale.dtype != self.wo_scale.dtype:
+            raise ValueError("wq_b and wo scales must share a dtype")
+        wkv = wkv_b.to(dev).contiguous()
+        wkv_s = wkv_b_scale.to(dev).contiguous()
+        self.wkv_b_bf16 = torch.empty(wkv.shape, device=dev, dtype=torch.bfloat16)
+        check(lib().qcau_dequant_fp8_weight(wkv.data_ptr(), wkv_s.data_ptr(),
+                                            self._scale_code(wkv_s.dtype),
+                                            self.wkv_b_bf16.data_ptr(), wkv.size(0), wkv.size(1),
+                                            stream_ptr(dev)), "dequant wkv_b")
+
+    @staticmethod
+    def _scale_code(dt):
+        if dt == torch.float8_e8m0fnu:
+            return _lib.SCALE_E8M0
+        if dt == torch.float32:
+            return _lib.SCALE_F32
+        raise ValueError(f"unsupported scale dtype {dt}")
+
+    def random_weights(self, seed: int = 0, std: float = 0.02, e8m0: bool = False):
+        """Random-init weights ~N(0, std) quantised to FP8 with block scales.
+
+        Every rank draws the full (unsharded) tensors from the same seed and
+        keeps its shard, so a multi-rank layer equals the single-rank one.
+        Returns the full quantised tensors.
+        """
+        c = self.cfg
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        H = c.n_heads
+        dq, dkv = c.d_nope + c.d_rope, c.d_nope + c.d_v
+
+        def rnd(r, k):
+            return torch.randn(r, k, generator=g, device=self.device) * std
+
+        wq, wqs = quantize_weight_fp8(rnd(H * dq, c.dc), e8m0)
+        wkv, wkvs = quantize_weight_fp8(rnd(H * dkv, c.kv_lora), e8m0)
+        wo, wos = quantize_weight_fp8(rnd(c.dim, H * c.d_v), e8m0)
+        self.load_weights(wq, wqs, wkv, wkvs, wo, wos)
+        return (wq, wqs, wkv, wkvs, wo, wos)
+
+    # ------------------------------------------------------------ step
+    def dims(self, batch: int, max_pages: int, num_pages: int, max_seqlen: int, npos: int,
+             out_fp32: bool = False) -> _lib.MlaDims:
+        c = self.cfg
+        d = _lib.MlaDims()
+        d.batch, d.n_heads, d.dc = batch, self.n_local, c.dc
+        d.d_nope, d.d_rope, d.kv_lora, d.d_v, d.dim = c.d_nope, c.d_rope, c.kv_lora, c.d_v, c.dim
+        d.page_size, d.max_pages, d.num_pages = c.page_size, max_pages, num_pages
+        d.max_seqlen, d.npos = max_seqlen, npos
+        d.softmax_scale = c.softmax_scale
+        d.w_scale_dtype = self._scale_code(self.wq_b_scale.dtype)
+        d.act_round_scale = int(c.act_round_scale)
+        d.out_dtype = _lib.OUT_F32 if out_fp32 else _lib.OUT_BF16
+        return d
+
+    def workspace(self, d: _lib.MlaDims) -> torch.Tensor:
+        need = lib().qcau_mla_decode_workspace_size(d)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(max(need, 1), device=self.device, dtype=torch.uint8)
+        return self._ws
+
+    def forward_local(self, q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen,
+                      y: Optional[torch.Tensor] = None, out_fp32: bool = False) -> torch.Tensor:
+        """This rank's partial y [batch, dim] (no all-reduce)."""
+        B = q_lora.size(0)
+        d = self.dims(B, block_table.size(1), cache.size(0), max_seqlen, freqs.size(0), out_fp32)
+        ws = self.workspace(d)
+        if y is None:
+            y = torch.empty(B, self.cfg.dim, device=self.device,
+                            dtype=torch.float32 if out_fp32 else torch.bfloat16)
+        check(lib().qcau_mla_decode(d, q_lora.data_ptr(), self.wq_b.data_ptr(),
+                                    self.wq_b_scale.data_ptr(), self.wkv_b_bf16.data_ptr(),
+                                    self.wo.data_ptr(), self.wo_scale.data_ptr(), cache.data_ptr(),
+                                    block_table.data_ptr(), seqlens.data_ptr(),
+                                    positions.data_ptr(), freqs.data_ptr(), y.data_ptr(),
+                                    ws.data_ptr(), ws.numel(), stream_ptr(self.device)),
+              "mla_decode")
+        return y
+
+    def forward(self, q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen,
+                y: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y [batch, dim] bf16, summed over the head shards."""
+        y = self.forward_local(q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen, y)
+        if self.world_size > 1:
+            dist.all_reduce(y, group=self.group)
+        return y
+
+
+def make_paged_cache(batch: int, ctx: int, page_size: int, width: int, device, seed: int = 0,
+                     rms_normalise: bool = True):
+    """Synthetic paged latent cache: rows ~N(0,1) RMS-normalised, pages shuffled.
+
+    Returns (cache [batch*ctx/page, page, width] bf16, block_table [batch,
+    ctx/page] int32 = a random permutation of the physical pages, seqlens).
+    """
+    assert ctx % page_size == 0
+    pages = batch * ctx // page_size
+    g = torch.Generator(device=device).manual_seed(seed)
+    cache = torch.empty(pages, page_size, width, device=device, dtype=torch.bfloat16)
+    chunk = max(1, (1 << 28) // (page_size * width * 4))
+    for p0 in range(0, pages, chunk):
+        p1 = min(pages, p0 + chunk)
+        x = torch.randn(p1 - p0, page_size, width, generator=g, device=device)
+        if rms_normalise:
+            x = x * torch.rsqrt(x.square().mean(-1, keepdim=True) + 1e-6)
+        cache[p0:p1] = x.to(torch.bfloat16)
+    perm = torch.randperm(pages, generator=g, device=device).to(torch.int32)
+    table = perm.view(batch, ctx // page_size).contiguous()
+    seqlens = torch.full((batch,), ctx, device=device, dtype=torch.int32)
+    return cache, table, seqlens

@@ -1,0 +1,233 @@
+/*
+ * qcau_b200.h -- C ABI of the B200 (sm_100a) QCAU path.
+ *
+ * The QCAU ("Query-Core Attention Unit") of DeepSeek-V4-Flash runs from the
+ * q_lora activation c_q through the FP8 block-scaled query-up projection,
+ * per-head RMSNorm and RoPE, MQA attention over a shared latent KV row with an
+ * attention sink, and inverse RoPE.  This library implements it as
+ * hand-written CUDA for sm_100a and also serves the absorbed-MLA decode layer
+ * (query absorption into the latent space, dense paged decode attention,
+ * v-up, FP8 output projection).
+ *
+ * Conventions
+ *   - Every pointer is a device pointer unless the name says otherwise; all
+ *     tensors are dense row-major (C-contiguous) with the shapes given.
+ *   - bf16 tensors are passed as void*; FP8 tensors are float8_e4m3fn bytes;
+ *     scale tensors are either fp32 or E8M0 bytes (value 2^(b-127)),
+ *     selected by a qcau_scale_dtype argument.
+ *   - Every call takes a cudaStream_t (passed as void*) and only enqueues
+ *     work: no host synchronisation happens inside any entry point.
+ *   - Return value: QCAU_OK (0) or a negative qcau_status.  On failure
+ *     qcau_last_error() returns a message (thread-local).  Shape or dtype
+ *     errors are reported before anything is enqueued.
+ *   - Device-side anomalies (an index outside its range in a checked mode, a
+ *     pipeline wait that timed out) set a device error word; read it with
+ *     qcau_device_error() after the stream has been synchronised.
+ *   - The library never allocates device memory on its own: callers pass a
+ *     workspace where one is needed, sized by the matching *_workspace_size().
+ *
+ * Reference file:line citations are relative to the reference project root
+ * (dinhthituyetmai05/Deepseek-V4-Flash).
+ */
+#ifndef QCAU_B200_H
+#define QCAU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    QCAU_OK = 0,
+    QCAU_ERR_INVALID = -1,      /* shape / dtype / argument error  (ValueError) */
+    QCAU_ERR_CUDA = -2,         /* CUDA runtime or driver error    (RuntimeError) */
+    QCAU_ERR_UNSUPPORTED = -3,  /* valid but not implemented here  (NotImplementedError) */
+    QCAU_ERR_WORKSPACE = -4,    /* workspace too small             (ValueError) */
+    QCAU_ERR_DEVICE = -5        /* device error word was set        (RuntimeError) */
+} qcau_status;
+
+typedef enum { QCAU_SCALE_F32 = 0, QCAU_SCALE_E8M0 = 1 } qcau_scale_dtype;
+typedef enum { QCAU_OUT_BF16 = 0, QCAU_OUT_F32 = 1 } qcau_out_dtype;
+
+/* Device error word bits (qcau_device_error). */
+#define QCAU_DEVERR_TIMEOUT 1   /* a bounded pipeline wait expired; the kernel returned early */
+#define QCAU_DEVERR_INDEX 2     /* a block-table entry was outside [0, num_pages) */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int qcau_version(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* qcau_last_error(void);
+
+/* Synchronise `stream`, read and clear the device error word of the current
+ * device.  Returns the QCAU_DEVERR_* bits (0 = none) or a negative status. */
+int qcau_device_error(void* stream);
+
+/* ------------------------------------------------------------------------
+ * act_quant -- replaces kernel.act_quant (Deepseek_origin/inference/
+ * kernel.py:105-125, TileLang kernel :40-102; CPU restatement
+ * QCAU/QCAU_inference/inference/kernel_fallback.py:48-64).
+ *   x [m, n] bf16, n % block_size == 0.
+ *   round_scale = 0: s = amax/448 (fp32);  1: s = 2^ceil(log2(amax/448))
+ *   (scale_fmt="ue8m0", kernel.py:22-37).  amax is floored at 1e-4.
+ *   inplace = 0: y [m, n] e4m3 codes, s [m, n/block] in scale_dtype.
+ *   inplace = 1: x is overwritten with bf16(e4m3(x/s) * s); y and s unused
+ *   (may be NULL).  Codes and scales are bit-exact with the reference.
+ * ---------------------------------------------------------------------- */
+int qcau_act_quant(const void* x, void* y, void* s, int64_t m, int64_t n,
+                   int32_t block_size, int32_t round_scale, int32_t scale_dtype,
+                   int32_t inplace, void* stream);
+
+/* ------------------------------------------------------------------------
+ * fp8_gemm -- replaces kernel.fp8_gemm (kernel.py:257-273, TileLang kernel
+ * :203-254; C++ port qcau_c/src/qcau.cpp:30-90).
+ *   c[m, n] = sum_kb (a[m, kb-block] . b[n, kb-block]) * a_s[m, kb] * b_s[n/128, kb]
+ *   a [m, k] e4m3, a_s [m, k/128], b [n, k] e4m3, b_s [n/128, k/128];
+ *   k % 128 == 0, n % 128 == 0; c [m, n] bf16 or fp32 (out_dtype).
+ *   Each 128-wide K block is accumulated in fp32 on the tensor cores and then
+ *   promoted with its two scales into a second fp32 accumulator, as the
+ *   reference's two-level accumulation does.
+ * ---------------------------------------------------------------------- */
+int qcau_fp8_gemm(const void* a, const void* a_s, const void* b, const void* b_s,
+                  void* c, int64_t m, int64_t n, int64_t k, int32_t scale_dtype,
+                  int32_t out_dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * head_norm_rope -- per-head RMSNorm (bf16 arithmetic, model.py:498,
+ * QCAU/QCAU_inference/inference/QCAU.py:16-27, optional gamma [h, d]) followed
+ * by RoPE of the last rope_dim values (model.py:231-243, QCAU.py:30-68), in
+ * place on q [b, s, h, d] bf16.  freqs [npos, rope_dim/2, 2] fp32 (re, im);
+ * row (b, t, .) uses freqs[pos0 + t].  do_norm = 0 skips the RMSNorm.
+ * ---------------------------------------------------------------------- */
+int qcau_head_norm_rope(void* q, const void* gamma, const float* freqs,
+                        int64_t b, int64_t s, int64_t h, int64_t d,
+                        int64_t row_stride, int64_t rope_dim, int64_t npos,
+                        int64_t pos0, float eps, int32_t do_norm, void* stream);
+
+/* RoPE alone, forward or inverse (conjugate), in place on rows of width d
+ * (the rotated values are the last rope_dim of each row); model.py:231-243. */
+int qcau_rope(void* x, const float* freqs, int64_t b, int64_t s, int64_t h,
+              int64_t d, int64_t row_stride, int64_t rope_dim, int64_t npos,
+              int64_t pos0, int32_t inverse, void* stream);
+
+/* ------------------------------------------------------------------------
+ * sparse_attn -- replaces kernel.sparse_attn (kernel.py:355-368, TileLang
+ * kernel :276-352; QCAU.py:126-242; qcau_c/src/qcau.cpp:169-284).
+ *   q [b, s, h, d_qk] bf16, kv [b, n_kv, d_kv] bf16 (d_kv >= d_qk),
+ *   attn_sink [h] fp32 (NULL = no sink), topk_idxs [b, s, topk] int32,
+ *   o [b, s, h, d_v] bf16 with V = kv[..., :d_v] (V4 model: d_v = d_qk = 512).
+ *   Indices outside [0, n_kv) (the reference uses -1) are skipped.  P is
+ *   rounded to bf16 before P.V as kernel.py:340 does; the sink enters the
+ *   denominator once after the loop (kernel.py:345).  A query with no valid
+ *   index returns zeros (QCAU.py:201-242 guard).
+ *   inv_rope = 1 additionally applies the inverse RoPE of the last rope_dim
+ *   values with freqs[pos0 + t] (QCAU.py:313-319) in the epilogue.
+ * ---------------------------------------------------------------------- */
+int qcau_sparse_attn(const void* q, const void* kv, const float* attn_sink,
+                     const int32_t* topk_idxs, void* o, int64_t b, int64_t s,
+                     int64_t h, int64_t d_qk, int64_t d_v, int64_t d_kv,
+                     int64_t n_kv, int64_t topk, float softmax_scale,
+                     int32_t inv_rope, const float* freqs, int64_t rope_dim,
+                     int64_t npos, int64_t pos0, void* stream);
+
+/* ------------------------------------------------------------------------
+ * qcau_forward -- the whole QCAU block, QCAU/QCAU_inference/inference/
+ * QCAU.py:245-319 with w_uq given as the FP8 weight of wq_b
+ * (ColumnParallelLinear, model.py:155-163 -> linear() :108-120):
+ *   act_quant(c_q) -> fp8_gemm(wq_b) -> per-head RMSNorm -> RoPE ->
+ *   sparse attention with sink -> inverse RoPE.
+ *   c_q [b, s, dc] bf16; wq_b [h*d, dc] e4m3; wq_b_scale [h*d/128, dc/128];
+ *   act_round_scale selects the activation scale format (1 = ue8m0, the
+ *   model's scale_fmt); gamma [h, d] bf16 or NULL; kv [b, n_kv, d] bf16;
+ *   topk_idxs [b, s, topk]; attn_sink [h]; freqs [npos, rope_dim/2, 2];
+ *   o [b, s, h, d] bf16.  workspace >= qcau_forward_workspace_size(...).
+ * ---------------------------------------------------------------------- */
+size_t qcau_forward_workspace_size(int64_t b, int64_t s, int64_t h, int64_t d,
+                                   int64_t dc);
+int qcau_forward(const void* c_q, const void* wq_b, const void* wq_b_scale,
+                 int32_t w_scale_dtype, int32_t act_round_scale, const void* gamma,
+                 const void* kv, const int32_t* topk_idxs, const float* attn_sink,
+                 const float* freqs, void* o, int64_t b, int64_t s, int64_t h,
+                 int64_t d, int64_t dc, int64_t n_kv, int64_t topk,
+                 int64_t rope_dim, int64_t npos, int64_t pos0, float norm_eps,
+                 float softmax_scale, void* workspace, size_t workspace_bytes,
+                 void* stream);
+
+/* ------------------------------------------------------------------------
+ * decode_attn_paged -- dense decode attention of one query token per
+ * sequence over a paged latent cache (the decode branch of
+ * Attention.forward, model.py:529-533, with the window/compressed index list
+ * replaced by "all cached tokens"; same numerics as sparse_attn).
+ *   q [b, h, d_qk] bf16; cache [num_pages, page_size, d_kv] bf16;
+ *   block_table [b, max_pages] int32; seqlens [b] int32 (tokens per
+ *   sequence, <= max_pages*page_size); attn_sink [h] or NULL;
+ *   o [b, h, d_v] bf16 (V = cache row[:d_v]).
+ *   Split-KV: partial results go to the workspace and a combine kernel
+ *   merges them (workspace >= qcau_decode_attn_workspace_size(...)).
+ *   On sm_100a with h % 64 == 0, d_qk == 576, d_v == 512, page_size == 64
+ *   this runs the tcgen05 two-CTA kernel; other shapes run the general
+ *   split-KV kernel.
+ * ---------------------------------------------------------------------- */
+size_t qcau_decode_attn_workspace_size(int64_t b, int64_t h, int64_t d_v,
+                                       int64_t max_seqlen);
+int qcau_decode_attn_paged(const void* q, const void* cache,
+                           const int32_t* block_table, const int32_t* seqlens,
+                           const float* attn_sink, void* o, int64_t b, int64_t h,
+                           int64_t d_qk, int64_t d_v, int64_t d_kv,
+                           int64_t page_size, int64_t max_pages, int64_t num_pages,
+                           int64_t max_seqlen, float softmax_scale, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Absorbed-MLA decode layer (BASELINE decode configs; the reference's V4
+ * attention has no wkv_b, so these extend its surface).  Weights:
+ *   wq_b   [h*(d_nope+d_rope), dc] e4m3 + scale [.. /128, dc/128]
+ *   wkv_b  [h*(d_nope+d_v), kv_lora] bf16 (dequantised once from FP8 by
+ *          qcau_dequant_fp8_weight)
+ *   wo     [dim, h*d_v] e4m3 + scale [dim/128, h*d_v/128]   (row-parallel)
+ * Per step:
+ *   act_quant(q_lora) -> fp8_gemm(wq_b) -> RoPE(q_rope at positions[b]) ->
+ *   absorb q_nope . W_UK -> decode_attn_paged -> v-up o_lat . W_UV ->
+ *   act_quant -> fp8_gemm(wo) -> y [b, dim] (bf16 or fp32, to be summed
+ *   over head shards by the caller's all-reduce, as RowParallelLinear does,
+ *   model.py:166-180).
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    int64_t batch;       /* sequences, one query token each            */
+    int64_t n_heads;     /* local heads on this rank                   */
+    int64_t dc;          /* q_lora_rank                                */
+    int64_t d_nope;      /* 128                                        */
+    int64_t d_rope;      /* 64                                         */
+    int64_t kv_lora;     /* 512                                        */
+    int64_t d_v;         /* 128                                        */
+    int64_t dim;         /* model width of the o-projection output     */
+    int64_t page_size;   /* 64                                         */
+    int64_t max_pages;   /* block_table row length                     */
+    int64_t num_pages;   /* physical pages in the cache                */
+    int64_t max_seqlen;  /* upper bound of seqlens[]                   */
+    int64_t npos;        /* rows of freqs                              */
+    float softmax_scale;
+    int32_t w_scale_dtype;   /* scale format of wq_b / wo scales        */
+    int32_t act_round_scale; /* 1: ue8m0 activation scales              */
+    int32_t out_dtype;       /* y dtype                                 */
+} qcau_mla_dims;
+
+/* FP8 weight with 128x128 block scales -> bf16 (one-time weight preparation). */
+int qcau_dequant_fp8_weight(const void* w, const void* w_scale, int32_t scale_dtype,
+                            void* out_bf16, int64_t rows, int64_t cols, void* stream);
+
+size_t qcau_mla_decode_workspace_size(const qcau_mla_dims* dims);
+int qcau_mla_decode(const qcau_mla_dims* dims, const void* q_lora,
+                    const void* wq_b, const void* wq_b_scale, const void* wkv_b_bf16,
+                    const void* wo, const void* wo_scale, const void* cache,
+                    const int32_t* block_table, const int32_t* seqlens,
+                    const int32_t* positions, const float* freqs, void* y,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QCAU_B200_H */
