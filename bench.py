@@ -1,0 +1,346 @@
+"""Benchmark of one absorbed-MLA QCAU decode layer step (B=128, ctx 32K).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N)
+
+Workload (the decode configuration the metric is quoted on): batch 128
+sequences, one new token each, 128 heads split evenly across the N ranks,
+32768 cached tokens per sequence in a paged bf16 latent cache (page 64,
+65,536 physical pages of [64, 576], block tables a random permutation), FP8
+wq_b [128*192, 1536] / wkv_b [128*256, 512] / wo [7168, 16384] with fp32
+128x128 block scales, all-reduce of the bf16 [128, 7168] output over NCCL.
+Synthetic seeded data (no checkpoint or dataset): q_lora ~N(0,1) RMS-normalised,
+weights ~N(0, 0.02), cache rows ~N(0,1) RMS-normalised.
+
+One step = the whole layer for all 128 tokens.  value = 128 * K / (max over
+ranks of the device time of K steps).  The 4.83 GB cache is far larger than
+L2 (126 MB), so no L2 flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "deepseek-v4-flash_b200"))
+
+BATCH, HEADS, CTX, PAGE = 128, 128, 32768, 64
+DC, DIM, WIDTH = 1536, 7168, 576
+METRIC = "QCAU layer decode tok/s (B=128, ctx 32K)"
+MEASURED = REPO / "MEASURED_PEAKS.json"
+
+
+def peaks():
+    try:
+        p = json.loads(MEASURED.read_text())
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        under_load = [s for s, p in zip(sm, power) if p > 0.3 * max(power)] or sm
+        return {"sm_mhz": statistics.median(under_load), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference(steps: int, warmup: int, threads: int):
+    """The reference's qcau_c C++ (oracle/_ref) on this host: one decode token of
+    the same workload per thread per step.  Returns (tok/s, sample text)."""
+    sys.path.insert(0, str(REPO / "oracle"))
+    import oracle as O  # CPU checker / baseline only
+
+    if not O.ref_available():
+        return None, "oracle/_ref/qcau_ref not built"
+    args = (threads, threads, HEADS, WIDTH, CTX, DC, HEADS * 192, DIM)
+    for _ in range(warmup):
+        O.ref_bench_decode(*args)
+    secs = 0.0
+    for _ in range(steps):
+        secs += O.ref_bench_decode(*args)["seconds"]
+    sample = (f"{threads} tokens per step (one per thread), each: qcau_c quant_gemm q-up "
+              f"[1,{DC}]x[{HEADS * 192},{DC}], sparse_attention over {CTX} rows x {HEADS} "
+              f"heads x {WIDTH} (the C++ port has one width for K and V), quant_gemm o-proj "
+              f"[1,{HEADS * 128}]x[{DIM},{HEADS * 128}]; {steps} steps")
+    return threads * steps / secs, sample
+
+
+def traffic_from_profiles():
+    """dram bytes per launch of the decode attention kernel from the committed ncu
+    summary (a line `traffic_bytes_per_launch: N`), or None."""
+    for f in sorted((REPO / "profiles").glob("*.md")):
+        for line in f.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:") and "decode_attn" in f.name:
+                try:
+                    return float(line.split(":", 1)[1].strip().split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    v, sample = cpu_reference(args.steps, args.warmup, threads)
+    if v is None:
+        print(json.dumps({"impl": "reference", "unavailable": sample}))
+        return
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * threads / v,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "absorbed-MLA decode layer, batch 128, 128 heads, ctx 32768",
+                   "global_batch": BATCH, "seq_len": CTX, "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+
+    import qcau_b200
+    from qcau_b200 import _lib
+    from qcau_b200.mla import MLAConfig, MLADecodeLayer, make_paged_cache, precompute_freqs_cis
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=dev)
+    cfg = MLAConfig(n_heads=HEADS, dc=DC, dim=DIM)
+    layer = MLADecodeLayer(cfg, dev, rank=rank, world_size=ws)
+    layer.random_weights(seed=0)
+    cache, table, seqlens = make_paged_cache(BATCH, CTX, PAGE, WIDTH, dev, seed=0)
+    positions = seqlens.clone()
+    freqs = precompute_freqs_cis(64, CTX + 1, cfg.rope_theta, dev)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    q_lora = torch.randn(BATCH, DC, device=dev, generator=gen)
+    q_lora = (q_lora * torch.rsqrt(q_lora.square().mean(-1, keepdim=True))).to(torch.bfloat16)
+    y = torch.empty(BATCH, DIM, device=dev, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        layer.forward(q_lora, cache, table, seqlens, positions, freqs, CTX, y)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    assert _lib.device_error() == 0, "device error during warm-up"
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    value = BATCH * args.steps / (ms_total / 1000.0)
+
+    # ---- dominant kernel alone: the decode attention, timed on its stream
+    L = _lib.lib()
+    H = layer.n_local
+    q_abs = torch.randn(BATCH, H, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
+    o_lat = torch.empty(BATCH, H, 512, device=dev, dtype=torch.bfloat16)
+    need = L.qcau_decode_attn_workspace_size(BATCH, H, 512, CTX)
+    wsb = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+
+    def attn():
+        _lib.check(L.qcau_decode_attn_paged(q_abs.data_ptr(), cache.data_ptr(), table.data_ptr(),
+                                            seqlens.data_ptr(), None, o_lat.data_ptr(), BATCH, H,
+                                            WIDTH, 512, WIDTH, PAGE, table.size(1), cache.size(0),
+                                            CTX, cfg.softmax_scale, wsb.data_ptr(), need,
+                                            _lib.stream_ptr(dev)), "attn")
+
+    for _ in range(3):
+        attn()
+    torch.cuda.synchronize(dev)
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    n_attn = max(5, args.steps)
+    a0.record(stream)
+    for _ in range(n_attn):
+        attn()
+    a1.record(stream)
+    torch.cuda.synchronize(dev)
+    attn_ms = a0.elapsed_time(a1) / n_attn
+    cache_bytes = BATCH * CTX * WIDTH * 2
+    attn_bytes = cache_bytes + BATCH * H * (WIDTH + 512) * 2 + table.numel() * 4
+    attn_flops = 2.0 * BATCH * CTX * H * (WIDTH + 512)
+    hbm, tflops, peak_kind = peaks()
+    t_bw = attn_bytes / (hbm * 1e9)
+    t_tc = attn_flops / (tflops * 1e12)
+    if t_bw >= t_tc:
+        roof = {"bound": "hbm", "achieved": attn_bytes / (attn_ms * 1e-3) / 1e9, "peak": hbm,
+                "unit": "GB/s"}
+    else:
+        roof = {"bound": "tensor", "achieved": attn_flops / (attn_ms * 1e-3) / 1e12,
+                "peak": tflops, "unit": "TFLOP/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = traffic_from_profiles()
+    roof["kernel"] = "decode attention (split-KV + combine), per launch"
+    roof["ms_per_launch"] = attn_ms
+    roof["peak_source"] = f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else peak_kind
+    roof["algorithmic_bytes"] = attn_bytes
+    roof["algorithmic_flops"] = attn_flops
+
+    # ---- end to end through the public API with host buffers
+    q_host = q_lora.cpu().pin_memory()
+    y_host = torch.empty(BATCH, DIM, dtype=torch.bfloat16).pin_memory()
+    q_dev = torch.empty_like(q_lora)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        layer.forward(q_dev, cache, table, seqlens, positions, freqs, CTX, y)
+        y_host.copy_(y, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    b0 = torch.cuda.Event(enable_timing=True)
+    b1 = torch.cuda.Event(enable_timing=True)
+    b0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    b1.record(stream)
+    barrier()
+    te = torch.tensor([b0.elapsed_time(b1)], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_val = BATCH * args.steps / (float(te.item()) / 1000.0)
+    assert _lib.device_error() == 0, "device error during the timed region"
+
+    launches_per_step = 8 + 1  # act_quant, gemm, rope, bmm, attention, combine, bmm, act_quant, gemm
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random weights, cache and activations)",
+            "config": {"workload": "absorbed-MLA QCAU decode layer: batch 128, 128 heads "
+                                   "head-sharded over ranks, ctx 32768, paged bf16 latent "
+                                   "cache page 64, FP8 block-scaled wq_b/wo, bf16 all-reduce "
+                                   "[128,7168]",
+                       "global_batch": BATCH, "seq_len": CTX, "heads_per_rank": H,
+                       "parallelism": f"head-shard tp{ws}",
+                       "l2": "inputs (4.83 GB cache) larger than L2; no flush"},
+            "roofline": roof,
+            "e2e": {"value": e2e_val, "unit": "tok/s",
+                    "h2d_bytes_per_step": q_lora.numel() * 2,
+                    "d2h_bytes_per_step": y.numel() * 2},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+        }
+        if ws == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            v, sample = cpu_reference(1, 0, threads)
+            line["cpu_baseline"] = ({"value": v, "unit": "tok/s", "cores": threads,
+                                     "kind": "reference", "sample": sample}
+                                    if v is not None else {"value": None, "unavailable": sample})
+        print(json.dumps(line))
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,286 @@
+"""GPU parity of the sm_100a kernels against the oracle and the reference's
+golden vectors.  Every call goes through the C ABI of libqcau_b200.so (via the
+qcau_b200 drop-ins).  Tolerances are those of tests/helpers.py."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from helpers import assert_close_attn, cosine, f32, n_bf16, n_u8, t_bf16, t_u8
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    import qcau_b200
+    from qcau_b200 import _lib, kernel
+    from qcau_b200.mla import MLAConfig, MLADecodeLayer, make_paged_cache, precompute_freqs_cis
+
+
+def _no_device_error():
+    assert _lib.device_error() == 0
+
+
+# ------------------------------------------------------------------ act_quant
+
+def test_act_quant_36_goldens_bitwise(golden_dir):
+    g = np.load(golden_dir / "act_quant_goldens.npz")
+    for c in g["cases"]:
+        x = t_bf16(g[f"{c}/c_q"])
+        y, s = kernel.act_quant(x, 128, "ue8m0", torch.float8_e8m0fnu)
+        assert np.array_equal(n_u8(y), g[f"{c}/x"]), c
+        assert np.array_equal(n_u8(s), g[f"{c}/s"]), c
+    _no_device_error()
+
+
+def test_act_quant_modes_bitwise(golden_dir):
+    g = np.load(golden_dir / "ref_synthetic.npz")
+    x = t_bf16(g["aq/x"])
+    y, s = kernel.act_quant(x, 128, None, torch.float32)
+    assert np.array_equal(n_u8(y), g["aq/y_f32"])
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), g["aq/s_f32"].view(np.uint32))
+    y, s = kernel.act_quant(x, 128, "ue8m0", torch.float8_e8m0fnu)
+    assert np.array_equal(n_u8(y), g["aq/y_ue8m0"])
+    assert np.array_equal(n_u8(s), g["aq/s_ue8m0"])
+    kv = x[:, :448].clone()
+    kernel.act_quant(kv, 64, "ue8m0", torch.float8_e8m0fnu, inplace=True)
+    assert np.array_equal(n_bf16(kv), g["aq/inplace64"])
+
+
+def test_act_quant_prefill_size_bitwise():
+    """The prefill activation size [16384, 1536] against the oracle."""
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    x = (torch.randn(16384, 1536, device="cuda", generator=gen) * 4).to(torch.bfloat16)
+    x[7, :128] = 0
+    y, s = kernel.act_quant(x, 128, None, torch.float32)
+    yo, so = O.act_quant(n_bf16(x), 128, False)
+    assert np.array_equal(n_u8(y), yo)
+    assert np.array_equal(s.cpu().numpy(), so)
+
+
+# ------------------------------------------------------------------ fp8_gemm
+
+def test_fp8_gemm_matches_reference(golden_dir):
+    g = np.load(golden_dir / "ref_synthetic.npz")
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        c = kernel.fp8_gemm(t_u8(g["gemm/a"]), torch.from_numpy(g["gemm/sa"]).cuda(),
+                            t_u8(g["gemm/b"]), torch.from_numpy(g["gemm/sb"]).cuda())
+    finally:
+        torch.set_default_dtype(prev)
+    got = f32(n_bf16(c))
+    ref = f32(g["gemm/c_bf16"])
+    assert np.mean(got == ref) > 0.99
+    assert cosine(got, ref) > 0.99999
+    assert np.abs(got - ref).max() <= 2 ** -7 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("m", [1, 32, 128, 200])
+@pytest.mark.parametrize("e8m0", [False, True])
+def test_fp8_gemm_shapes(m, e8m0):
+    gen = torch.Generator(device="cuda").manual_seed(m)
+    n, k = 384, 1536
+    a = (torch.randn(m, k, device="cuda", generator=gen) * 2).to(torch.bfloat16)
+    w = torch.randn(n, k, device="cuda", generator=gen) * 0.02
+    sdt = torch.float8_e8m0fnu if e8m0 else torch.float32
+    aq, asc = kernel.act_quant(a, 128, "ue8m0" if e8m0 else None, sdt)
+    wq, wsc = qcau_b200.mla.quantize_weight_fp8(w, e8m0)
+    c = kernel.fp8_gemm(aq, asc, wq, wsc, sdt)  # default dtype fp32 -> fp32 output
+    assert c.dtype == torch.float32
+    sa = asc.float().cpu().numpy() if not e8m0 else O.e8m0_to_f32(n_u8(asc))
+    sb = wsc.float().cpu().numpy() if not e8m0 else O.e8m0_to_f32(n_u8(wsc))
+    ref = O.fp8_gemm(n_u8(aq), sa, n_u8(wq), sb)
+    got = c.cpu().numpy()
+    assert cosine(got, ref) > 0.99999
+    assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max() + 1e-6
+
+
+# ------------------------------------------------------------------ attention
+
+def _sparse_attn_abi(q, kv, sink, idx, scale, inv_rope=False, freqs=None, pos0=0):
+    B, S, H, D = q.shape
+    o = torch.empty_like(q)
+    f = freqs if freqs is not None else None
+    _lib.check(_lib.lib().qcau_sparse_attn(
+        q.data_ptr(), kv.data_ptr(), None if sink is None else sink.data_ptr(), idx.data_ptr(),
+        o.data_ptr(), B, S, H, D, D, kv.size(-1), kv.size(1), idx.size(-1), float(scale),
+        int(inv_rope), None if f is None else f.data_ptr(), 64, 0 if f is None else f.size(0),
+        pos0, _lib.stream_ptr()), "sparse_attn")
+    return o
+
+
+def test_sparse_attn_inverse_rope_36_goldens(golden_dir):
+    g = np.load(golden_dir / "attn_goldens.npz")
+    exact = total = 0
+    for c in g["cases"]:
+        q = t_bf16(g[f"{c}/q"])
+        kv = t_bf16(g[f"{c}/kv"])
+        idx = torch.from_numpy(g[f"{c}/idx"]).cuda()
+        sink = torch.from_numpy(g[f"{c}/sink"]).cuda()
+        freqs = torch.from_numpy(g[f"{c}/freqs"]).cuda()
+        o = _sparse_attn_abi(q, kv, sink, idx, float(g[f"{c}/scale"]), True, freqs)
+        got = n_bf16(o)
+        ref = g[f"{c}/qcau_o"]
+        exact += int(np.sum(got == ref))
+        total += got.size
+        assert_close_attn(f32(got), f32(ref), c)
+    # most values are bit-identical with the TileLang golden output
+    assert exact / total > 0.8
+    _no_device_error()
+
+
+def test_sparse_attn_matches_reference_edge_cases(golden_dir):
+    g = np.load(golden_dir / "ref_synthetic.npz")
+    o = kernel.sparse_attn(t_bf16(g["attn/q"]), t_bf16(g["attn/kv"]),
+                           torch.from_numpy(g["attn/sink"]).cuda(),
+                           torch.from_numpy(g["attn/idx"]).cuda(), float(g["attn/scale"]))
+    assert_close_attn(f32(n_bf16(o)), f32(g["attn/o"]), "synthetic")
+
+
+@pytest.mark.parametrize("h,topk,n", [(1, 1, 5), (3, 63, 70), (17, 64, 64), (16, 65, 300),
+                                      (64, 200, 1000), (5, 130, 40)])
+def test_sparse_attn_shapes_vs_oracle(h, topk, n):
+    gen = torch.Generator(device="cuda").manual_seed(h * 1000 + topk)
+    B, S, D = 2, 3, 512
+    q = torch.randn(B, S, h, D, device="cuda", generator=gen).to(torch.bfloat16)
+    kv = torch.randn(B, n, D, device="cuda", generator=gen).to(torch.bfloat16)
+    idx = torch.randint(-1, n + 2, (B, S, topk), device="cuda", generator=gen, dtype=torch.int32)
+    idx[0, 0, :] = -1  # a query with no valid key -> zeros
+    sink = torch.randn(h, device="cuda", generator=gen)
+    o = kernel.sparse_attn(q, kv, sink, idx, D ** -0.5)
+    ref = O.sparse_attn(n_bf16(q), n_bf16(kv), sink.cpu().numpy(), idx.cpu().numpy(), D ** -0.5)
+    got = f32(n_bf16(o))
+    assert np.all(got[0, 0] == 0)
+    assert_close_attn(got, f32(O.f32_to_bf16(ref)), f"h{h} k{topk}")
+
+
+# ------------------------------------------------------------------ QCAU block
+
+def _qcau_inputs(golden_dir):
+    g = np.load(golden_dir / "ref_synthetic.npz")
+    w = t_u8(g["qcau/w"])
+    w.scale = t_u8(g["qcau/w_scale_e8m0"], torch.float8_e8m0fnu)
+    freqs = torch.view_as_complex(torch.from_numpy(g["qcau/freqs"]).contiguous()).cuda()
+    return g, w, freqs
+
+
+def test_qcau_fused_matches_reference(golden_dir):
+    g, w, freqs = _qcau_inputs(golden_dir)
+    o = qcau_b200.QCAU(c_q=t_bf16(g["qcau/c_q"]), w_uq=w, kv=t_bf16(g["qcau/kv"]),
+                       topk_idxs=torch.from_numpy(g["qcau/idx"]).cuda(),
+                       attn_sink=torch.from_numpy(g["qcau/sink"]).cuda(), freqs_cis=freqs,
+                       n_local_heads=g["qcau/sink"].shape[0])
+    assert_close_attn(f32(n_bf16(o)), f32(g["qcau/o"]), "QCAU fused")
+    _no_device_error()
+
+
+def test_qcau_callable_projector_matches_reference(golden_dir):
+    g, w, freqs = _qcau_inputs(golden_dir)
+
+    def projector(x):
+        xq, xs = kernel.act_quant(x, 128, "ue8m0", torch.float8_e8m0fnu)
+        prev = torch.get_default_dtype()
+        torch.set_default_dtype(torch.bfloat16)
+        try:
+            return kernel.fp8_gemm(xq, xs, w, w.scale, torch.float8_e8m0fnu)
+        finally:
+            torch.set_default_dtype(prev)
+
+    o = qcau_b200.QCAU(c_q=t_bf16(g["qcau/c_q"]), w_uq=projector, kv=t_bf16(g["qcau/kv"]),
+                       topk_idxs=torch.from_numpy(g["qcau/idx"]).cuda(),
+                       attn_sink=torch.from_numpy(g["qcau/sink"]).cuda(), freqs_cis=freqs)
+    assert_close_attn(f32(n_bf16(o)), f32(g["qcau/o"]), "QCAU callable")
+
+
+def test_qcau_validation_messages(golden_dir):
+    g, w, freqs = _qcau_inputs(golden_dir)
+    with pytest.raises(ValueError, match="attn_sink must match"):
+        qcau_b200.QCAU(c_q=t_bf16(g["qcau/c_q"]), w_uq=w, kv=t_bf16(g["qcau/kv"]),
+                       topk_idxs=torch.from_numpy(g["qcau/idx"]).cuda(),
+                       attn_sink=torch.zeros(5, device="cuda"), freqs_cis=freqs)
+    with pytest.raises(ValueError, match="freqs_cis does not cover"):
+        qcau_b200.QCAU(c_q=t_bf16(g["qcau/c_q"]), w_uq=w, kv=t_bf16(g["qcau/kv"]),
+                       topk_idxs=torch.from_numpy(g["qcau/idx"]).cuda(),
+                       attn_sink=torch.from_numpy(g["qcau/sink"]).cuda(), freqs_cis=freqs[:1],
+                       start_pos=3)
+
+
+# ------------------------------------------------------------------ paged decode
+
+def _decode_abi(q, cache, table, seqlens, sink, scale, d_v, max_seqlen):
+    B, H, dqk = q.shape
+    o = torch.empty(B, H, d_v, device="cuda", dtype=torch.bfloat16)
+    L = _lib.lib()
+    need = L.qcau_decode_attn_workspace_size(B, H, d_v, max_seqlen)
+    ws = torch.empty(max(need, 1), device="cuda", dtype=torch.uint8)
+    _lib.check(L.qcau_decode_attn_paged(q.data_ptr(), cache.data_ptr(), table.data_ptr(),
+                                        seqlens.data_ptr(), None if sink is None else sink.data_ptr(),
+                                        o.data_ptr(), B, H, dqk, d_v, cache.size(-1),
+                                        cache.size(1), table.size(1), cache.size(0), max_seqlen,
+                                        float(scale), ws.data_ptr(), need, _lib.stream_ptr()),
+               "decode_attn_paged")
+    return o
+
+
+@pytest.mark.parametrize("h,seqlens", [(16, [1, 100, 1000]), (128, [4096, 64, 777]),
+                                       (64, [0, 2000, 513])])
+def test_decode_paged_vs_oracle(h, seqlens):
+    gen = torch.Generator(device="cuda").manual_seed(h)
+    B, page, width = len(seqlens), 64, 576
+    max_pages = (max(seqlens) + page - 1) // page
+    pages = B * max_pages + 3
+    cache = torch.randn(pages, page, width, device="cuda", generator=gen).to(torch.bfloat16)
+    table = torch.randperm(pages, device="cuda", generator=gen)[:B * max_pages]
+    table = table.view(B, max_pages).to(torch.int32).contiguous()
+    sl = torch.tensor(seqlens, device="cuda", dtype=torch.int32)
+    q = torch.randn(B, h, width, device="cuda", generator=gen).to(torch.bfloat16)
+    sink = torch.randn(h, device="cuda", generator=gen)
+    scale = 192 ** -0.5
+    o = _decode_abi(q, cache, table, sl, sink, scale, 512, max(seqlens))
+    ref = O.paged_decode_attn(n_bf16(q), n_bf16(cache), table.cpu().numpy(), sl.cpu().numpy(),
+                              sink.cpu().numpy(), scale, 512)
+    assert_close_attn(f32(n_bf16(o)), f32(O.f32_to_bf16(ref)), f"decode h{h}")
+    _no_device_error()
+
+
+# ------------------------------------------------------------------ absorbed decode layer
+
+def _oracle_layer(layer, weights, q_lora, cache, table, seqlens, positions, freqs):
+    c = layer.cfg
+    wq, wqs, wkv, wkvs, wo, wos = [t.cpu() for t in weights]
+    B, H = q_lora.shape[0], c.n_heads
+    xq, xs = O.act_quant(n_bf16(q_lora), 128, False)
+    q = O.f32_to_bf16(O.fp8_gemm(xq, xs, n_u8(wq), wqs.numpy()))
+    q = q.reshape(B, 1, H, 192)
+    # RoPE of q_rope at each sequence's position
+    qr = np.stack([O.rope(q[b:b + 1], freqs, 64, int(positions[b])) for b in range(B)])[:, 0]
+    qr = qr.reshape(B, H, 192)
+    wkv_bf16 = O.f32_to_bf16(O.e4m3_to_f32(n_u8(wkv)) *
+                             np.repeat(np.repeat(wkvs.numpy(), 128, 0), 128, 1))
+    q_lat = O.mla_absorb(qr, wkv_bf16, 128, 128)
+    q_abs = np.concatenate([q_lat, qr[..., 128:]], axis=-1)
+    o_lat = O.paged_decode_attn(q_abs, n_bf16(cache), table, seqlens, None, c.softmax_scale, 512)
+    o_v = O.mla_vup(O.f32_to_bf16(o_lat), wkv_bf16, 128, 128).reshape(B, H * 128)
+    xo, so = O.act_quant(o_v, 128, False)
+    return O.fp8_gemm(xo, so, n_u8(wo), wos.numpy())
+
+
+def test_mla_decode_layer_vs_oracle():
+    cfg = MLAConfig(n_heads=16)
+    layer = MLADecodeLayer(cfg, "cuda")
+    weights = layer.random_weights(seed=1)
+    B, ctx = 4, 256
+    cache, table, seqlens = make_paged_cache(B, ctx, 64, 576, "cuda", seed=2)
+    seqlens = torch.tensor([256, 1, 130, 64], device="cuda", dtype=torch.int32)
+    positions = seqlens.clone()
+    freqs = precompute_freqs_cis(64, 1024, cfg.rope_theta, "cuda")
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    q_lora = torch.randn(B, cfg.dc, device="cuda", generator=gen)
+    q_lora = (q_lora * torch.rsqrt(q_lora.square().mean(-1, keepdim=True))).to(torch.bfloat16)
+    y = layer.forward(q_lora, cache, table, seqlens, positions, freqs, ctx)
+    ref = _oracle_layer(layer, weights, q_lora, cache, table.cpu().numpy(),
+                        seqlens.cpu().numpy(), positions.cpu().numpy(), freqs.cpu().numpy())
+    assert_close_attn(f32(n_bf16(y)), f32(O.f32_to_bf16(ref)), "mla decode layer")
+    _no_device_error()
