@@ -3,7 +3,11 @@ tolerance checks used throughout.
 
 Tolerances (stated once, used by every floating-point parity test):
   * attention / QCAU / decode-layer outputs: cosine >= 0.999 and
-    max |diff| <= 2e-2 * RMS(reference)   (the bar stated for this path);
+    max |diff| <= 2e-2 * RMS(reference)   (the bar stated for this path),
+    where an element may also differ by one bf16 ulp of its reference value:
+    for peaked attention an output element can be ~10x the RMS, and one bf16
+    rounding step of it (2^-8 relative) then exceeds 2e-2 * RMS even though
+    both sides are correctly rounded;
   * GEMM-only outputs additionally: >= 99% of bf16 values within one ulp.
 Integer / byte outputs (FP8 codes, E8M0 scales) must be bit-exact.
 """
@@ -53,7 +57,12 @@ def assert_close_attn(got, ref, what=""):
     assert np.all(np.isfinite(got)), f"{what}: non-finite output"
     rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
     c = cosine(got, ref)
-    m = float(np.abs(got - ref).max()) if got.size else 0.0
+    diff = np.abs(got - ref)
+    m = float(diff.max()) if got.size else 0.0
     assert c >= COS_MIN, f"{what}: cosine {c}"
-    assert m <= MAXABS_RMS * max(rms, 1e-6), f"{what}: max|diff| {m} > {MAXABS_RMS} * rms {rms}"
+    ulp = np.spacing(np.abs(ref).astype(np.float32)) * np.float32(65536.0)  # bf16 ulp
+    tol = np.maximum(np.float32(MAXABS_RMS * max(rms, 1e-6)), ulp)
+    bad = int(np.sum(diff > tol))
+    assert bad == 0, (f"{what}: {bad} elements beyond max(2e-2*rms, 1 bf16 ulp); "
+                      f"max|diff| {m}, rms {rms}")
     return c, m
