@@ -1,14 +1,486 @@
-// attn_decode_sm100.cu -- tcgen05 two-CTA paged decode attention (placeholder
-// until the kernel lands: reports "unsupported" so the general kernel runs).
+// attn_decode_sm100.cu -- tcgen05 two-CTA split-KV decode attention over a
+// paged latent cache (absorbed MLA: 576-wide K rows, V = first 512 values).
+//
+// Numerics are those of the reference attention core
+// (Deepseek_origin/inference/kernel.py:276-352): fp32 scores, online softmax,
+// P rounded to bf16 before P.V, denominator summed from fp32 P; the sink and
+// the final normalisation are applied by attn_combine (kernel.py:345-348).
+// One deliberate difference in the schedule, not in the result: the running
+// max is only raised when a tile's max exceeds it by more than 2^8 (log2
+// units); P and the denominator then share that stale max, so O / l is the
+// same quotient and P stays <= 2^8 (bf16 rounding is scale-free).
+//
+// Work unit = one CTA pair (cluster of 2) x one sequence x one KV split x 128
+// heads.  CTA r of the pair owns heads [64r, 64r+64) of the group:
+//   QK : tcgen05.mma.cta_group::2, M = 128 heads, N = 128 tokens (CTA r
+//        supplies page 2t+r of the 128-token tile), K = 576 in 9 chunks
+//        -> S in TMEM, 2x2 lane layout: lanes 0-63 tokens 0-63, lanes 64-127
+//        tokens 64-127 of the CTA's 64 heads (64 columns, double-buffered)
+//   PV : cta_group::2, M = 128 heads, N = 256 dims (two MMAs cover 512),
+//        K = 128 tokens; A = bf16 P in shared memory, B = V rows given
+//        MN-major (CTA r supplies dims [256j + 128r, +128))
+//        -> O in TMEM: lanes 0-63 dims [256j, +128), lanes 64-127 the next 128
+// Shared memory: Q (64 heads x 576, 72 KB), P (2 x 16 KB), and a ring of
+// 14 x 8 KB TMA slots filled in the order the MMAs consume them:
+// K(0), K(1), V(0), K(2), V(1), ..., V(T-1); a K slot is one page x 64 dims,
+// a V slot is 32 tokens x 128 dims.
+// Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer (pair leader only),
+// 2-5 softmax / O correction / epilogue (one TMEM lane each).
+// Every wait is bounded; a timeout raises QCAU_DEVERR_TIMEOUT, drains the
+// copies in flight, frees TMEM and returns.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace qcau {
+namespace {
 
-bool decode_attn_sm100_supported(const AttnArgs&) { return false; }
+constexpr int kThreads = 192;
+constexpr int kRing = 14;
+constexpr int kSlot = 8192;
+constexpr int kQBytes = 9 * kSlot;   // 64 heads x 576 bf16
+constexpr int kPBytes = 2 * kSlot;   // 64 heads x 128 tokens bf16
+constexpr int kTile = 128;           // tokens per tile (two pages)
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescale = 8.0f;     // raise the running max only beyond 2^8
 
-cudaError_t launch_decode_attn_sm100(const AttnArgs&, cudaStream_t) {
-  return cudaErrorNotSupported;
+constexpr uint32_t kTmemO = 0;       // 2 accumulators x 128 columns
+constexpr uint32_t kTmemS = 256;     // 2 buffers x 64 columns
+constexpr uint32_t kTmemCols = 512;
+
+struct DecodeShared {
+  uint64_t full[kRing];   // leader: slot landed in both CTAs
+  uint64_t empty[kRing];  // both: slot consumed by the MMAs
+  uint64_t q_full;        // leader: Q landed in both CTAs
+  uint64_t s_full[2];     // both: S(t) ready
+  uint64_t s_free[2];     // leader: 8 softmax warps have read S(t)
+  uint64_t p_full[2];     // leader: 8 softmax warps wrote P(t) / corrected O
+  uint64_t p_free[2];     // both: PV(t) done with P(t)
+  uint64_t o_full;        // both: last PV done
+  uint64_t xbar[2];       // local: the 4 softmax warps exchanged tile maxima
+  uint64_t lbar;          // local: denominator exchange
+  float xmax[2][128];
+  float xsum[128];
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr size_t kSmemBytes = 1024 + kQBytes + 2 * kPBytes + (size_t)kRing * kSlot +
+                              sizeof(DecodeShared);
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+
+struct DecodeParams {
+  const int32_t* table;
+  const int32_t* seqlens;
+  float* part_o;
+  float* part_ml;
+  int* err;
+  int64_t max_pages, num_pages;
+  int h, hgroups, splits;
+  float scale;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// All lanes wait; the warp agrees on the outcome (timeouts are per lane).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  const bool ok = mbar_wait<true>(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    decode_attn_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
+                             const __grid_constant__ CUtensorMap tm_k,
+                             const __grid_constant__ CUtensorMap tm_v, DecodeParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  uint8_t* sQ = smem_raw + pad;
+  uint8_t* sP = sQ + kQBytes;
+  uint8_t* sRing = sP + 2 * kPBytes;
+  DecodeShared* sh = reinterpret_cast<DecodeShared*>(sRing + (size_t)kRing * kSlot);
+  volatile int* abort = &sh->abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int64_t unit = blockIdx.x >> 1;
+  const int hg = (int)(unit % p.hgroups);
+  const int64_t rest = unit / p.hgroups;
+  const int split = (int)(rest % p.splits);
+  const int64_t b = rest / p.splits;
+  const int seqlen = p.seqlens[b];
+  const int ntiles = (seqlen + kTile - 1) / kTile;
+  const int t_begin = (int)((int64_t)ntiles * split / p.splits);
+  const int t_end = (int)((int64_t)ntiles * (split + 1) / p.splits);
+  const int T = t_end - t_begin;
+  const int head0 = hg * 128 + (int)rank * 64;
+
+  if (T <= 0) {  // both CTAs of the pair take this branch together
+    for (int i = threadIdx.x; i < 64; i += blockDim.x) {
+      const int64_t prow = (b * p.splits + split) * p.h + head0 + i;
+      p.part_ml[prow * 2] = -INFINITY;
+      p.part_ml[prow * 2 + 1] = 0.f;
+    }
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kRing; i++) {
+      mbar_init(&sh->full[i], 1);
+      mbar_init(&sh->empty[i], 1);
+    }
+    mbar_init(&sh->q_full, 1);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&sh->s_full[i], 1);
+      mbar_init(&sh->s_free[i], 8);
+      mbar_init(&sh->p_full[i], 8);
+      mbar_init(&sh->p_free[i], 1);
+      mbar_init(&sh->xbar[i], 4);
+    }
+    mbar_init(&sh->o_full, 1);
+    mbar_init(&sh->lbar, 4);
+    sh->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc<2>(&sh->tmem_base, kTmemCols);
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+
+  const int pages_used = (seqlen + 63) / 64;
+  auto page_of = [&](int pidx) -> int {
+    if (pidx >= pages_used) pidx = pages_used - 1;  // masked tokens: any valid page
+    const int64_t e = p.table[b * p.max_pages + pidx];
+    if (e < 0 || e >= p.num_pages) {
+      raise_dev_error(p.err, QCAU_DEVERR_INDEX);
+      return 0;
+    }
+    return (int)e;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int last_use[kRing];
+      for (int i = 0; i < kRing; i++) last_use[i] = -1;
+      const uint32_t q_full_l = mapa_shared(smem_u32(&sh->q_full), 0);
+      if (leader) mbar_arrive_expect_tx(&sh->q_full, 2 * kQBytes);
+      for (int k = 0; k < 9; k++)
+        tma_load_3d_pair(sQ + k * kSlot, &tm_q, q_full_l, 64 * k, head0, (int)b);
+      int n = 0;
+      bool ok = true;
+      auto acquire = [&](int& slot) -> bool {
+        slot = n % kRing;
+        const int u = n / kRing;
+        n++;
+        if (!mbar_wait<true>(&sh->empty[slot], (u & 1) ^ 1, abort)) return false;
+        if (leader) mbar_arrive_expect_tx(&sh->full[slot], 2 * kSlot);
+        last_use[slot] = u;
+        return true;
+      };
+      for (int it = 0; it <= T && ok; it++) {
+        if (it < T) {
+          const int page = page_of(2 * (t_begin + it) + (int)rank);
+          for (int k = 0; k < 9 && ok; k++) {
+            int slot;
+            if (!(ok = acquire(slot))) break;
+            tma_load_3d_pair(sRing + slot * kSlot, &tm_k,
+                             mapa_shared(smem_u32(&sh->full[slot]), 0), 64 * k, 0, page);
+          }
+        }
+        if (it >= 1 && ok) {
+          const int t = t_begin + it - 1;
+          for (int j = 0; j < 2 && ok; j++) {
+            const int q0 = 4 * j + 2 * (int)rank;
+            for (int s = 0; s < 4 && ok; s++) {
+              const int page = page_of(2 * t + (s >> 1));
+              int slot;
+              if (!(ok = acquire(slot))) break;
+              const uint32_t fb = mapa_shared(smem_u32(&sh->full[slot]), 0);
+              tma_load_3d_pair(sRing + slot * kSlot, &tm_v, fb, 64 * q0, 32 * (s & 1), page);
+              tma_load_3d_pair(sRing + slot * kSlot + 4096, &tm_v, fb, 64 * (q0 + 1),
+                               32 * (s & 1), page);
+            }
+          }
+        }
+      }
+      if (*abort && leader) {
+        // the leader's full barriers count both CTAs' copies: drain them all
+        volatile int never = 0;
+        mbar_wait<true>(&sh->q_full, 0, &never);
+        for (int i = 0; i < kRing; i++)
+          if (last_use[i] >= 0) mbar_wait<true>(&sh->full[i], last_use[i] & 1, &never);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer (pair leader)
+    if (leader && lane == 0) {
+      const uint32_t idesc_qk = make_idesc(128, 128, kFmtBF16, kFmtBF16, false, false);
+      const uint32_t idesc_pv = make_idesc(128, 256, kFmtBF16, kFmtBF16, false, true);
+      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP), r_addr = smem_u32(sRing);
+      int n = 0, last_slot = -1, last_u = 0;
+      auto take = [&](int& slot) -> bool {
+        slot = n % kRing;
+        const int u = n / kRing;
+        n++;
+        if (!mbar_wait<true>(&sh->full[slot], u & 1, abort)) return false;
+        tc_fence_after();
+        last_slot = slot;
+        last_u = u;
+        return true;
+      };
+      auto qk = [&](int it) -> bool {
+        const int sb = it & 1;
+        if (it >= 2 && !mbar_wait<true>(&sh->s_free[sb], ((it >> 1) - 1) & 1, abort)) return false;
+        tc_fence_after();
+        for (int k = 0; k < 9; k++) {
+          int slot;
+          if (!take(slot)) return false;
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++)
+            mma_bf16_pair(tmem + kTmemS + sb * 64, make_sdesc(q_addr + k * kSlot + kk * 32, 16, 1024),
+                          make_sdesc(r_addr + slot * kSlot + kk * 32, 16, 1024), idesc_qk,
+                          (k | kk) != 0 ? 1u : 0u);
+          tc_commit_pair(&sh->empty[slot], 3);
+        }
+        tc_commit_pair(&sh->s_full[sb], 3);
+        return true;
+      };
+      auto pv = [&](int it) -> bool {
+        const int pb = it & 1;
+        if (!mbar_wait<true>(&sh->p_full[pb], (it >> 1) & 1, abort)) return false;
+        tc_fence_after();
+        for (int j = 0; j < 2; j++) {
+          for (int s = 0; s < 4; s++) {
+            int slot;
+            if (!take(slot)) return false;
+#pragma unroll
+            for (int kk = 0; kk < 2; kk++) {
+              const int ks = 2 * s + kk;  // 16-token step within the tile
+              const uint64_t ad =
+                  make_sdesc(p_addr + pb * kPBytes + (ks >> 2) * kSlot + (ks & 3) * 32, 16, 1024);
+              const uint64_t bd = make_sdesc(r_addr + slot * kSlot + kk * 2048, 4096, 1024);
+              mma_bf16_pair(tmem + kTmemO + j * 128, ad, bd, idesc_pv,
+                            (it > 0 || s > 0 || kk > 0) ? 1u : 0u);
+            }
+            tc_commit_pair(&sh->empty[slot], 3);
+          }
+        }
+        tc_commit_pair(&sh->p_free[pb], 3);
+        return true;
+      };
+      bool ok = mbar_wait<true>(&sh->q_full, 0, abort);
+      tc_fence_after();
+      if (ok) ok = qk(0);
+      for (int it = 1; it < T && ok; it++) {
+        ok = qk(it);
+        if (ok) ok = pv(it - 1);
+      }
+      if (ok) ok = pv(T - 1);
+      if (ok) tc_commit_pair(&sh->o_full, 3);
+      if (*abort && last_slot >= 0) {
+        // the MMAs issued so far finish before TMEM and the slots go away
+        volatile int never = 0;
+        mbar_wait<true>(&sh->empty[last_slot], last_u & 1, &never);
+      }
+    }
+  } else {
+    // ------------------------------------------------ softmax / correction / epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // TMEM lane
+    const int hl = row & 63, half = row >> 6;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const float sl2 = p.scale * kLog2e;
+    const uint32_t s_free_l[2] = {mapa_shared(smem_u32(&sh->s_free[0]), 0),
+                                  mapa_shared(smem_u32(&sh->s_free[1]), 0)};
+    const uint32_t p_full_l[2] = {mapa_shared(smem_u32(&sh->p_full[0]), 0),
+                                  mapa_shared(smem_u32(&sh->p_full[1]), 0)};
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int it = 0; it < T && ok; it++) {
+      const int sb = it & 1;
+      if (!(ok = warp_wait(&sh->s_full[sb], (it >> 1) & 1, abort))) break;
+      tc_fence_after();
+      float s[64];
+      {
+        float v0[32], v1[32];
+        tmem_ld32(tmem + lane_base + kTmemS + sb * 64, v0);
+        tmem_ld32(tmem + lane_base + kTmemS + sb * 64 + 32, v1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          s[i] = v0[i];
+          s[32 + i] = v1[i];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(s_free_l[sb]);
+
+      const int tok0 = (t_begin + it) * kTile + half * 64;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; i++) {
+        s[i] = (tok0 + i < seqlen) ? s[i] * sl2 : -INFINITY;
+        mx = fmaxf(mx, s[i]);
+      }
+      sh->xmax[sb][row] = mx;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->xbar[sb]);
+      if (!(ok = warp_wait(&sh->xbar[sb], (it >> 1) & 1, abort))) break;
+      const float tmax = fmaxf(mx, sh->xmax[sb][row ^ 64]);
+      float alpha = 1.f;
+      bool resc = false;
+      if (m_run == -INFINITY) {
+        m_run = tmax;  // first tile: PV starts a fresh accumulator
+      } else if (tmax > m_run + kRescale) {
+        alpha = exp2f(m_run - tmax);
+        m_run = tmax;
+        resc = true;
+      }
+      uint32_t pk[32];
+      float ps = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; i++) {
+        const float p0 = exp2f(s[2 * i] - m_run);
+        const float p1 = exp2f(s[2 * i + 1] - m_run);
+        ps += p0 + p1;
+        pk[i] = pack_bf16(p0, p1);
+      }
+      l_run = l_run * alpha + ps;
+
+      // P(t) reuses the buffer of P(t-2): PV(t-2) must be done with it
+      if (it >= 2 && !(ok = warp_wait(&sh->p_free[sb], ((it >> 1) - 1) & 1, abort))) break;
+      if (__any_sync(0xffffffffu, resc)) {
+        // O holds tiles < t once PV(t-1) is done; rescale this warp's rows
+        if (it >= 1 && !(ok = warp_wait(&sh->p_free[sb ^ 1], ((it - 1) >> 1) & 1, abort))) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 8; c++) {
+          float v[32];
+          const uint32_t ta = tmem + lane_base + kTmemO + c * 32;
+          tmem_ld32(ta, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; i++) v[i] *= alpha;
+          tmem_st32(ta, v);
+        }
+        tmem_st_wait();
+      }
+      uint8_t* prow = sP + sb * kPBytes + half * kSlot + hl * 128;
+#pragma unroll
+      for (int c = 0; c < 8; c++)
+        *reinterpret_cast<uint4*>(prow + ((c ^ (hl & 7)) << 4)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(p_full_l[sb]);
+    }
+    if (ok) ok = warp_wait(&sh->o_full, 0, abort);
+    sh->xsum[row] = l_run;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sh->lbar);
+    if (ok) ok = warp_wait(&sh->lbar, 0, abort);
+    if (ok) {
+      tc_fence_after();
+      const float l_tot = l_run + sh->xsum[row ^ 64];
+      const int64_t prow = (b * p.splits + split) * p.h + head0 + hl;
+      float* po = p.part_o + prow * 512 + 128 * half;
+#pragma unroll 1
+      for (int c = 0; c < 8; c++) {
+        float v[32];
+        tmem_ld32(tmem + lane_base + kTmemO + c * 32, v);
+        tmem_ld_wait();
+        float4* dst = reinterpret_cast<float4*>(po + (c >> 2) * 256 + (c & 3) * 32);
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+          dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+      }
+      if (half == 0) {
+        p.part_ml[prow * 2] = m_run;
+        p.part_ml[prow * 2 + 1] = l_tot;
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<2>(tmem, kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort) raise_dev_error(p.err, QCAU_DEVERR_TIMEOUT);
+}
+
+bool is_sm100_device() {
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  return major == 10 && minor == 0;
+}
+
+}  // namespace
+
+bool decode_attn_sm100_supported(const AttnArgs& a) {
+  return a.block_table != nullptr && a.seqlens != nullptr && a.s == 1 && a.d_qk == 576 &&
+         a.d_v == 512 && a.d_kv == 576 && a.page_size == 64 && a.h % 128 == 0 &&
+         a.q_row_stride == 576 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(a.kv) & 15) == 0 && a.num_pages < (1LL << 31) &&
+         a.max_pages < (1LL << 30) && is_sm100_device();
+}
+
+cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
+  if (!decode_attn_sm100_supported(a)) return cudaErrorNotSupported;
+  if (a.b == 0) return cudaSuccess;
+  CUtensorMap tq, tk, tv;
+  {
+    const uint64_t dims[3] = {576, (uint64_t)a.h, (uint64_t)a.b};
+    const uint64_t strides[2] = {1152, (uint64_t)a.h * 1152};
+    const uint32_t box[3] = {64, 64, 1};
+    if (!make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.q, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+  }
+  {
+    const uint64_t dims[3] = {576, 64, (uint64_t)a.num_pages};
+    const uint64_t strides[2] = {1152, 64 * 1152};
+    const uint32_t box_k[3] = {64, 64, 1};
+    const uint32_t box_v[3] = {64, 32, 1};
+    if (!make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.kv, dims, strides, box_k,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.kv, dims, strides, box_v,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+  }
+  DecodeParams p;
+  p.table = a.block_table;
+  p.seqlens = a.seqlens;
+  p.part_o = a.part_o;
+  p.part_ml = a.part_ml;
+  p.err = device_error_word();
+  p.max_pages = a.max_pages;
+  p.num_pages = a.num_pages;
+  p.h = (int)a.h;
+  p.hgroups = (int)(a.h / 128);
+  p.splits = a.splits;
+  p.scale = a.scale;
+  cudaError_t e = cudaFuncSetAttribute(decode_attn_sm100_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const int64_t units = a.b * a.splits * p.hgroups;
+  decode_attn_sm100_kernel<<<(unsigned)(2 * units), kThreads, kSmemBytes, st>>>(tq, tk, tv, p);
+  return cudaGetLastError();
 }
 
 }  // namespace qcau

@@ -120,20 +120,30 @@ int general_splits(int64_t b, int64_t h, int64_t max_len) {
   return (int)want;
 }
 
-// Splits of the tcgen05 two-CTA decode kernel (one CTA pair per 64 heads).
+// Splits of the tcgen05 two-CTA decode kernel: one CTA pair per (sequence,
+// 128-head group, split), one pair per two SMs.  Pick the split count whose
+// last wave is fullest (at least 4 tiles of 128 tokens per split).
 int sm100_splits(int64_t b, int64_t h, int64_t max_len) {
-  const int64_t pairs = b * (h / 64 > 0 ? h / 64 : 1);
-  const int64_t pair_slots = kNumSms / 2;
-  int64_t want = (4 * pair_slots + pairs - 1) / (pairs > 0 ? pairs : 1);
-  const int64_t cap = (max_len + 511) / 512;
-  if (want > cap) want = cap;
-  if (want < 2) want = 2;
-  if (want > 64) want = 64;
-  return (int)want;
+  const int64_t pairs = b * (h / 128 > 0 ? h / 128 : 1);
+  const int64_t slots = kNumSms / 2;
+  const int64_t cap = (max_len + 511) / 512 > 0 ? (max_len + 511) / 512 : 1;
+  int best = 1;
+  double best_score = -1.0;
+  for (int s = 1; s <= 32 && s <= cap; s++) {
+    const double units = (double)(pairs * s);
+    const double waves = units / (double)slots;
+    const double eff = waves / (double)((int64_t)((units + slots - 1) / slots));
+    const double score = eff - 0.004 * s;  // partials cost a little per split
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = s;
+    }
+  }
+  return best;
 }
 
-size_t attn_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int splits) {
-  if (splits <= 1) return 0;
+size_t attn_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int splits, bool always = false) {
+  if (splits <= 1 && !always) return 0;
   return align256((size_t)rows * splits * h * d_v * 4) + align256((size_t)rows * splits * h * 2 * 4);
 }
 
@@ -141,7 +151,7 @@ size_t attn_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int splits) {
 int run_decode_attn(AttnArgs a, void* ws, cudaStream_t st) {
   const bool sm100 = decode_attn_sm100_supported(a);
   a.splits = sm100 ? sm100_splits(a.b, a.h, a.max_len) : general_splits(a.b, a.h, a.max_len);
-  if (a.splits > 1) {
+  if (a.splits > 1 || sm100) {
     a.part_o = reinterpret_cast<float*>(ws);
     a.part_ml = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) +
                                          align256((size_t)a.b * a.splits * a.h * a.d_v * 4));
@@ -151,13 +161,13 @@ int run_decode_attn(AttnArgs a, void* ws, cudaStream_t st) {
   } else {
     QCAU_CHECK_CUDA(launch_attn_general(a, st));
   }
-  if (a.splits > 1) QCAU_CHECK_CUDA(launch_attn_combine(a, st));
+  if (a.splits > 1 || sm100) QCAU_CHECK_CUDA(launch_attn_combine(a, st));
   return QCAU_OK;
 }
 
 size_t decode_ws_bytes(int64_t b, int64_t h, int64_t d_v, int64_t max_len) {
   const size_t w1 = attn_ws_bytes(b, h, d_v, general_splits(b, h, max_len));
-  const size_t w2 = attn_ws_bytes(b, h, d_v, sm100_splits(b, h, max_len));
+  const size_t w2 = attn_ws_bytes(b, h, d_v, sm100_splits(b, h, max_len), true);
   return w1 > w2 ? w1 : w2;
 }
 

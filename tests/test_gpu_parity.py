@@ -284,3 +284,46 @@ def test_mla_decode_layer_vs_oracle():
                         seqlens.cpu().numpy(), positions.cpu().numpy(), freqs.cpu().numpy())
     assert_close_attn(f32(n_bf16(y)), f32(O.f32_to_bf16(ref)), "mla decode layer")
     _no_device_error()
+
+
+# ------------------------------------------------------------------ tcgen05 two-CTA decode kernel
+
+@pytest.mark.parametrize("h,seqlens", [(128, [4096, 64, 777, 1]), (128, [0, 130, 2000]),
+                                       (256, [513, 128, 3000])])
+def test_decode_paged_two_cta_vs_oracle(h, seqlens):
+    """h % 128 == 0 with 576/512 widths and 64-token pages runs the tcgen05 pair kernel."""
+    gen = torch.Generator(device="cuda").manual_seed(7 + h + len(seqlens))
+    B, page, width = len(seqlens), 64, 576
+    max_pages = (max(seqlens) + page - 1) // page
+    pages = B * max_pages + 5
+    cache = torch.randn(pages, page, width, device="cuda", generator=gen)
+    cache = (cache * torch.rsqrt(cache.square().mean(-1, keepdim=True))).to(torch.bfloat16)
+    table = torch.randperm(pages, device="cuda", generator=gen)[:B * max_pages]
+    table = table.view(B, max_pages).to(torch.int32).contiguous()
+    sl = torch.tensor(seqlens, device="cuda", dtype=torch.int32)
+    q = torch.randn(B, h, width, device="cuda", generator=gen).to(torch.bfloat16)
+    scale = 192 ** -0.5
+    o = _decode_abi(q, cache, table, sl, None, scale, 512, max(seqlens))
+    assert _lib.device_error() == 0
+    ref = O.paged_decode_attn(n_bf16(q), n_bf16(cache), table.cpu().numpy(), sl.cpu().numpy(),
+                              None, scale, 512)
+    assert_close_attn(f32(n_bf16(o)), f32(O.f32_to_bf16(ref)), f"two-cta h{h} {seqlens}")
+
+
+def test_mla_decode_layer_128_heads_vs_oracle():
+    cfg = MLAConfig(n_heads=128)
+    layer = MLADecodeLayer(cfg, "cuda")
+    weights = layer.random_weights(seed=3)
+    B, ctx = 2, 640
+    cache, table, _ = make_paged_cache(B, ctx, 64, 576, "cuda", seed=4)
+    seqlens = torch.tensor([640, 300], device="cuda", dtype=torch.int32)
+    positions = seqlens.clone()
+    freqs = precompute_freqs_cis(64, 1024, cfg.rope_theta, "cuda")
+    gen = torch.Generator(device="cuda").manual_seed(6)
+    q_lora = torch.randn(B, cfg.dc, device="cuda", generator=gen)
+    q_lora = (q_lora * torch.rsqrt(q_lora.square().mean(-1, keepdim=True))).to(torch.bfloat16)
+    y = layer.forward(q_lora, cache, table, seqlens, positions, freqs, ctx)
+    assert _lib.device_error() == 0
+    ref = _oracle_layer(layer, weights, q_lora, cache, table.cpu().numpy(),
+                        seqlens.cpu().numpy(), positions.cpu().numpy(), freqs.cpu().numpy())
+    assert_close_attn(f32(n_bf16(y)), f32(O.f32_to_bf16(ref)), "mla decode layer, 128 heads")
