@@ -168,6 +168,32 @@ def run_reference_arm(args, rank):
     print(json.dumps(line))
 
 
+def attn_only(batch: int, ctx: int, local: int):
+    """A small decode-attention case for ncu: 128 heads, `ctx` tokens per
+    sequence, the same paged layout; 2 warm-up launches then 3 launches."""
+    from qcau_b200 import _lib
+    from qcau_b200.mla import make_paged_cache
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cache, table, seqlens = make_paged_cache(batch, ctx, PAGE, WIDTH, dev, seed=0)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    q = torch.randn(batch, HEADS, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
+    o = torch.empty(batch, HEADS, 512, device=dev, dtype=torch.bfloat16)
+    L = _lib.lib()
+    need = L.qcau_decode_attn_workspace_size(batch, HEADS, 512, ctx)
+    wsb = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+    for _ in range(5):
+        _lib.check(L.qcau_decode_attn_paged(q.data_ptr(), cache.data_ptr(), table.data_ptr(),
+                                            seqlens.data_ptr(), None, o.data_ptr(), batch, HEADS,
+                                            WIDTH, 512, WIDTH, PAGE, table.size(1), cache.size(0),
+                                            ctx, 192 ** -0.5, wsb.data_ptr(), need,
+                                            _lib.stream_ptr(dev)), "attn")
+    torch.cuda.synchronize(dev)
+    assert _lib.device_error() == 0
+    print(json.dumps({"attn_only": True, "batch": batch, "ctx": ctx}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -175,8 +201,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--attn-only", action="store_true",
+                    help="profiling case: only the decode attention, --batch x --ctx, 5 launches")
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--ctx", type=int, default=4096)
     args = ap.parse_args()
     ws, rank, local = dist_env()
+    if args.attn_only:
+        attn_only(args.batch, args.ctx, local)
+        return
     if args.impl == "reference":
         run_reference_arm(args, rank)
         return
