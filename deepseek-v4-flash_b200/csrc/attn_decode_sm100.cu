@@ -20,12 +20,13 @@
 //        K = 128 tokens; A = bf16 P in shared memory, B = V rows given
 //        MN-major (CTA r supplies dims [256j + 128r, +128))
 //        -> O in TMEM: lanes 0-63 dims [256j, +128), lanes 64-127 the next 128
-// Shared memory: Q (64 heads x 576, 72 KB), P (2 x 16 KB), and a ring of
-// 14 x 8 KB TMA slots filled in the order the MMAs consume them:
-// K(0), K(1), V(0), K(2), V(1), ..., V(T-1); a K slot is one page x 64 dims,
-// a V slot is 32 tokens x 128 dims.
-// Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer (pair leader only),
-// 2-5 softmax / O correction / epilogue (one TMEM lane each).
+// Shared memory: Q (64 heads x 576, 72 KB), P (16 KB), a K ring of 9 x 8 KB
+// slots (one tile: one page x 64 dims per slot) and a V ring of 8 x 8 KB slots
+// (one tile: 32 tokens x 128 dims per slot).  The two rings have their own
+// producer warps, so V(t) streams in while QK(t+1) runs instead of queueing
+// behind K(t+1).
+// Warps: 0 K producer, 1 TMEM allocator + MMA issuer (pair leader only),
+// 2-5 softmax / O correction / epilogue (one TMEM lane each), 6 V producer.
 // Every wait is bounded; a timeout raises QCAU_DEVERR_TIMEOUT, drains the
 // copies in flight, frees TMEM and returns.
 #include "common.cuh"
@@ -34,8 +35,9 @@
 namespace qcau {
 namespace {
 
-constexpr int kThreads = 192;
-constexpr int kRing = 14;
+constexpr int kThreads = 224;
+constexpr int kKSlots = 9;           // one tile of K: 9 chunks of 64 dims
+constexpr int kVSlots = 8;           // one tile of V: 2 MMAs x 4 quarters of 32 tokens
 constexpr int kSlot = 8192;
 constexpr int kQBytes = 9 * kSlot;   // 64 heads x 576 bf16
 constexpr int kPBytes = 2 * kSlot;   // 64 heads x 128 tokens bf16
@@ -48,13 +50,15 @@ constexpr uint32_t kTmemS = 256;     // 2 buffers x 64 columns
 constexpr uint32_t kTmemCols = 512;
 
 struct DecodeShared {
-  uint64_t full[kRing];   // leader: slot landed in both CTAs
-  uint64_t empty[kRing];  // both: slot consumed by the MMAs
+  uint64_t kfull[kKSlots];   // leader: K slot landed in both CTAs
+  uint64_t kempty[kKSlots];  // both: K slot consumed by QK
+  uint64_t vfull[kVSlots];   // leader: V slot landed in both CTAs
+  uint64_t vempty[kVSlots];  // both: V slot consumed by PV
   uint64_t q_full;        // leader: Q landed in both CTAs
   uint64_t s_full[2];     // both: S(t) ready
   uint64_t s_free[2];     // leader: 8 softmax warps have read S(t)
-  uint64_t p_full[2];     // leader: 8 softmax warps wrote P(t) / corrected O
-  uint64_t p_free[2];     // both: PV(t) done with P(t)
+  uint64_t p_full;        // leader: 8 softmax warps wrote P(t) / corrected O
+  uint64_t p_free;        // both: PV(t) done with P and O
   uint64_t o_full;        // both: last PV done
   uint64_t xbar[2];       // local: the 4 softmax warps exchanged tile maxima
   uint64_t lbar;          // local: denominator exchange
@@ -64,7 +68,7 @@ struct DecodeShared {
   int abort;
 };
 
-constexpr size_t kSmemBytes = 1024 + kQBytes + 2 * kPBytes + (size_t)kRing * kSlot +
+constexpr size_t kSmemBytes = 1024 + kQBytes + kPBytes + (size_t)(kKSlots + kVSlots) * kSlot +
                               sizeof(DecodeShared);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
@@ -102,8 +106,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* sQ = smem_raw + pad;
   uint8_t* sP = sQ + kQBytes;
-  uint8_t* sRing = sP + 2 * kPBytes;
-  DecodeShared* sh = reinterpret_cast<DecodeShared*>(sRing + (size_t)kRing * kSlot);
+  uint8_t* sK = sP + kPBytes;
+  uint8_t* sV = sK + (size_t)kKSlots * kSlot;
+  DecodeShared* sh = reinterpret_cast<DecodeShared*>(sV + (size_t)kVSlots * kSlot);
   volatile int* abort = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -131,18 +136,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kRing; i++) {
-      mbar_init(&sh->full[i], 1);
-      mbar_init(&sh->empty[i], 1);
+    for (int i = 0; i < kKSlots; i++) {
+      mbar_init(&sh->kfull[i], 1);
+      mbar_init(&sh->kempty[i], 1);
+    }
+    for (int i = 0; i < kVSlots; i++) {
+      mbar_init(&sh->vfull[i], 1);
+      mbar_init(&sh->vempty[i], 1);
     }
     mbar_init(&sh->q_full, 1);
     for (int i = 0; i < 2; i++) {
       mbar_init(&sh->s_full[i], 1);
       mbar_init(&sh->s_free[i], 8);
-      mbar_init(&sh->p_full[i], 8);
-      mbar_init(&sh->p_free[i], 1);
       mbar_init(&sh->xbar[i], 4);
     }
+    mbar_init(&sh->p_full, 8);
+    mbar_init(&sh->p_free, 1);
     mbar_init(&sh->o_full, 1);
     mbar_init(&sh->lbar, 4);
     sh->abort = 0;
@@ -165,58 +174,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     return (int)e;
   };
 
-  if (warp == 0) {
-    // ------------------------------------------------ TMA producer (both CTAs)
+  if (warp == 0 || warp == 6) {
+    // ------------------------------------------------ TMA producers (both CTAs)
+    // warp 0 streams Q then K(0), K(1), ...; warp 6 streams V(0), V(1), ...
     if (lane == 0) {
-      int last_use[kRing];
-      for (int i = 0; i < kRing; i++) last_use[i] = -1;
-      const uint32_t q_full_l = mapa_shared(smem_u32(&sh->q_full), 0);
-      if (leader) mbar_arrive_expect_tx(&sh->q_full, 2 * kQBytes);
-      for (int k = 0; k < 9; k++)
-        tma_load_3d_pair(sQ + k * kSlot, &tm_q, q_full_l, 64 * k, head0, (int)b);
-      int n = 0;
+      const bool is_k = warp == 0;
+      uint64_t* fullb = is_k ? sh->kfull : sh->vfull;
+      uint64_t* emptyb = is_k ? sh->kempty : sh->vempty;
+      const int nslots = is_k ? kKSlots : kVSlots;
+      int last_tile[kKSlots];  // per slot: last tile whose copy was issued
+      for (int i = 0; i < kKSlots; i++) last_tile[i] = -1;
+      if (is_k) {
+        if (leader) mbar_arrive_expect_tx(&sh->q_full, 2 * kQBytes);
+        const uint32_t q_full_l = mapa_shared(smem_u32(&sh->q_full), 0);
+        for (int k = 0; k < 9; k++)
+          tma_load_3d_pair(sQ + k * kSlot, &tm_q, q_full_l, 64 * k, head0, (int)b);
+      }
       bool ok = true;
-      auto acquire = [&](int& slot) -> bool {
-        slot = n % kRing;
-        const int u = n / kRing;
-        n++;
-        if (!mbar_wait<true>(&sh->empty[slot], (u & 1) ^ 1, abort)) return false;
-        if (leader) mbar_arrive_expect_tx(&sh->full[slot], 2 * kSlot);
-        last_use[slot] = u;
-        return true;
-      };
-      for (int it = 0; it <= T && ok; it++) {
-        if (it < T) {
-          const int page = page_of(2 * (t_begin + it) + (int)rank);
-          for (int k = 0; k < 9 && ok; k++) {
-            int slot;
-            if (!(ok = acquire(slot))) break;
-            tma_load_3d_pair(sRing + slot * kSlot, &tm_k,
-                             mapa_shared(smem_u32(&sh->full[slot]), 0), 64 * k, 0, page);
-          }
-        }
-        if (it >= 1 && ok) {
-          const int t = t_begin + it - 1;
-          for (int j = 0; j < 2 && ok; j++) {
-            const int q0 = 4 * j + 2 * (int)rank;
-            for (int s = 0; s < 4 && ok; s++) {
-              const int page = page_of(2 * t + (s >> 1));
-              int slot;
-              if (!(ok = acquire(slot))) break;
-              const uint32_t fb = mapa_shared(smem_u32(&sh->full[slot]), 0);
-              tma_load_3d_pair(sRing + slot * kSlot, &tm_v, fb, 64 * q0, 32 * (s & 1), page);
-              tma_load_3d_pair(sRing + slot * kSlot + 4096, &tm_v, fb, 64 * (q0 + 1),
-                               32 * (s & 1), page);
-            }
+      for (int it = 0; it < T && ok; it++) {
+        const int t = t_begin + it;
+        for (int slot = 0; slot < nslots && ok; slot++) {
+          if (!(ok = mbar_wait<true>(&emptyb[slot], (it & 1) ^ 1, abort))) break;
+          if (leader) mbar_arrive_expect_tx(&fullb[slot], 2 * kSlot);
+          last_tile[slot] = it;
+          const uint32_t fb = mapa_shared(smem_u32(&fullb[slot]), 0);
+          if (is_k) {
+            tma_load_3d_pair(sK + slot * kSlot, &tm_k, fb, 64 * slot, 0,
+                             page_of(2 * t + (int)rank));
+          } else {
+            const int j = slot >> 2, q = slot & 3;  // PV MMA j, 32-token quarter q
+            const int q0 = 4 * j + 2 * (int)rank;   // this CTA's two 64-dim chunks
+            const int page = page_of(2 * t + (q >> 1));
+            tma_load_3d_pair(sV + slot * kSlot, &tm_v, fb, 64 * q0, 32 * (q & 1), page);
+            tma_load_3d_pair(sV + slot * kSlot + 4096, &tm_v, fb, 64 * (q0 + 1), 32 * (q & 1),
+                             page);
           }
         }
       }
       if (*abort && leader) {
         // the leader's full barriers count both CTAs' copies: drain them all
         volatile int never = 0;
-        mbar_wait<true>(&sh->q_full, 0, &never);
-        for (int i = 0; i < kRing; i++)
-          if (last_use[i] >= 0) mbar_wait<true>(&sh->full[i], last_use[i] & 1, &never);
+        if (is_k) mbar_wait<true>(&sh->q_full, 0, &never);
+        for (int slot = 0; slot < nslots; slot++)
+          if (last_tile[slot] >= 0) mbar_wait<true>(&fullb[slot], last_tile[slot] & 1, &never);
       }
     }
   } else if (warp == 1) {
@@ -224,56 +224,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (leader && lane == 0) {
       const uint32_t idesc_qk = make_idesc(128, 128, kFmtBF16, kFmtBF16, false, false);
       const uint32_t idesc_pv = make_idesc(128, 256, kFmtBF16, kFmtBF16, false, true);
-      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP), r_addr = smem_u32(sRing);
-      int n = 0, last_slot = -1, last_u = 0;
-      auto take = [&](int& slot) -> bool {
-        slot = n % kRing;
-        const int u = n / kRing;
-        n++;
-        if (!mbar_wait<true>(&sh->full[slot], u & 1, abort)) return false;
-        tc_fence_after();
-        last_slot = slot;
-        last_u = u;
-        return true;
-      };
+      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      uint64_t* last_bar = nullptr;  // barrier of the last commit, for the drain
+      int last_phase = 0;
       auto qk = [&](int it) -> bool {
         const int sb = it & 1;
         if (it >= 2 && !mbar_wait<true>(&sh->s_free[sb], ((it >> 1) - 1) & 1, abort)) return false;
         tc_fence_after();
-        for (int k = 0; k < 9; k++) {
-          int slot;
-          if (!take(slot)) return false;
+        for (int k = 0; k < kKSlots; k++) {
+          if (!mbar_wait<true>(&sh->kfull[k], it & 1, abort)) return false;
+          tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 4; kk++)
             mma_bf16_pair(tmem + kTmemS + sb * 64, make_sdesc(q_addr + k * kSlot + kk * 32, 16, 1024),
-                          make_sdesc(r_addr + slot * kSlot + kk * 32, 16, 1024), idesc_qk,
+                          make_sdesc(k_addr + k * kSlot + kk * 32, 16, 1024), idesc_qk,
                           (k | kk) != 0 ? 1u : 0u);
-          tc_commit_pair(&sh->empty[slot], 3);
+          tc_commit_pair(&sh->kempty[k], 3);
+          last_bar = &sh->kempty[k];
+          last_phase = it & 1;
         }
         tc_commit_pair(&sh->s_full[sb], 3);
         return true;
       };
       auto pv = [&](int it) -> bool {
-        const int pb = it & 1;
-        if (!mbar_wait<true>(&sh->p_full[pb], (it >> 1) & 1, abort)) return false;
+        if (!mbar_wait<true>(&sh->p_full, it & 1, abort)) return false;
         tc_fence_after();
-        for (int j = 0; j < 2; j++) {
-          for (int s = 0; s < 4; s++) {
-            int slot;
-            if (!take(slot)) return false;
+        for (int slot = 0; slot < kVSlots; slot++) {
+          const int j = slot >> 2, q = slot & 3;
+          if (!mbar_wait<true>(&sh->vfull[slot], it & 1, abort)) return false;
+          tc_fence_after();
 #pragma unroll
-            for (int kk = 0; kk < 2; kk++) {
-              const int ks = 2 * s + kk;  // 16-token step within the tile
-              const uint64_t ad =
-                  make_sdesc(p_addr + pb * kPBytes + (ks >> 2) * kSlot + (ks & 3) * 32, 16, 1024);
-              const uint64_t bd = make_sdesc(r_addr + slot * kSlot + kk * 2048, 4096, 1024);
-              mma_bf16_pair(tmem + kTmemO + j * 128, ad, bd, idesc_pv,
-                            (it > 0 || s > 0 || kk > 0) ? 1u : 0u);
-            }
-            tc_commit_pair(&sh->empty[slot], 3);
+          for (int kk = 0; kk < 2; kk++) {
+            const int ks = 2 * q + kk;  // 16-token step within the tile
+            const uint64_t ad = make_sdesc(p_addr + (ks >> 2) * kSlot + (ks & 3) * 32, 16, 1024);
+            const uint64_t bd = make_sdesc(v_addr + slot * kSlot + kk * 2048, 4096, 1024);
+            mma_bf16_pair(tmem + kTmemO + j * 128, ad, bd, idesc_pv,
+                          (it > 0 || q > 0 || kk > 0) ? 1u : 0u);
           }
+          tc_commit_pair(&sh->vempty[slot], 3);
+          last_bar = &sh->vempty[slot];
+          last_phase = it & 1;
         }
-        tc_commit_pair(&sh->p_free[pb], 3);
+        tc_commit_pair(&sh->p_free, 3);
         return true;
       };
       bool ok = mbar_wait<true>(&sh->q_full, 0, abort);
@@ -285,10 +278,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       if (ok) ok = pv(T - 1);
       if (ok) tc_commit_pair(&sh->o_full, 3);
-      if (*abort && last_slot >= 0) {
+      if (*abort && last_bar != nullptr) {
         // the MMAs issued so far finish before TMEM and the slots go away
         volatile int never = 0;
-        mbar_wait<true>(&sh->empty[last_slot], last_u & 1, &never);
+        mbar_wait<true>(last_bar, last_phase, &never);
       }
     }
   } else {
@@ -300,8 +293,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const float sl2 = p.scale * kLog2e;
     const uint32_t s_free_l[2] = {mapa_shared(smem_u32(&sh->s_free[0]), 0),
                                   mapa_shared(smem_u32(&sh->s_free[1]), 0)};
-    const uint32_t p_full_l[2] = {mapa_shared(smem_u32(&sh->p_full[0]), 0),
-                                  mapa_shared(smem_u32(&sh->p_full[1]), 0)};
+    const uint32_t p_full_l = mapa_shared(smem_u32(&sh->p_full), 0);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int it = 0; it < T && ok; it++) {
@@ -356,11 +348,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       l_run = l_run * alpha + ps;
 
-      // P(t) reuses the buffer of P(t-2): PV(t-2) must be done with it
-      if (it >= 2 && !(ok = warp_wait(&sh->p_free[sb], ((it >> 1) - 1) & 1, abort))) break;
+      // P(t) reuses the buffer of P(t-1), and O holds tiles < t, once PV(t-1) is done
+      if (it >= 1 && !(ok = warp_wait(&sh->p_free, (it - 1) & 1, abort))) break;
       if (__any_sync(0xffffffffu, resc)) {
-        // O holds tiles < t once PV(t-1) is done; rescale this warp's rows
-        if (it >= 1 && !(ok = warp_wait(&sh->p_free[sb ^ 1], ((it - 1) >> 1) & 1, abort))) break;
+        // rescale this warp's rows of O
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 8; c++) {
@@ -374,7 +365,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         tmem_st_wait();
       }
-      uint8_t* prow = sP + sb * kPBytes + half * kSlot + hl * 128;
+      uint8_t* prow = sP + half * kSlot + hl * 128;
 #pragma unroll
       for (int c = 0; c < 8; c++)
         *reinterpret_cast<uint4*>(prow + ((c ^ (hl & 7)) << 4)) =
@@ -382,7 +373,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_remote(p_full_l[sb]);
+      if (lane == 0) mbar_arrive_remote(p_full_l);
     }
     if (ok) ok = warp_wait(&sh->o_full, 0, abort);
     sh->xsum[row] = l_run;
