@@ -16,7 +16,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/qcau_b200.h"
+#include "qcau_b200.h"
 
 namespace qcau {
 
