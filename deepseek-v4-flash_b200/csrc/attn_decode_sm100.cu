@@ -11,20 +11,23 @@
 // same quotient and P stays <= 2^8 (bf16 rounding is scale-free).
 //
 // Work unit = one CTA pair (cluster of 2) x one sequence x one KV split x 128
-// heads.  CTA r of the pair owns heads [64r, 64r+64) of the group:
-//   QK : tcgen05.mma.cta_group::2, M = 128 heads, N = 128 tokens (CTA r
-//        supplies page 2t+r of the 128-token tile), K = 576 in 9 chunks
-//        -> S in TMEM, 2x2 lane layout: lanes 0-63 tokens 0-63, lanes 64-127
-//        tokens 64-127 of the CTA's 64 heads (64 columns, double-buffered)
+// heads; tiles of 256 tokens (4 pages).  CTA r of the pair owns heads
+// [64r, 64r+64) of the group:
+//   QK : tcgen05.mma.cta_group::2, M = 128 heads, N = 256 tokens (CTA r
+//        supplies pages 4t+2r and 4t+2r+1), K = 576 in 9 chunks of 64
+//        -> S in TMEM, 2x2 lane layout: lanes 0-63 tokens 0-127, lanes
+//        64-127 tokens 128-255 of the CTA's 64 heads (128 columns, two buffers)
 //   PV : cta_group::2, M = 128 heads, N = 256 dims (two MMAs cover 512),
-//        K = 128 tokens; A = bf16 P in shared memory, B = V rows given
+//        K = 256 tokens; A = bf16 P in shared memory, B = V rows given
 //        MN-major (CTA r supplies dims [256j + 128r, +128))
 //        -> O in TMEM: lanes 0-63 dims [256j, +128), lanes 64-127 the next 128
-// Shared memory: Q (64 heads x 576, 72 KB), P (16 KB), a K ring of 9 x 8 KB
-// slots (one tile: one page x 64 dims per slot) and a V ring of 8 x 8 KB slots
-// (one tile: 32 tokens x 128 dims per slot).  The two rings have their own
-// producer warps, so V(t) streams in while QK(t+1) runs instead of queueing
-// behind K(t+1).
+// N = 256 keeps the pair MMAs at full rate (N = 128 runs at two thirds), and
+// the TMA barriers are waited with CTA scope and no tcgen05 fence per chunk
+// (a cluster-scope wait plus fence per chunk halves the MMA rate).
+// Shared memory: Q (64 heads x 576, 72 KB), P (64 heads x 256 tokens, 32 KB),
+// a K ring of 4 x 16 KB slots (one 64-dim chunk of the CTA's two pages) and a
+// V ring of 6 x 8 KB slots (32 tokens x the CTA's 128 dims of one PV MMA),
+// each ring with its own producer warp.
 // Warps: 0 K producer, 1 TMEM allocator + MMA issuer (pair leader only),
 // 2-5 softmax / O correction / epilogue (one TMEM lane each), 6 V producer.
 // Every wait is bounded; a timeout raises QCAU_DEVERR_TIMEOUT, drains the
@@ -36,17 +39,20 @@ namespace qcau {
 namespace {
 
 constexpr int kThreads = 224;
-constexpr int kKSlots = 9;           // one tile of K: 9 chunks of 64 dims
-constexpr int kVSlots = 8;           // one tile of V: 2 MMAs x 4 quarters of 32 tokens
-constexpr int kSlot = 8192;
-constexpr int kQBytes = 9 * kSlot;   // 64 heads x 576 bf16
-constexpr int kPBytes = 2 * kSlot;   // 64 heads x 128 tokens bf16
-constexpr int kTile = 128;           // tokens per tile (two pages)
+constexpr int kTile = 256;            // tokens per tile (four pages)
+constexpr int kKSlot = 16384;         // 128 tokens x 64 dims
+constexpr int kKSlots = 4;
+constexpr int kKPerTile = 9;          // 576 / 64
+constexpr int kVSlot = 8192;          // 32 tokens x 128 dims
+constexpr int kVSlots = 6;
+constexpr int kVPerTile = 16;         // 2 PV MMAs x 8 quarters of 32 tokens
+constexpr int kQBytes = 9 * 8192;     // 64 heads x 576 bf16 (9 chunks of 64 rows)
+constexpr int kPBytes = 4 * 8192;     // 64 heads x 256 tokens bf16 (4 chunks of 64 tokens)
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kRescale = 8.0f;     // raise the running max only beyond 2^8
+constexpr float kRescale = 8.0f;      // raise the running max only beyond 2^8
 
-constexpr uint32_t kTmemO = 0;       // 2 accumulators x 128 columns
-constexpr uint32_t kTmemS = 256;     // 2 buffers x 64 columns
+constexpr uint32_t kTmemO = 0;        // 2 accumulators x 128 columns
+constexpr uint32_t kTmemS = 256;      // 2 buffers x 128 columns
 constexpr uint32_t kTmemCols = 512;
 
 struct DecodeShared {
@@ -54,22 +60,22 @@ struct DecodeShared {
   uint64_t kempty[kKSlots];  // both: K slot consumed by QK
   uint64_t vfull[kVSlots];   // leader: V slot landed in both CTAs
   uint64_t vempty[kVSlots];  // both: V slot consumed by PV
-  uint64_t q_full;        // leader: Q landed in both CTAs
-  uint64_t s_full[2];     // both: S(t) ready
-  uint64_t s_free[2];     // leader: 8 softmax warps have read S(t)
-  uint64_t p_full;        // leader: 8 softmax warps wrote P(t) / corrected O
-  uint64_t p_free;        // both: PV(t) done with P and O
-  uint64_t o_full;        // both: last PV done
-  uint64_t xbar[2];       // local: the 4 softmax warps exchanged tile maxima
-  uint64_t lbar;          // local: denominator exchange
+  uint64_t q_full;           // leader: Q landed in both CTAs
+  uint64_t s_full[2];        // both: S(t) ready
+  uint64_t s_free[2];        // leader: the 8 softmax warps have read S(t)
+  uint64_t p_full;           // leader: the 8 softmax warps wrote P(t) / corrected O
+  uint64_t p_free;           // both: PV(t) done with P and O
+  uint64_t o_full;           // both: last PV done
+  uint64_t xbar[2];          // local: the 4 softmax warps exchanged tile maxima
+  uint64_t lbar;             // local: denominator exchange
   float xmax[2][128];
   float xsum[128];
   uint32_t tmem_base;
   int abort;
 };
 
-constexpr size_t kSmemBytes = 1024 + kQBytes + kPBytes + (size_t)(kKSlots + kVSlots) * kSlot +
-                              sizeof(DecodeShared);
+constexpr size_t kSmemBytes = 1024 + kQBytes + kPBytes + (size_t)kKSlots * kKSlot +
+                              (size_t)kVSlots * kVSlot + sizeof(DecodeShared);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 struct DecodeParams {
@@ -107,8 +113,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint8_t* sQ = smem_raw + pad;
   uint8_t* sP = sQ + kQBytes;
   uint8_t* sK = sP + kPBytes;
-  uint8_t* sV = sK + (size_t)kKSlots * kSlot;
-  DecodeShared* sh = reinterpret_cast<DecodeShared*>(sV + (size_t)kVSlots * kSlot);
+  uint8_t* sV = sK + (size_t)kKSlots * kKSlot;
+  DecodeShared* sh = reinterpret_cast<DecodeShared*>(sV + (size_t)kVSlots * kVSlot);
   volatile int* abort = &sh->abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -176,38 +182,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   if (warp == 0 || warp == 6) {
     // ------------------------------------------------ TMA producers (both CTAs)
-    // warp 0 streams Q then K(0), K(1), ...; warp 6 streams V(0), V(1), ...
+    // warp 0: Q, then the K chunks of tiles 0, 1, ...; warp 6: the V quarters.
     if (lane == 0) {
       const bool is_k = warp == 0;
       uint64_t* fullb = is_k ? sh->kfull : sh->vfull;
       uint64_t* emptyb = is_k ? sh->kempty : sh->vempty;
       const int nslots = is_k ? kKSlots : kVSlots;
-      int last_tile[kKSlots];  // per slot: last tile whose copy was issued
-      for (int i = 0; i < kKSlots; i++) last_tile[i] = -1;
+      const int per_tile = is_k ? kKPerTile : kVPerTile;
+      int last_use[kVSlots];  // per slot: last ring pass whose copy was issued
+      for (int i = 0; i < kVSlots; i++) last_use[i] = -1;
       if (is_k) {
         if (leader) mbar_arrive_expect_tx(&sh->q_full, 2 * kQBytes);
         const uint32_t q_full_l = mapa_shared(smem_u32(&sh->q_full), 0);
         for (int k = 0; k < 9; k++)
-          tma_load_3d_pair(sQ + k * kSlot, &tm_q, q_full_l, 64 * k, head0, (int)b);
+          tma_load_3d_pair(sQ + k * 8192, &tm_q, q_full_l, 64 * k, head0, (int)b);
       }
+      int n = 0;
       bool ok = true;
       for (int it = 0; it < T && ok; it++) {
         const int t = t_begin + it;
-        for (int slot = 0; slot < nslots && ok; slot++) {
-          if (!(ok = mbar_wait<true>(&emptyb[slot], (it & 1) ^ 1, abort))) break;
-          if (leader) mbar_arrive_expect_tx(&fullb[slot], 2 * kSlot);
-          last_tile[slot] = it;
+        for (int i = 0; i < per_tile; i++, n++) {
+          const int slot = n % nslots, u = n / nslots;
+          if (!(ok = mbar_wait(&emptyb[slot], (u & 1) ^ 1, abort))) break;
+          if (leader) mbar_arrive_expect_tx(&fullb[slot], is_k ? 2 * kKSlot : 2 * kVSlot);
+          last_use[slot] = u;
           const uint32_t fb = mapa_shared(smem_u32(&fullb[slot]), 0);
           if (is_k) {
-            tma_load_3d_pair(sK + slot * kSlot, &tm_k, fb, 64 * slot, 0,
-                             page_of(2 * t + (int)rank));
+            // chunk i (dims 64i..64i+63) of this CTA's two pages
+            uint8_t* dst = sK + slot * kKSlot;
+            tma_load_3d_pair(dst, &tm_k, fb, 64 * i, 0, page_of(4 * t + 2 * (int)rank));
+            tma_load_3d_pair(dst + 8192, &tm_k, fb, 64 * i, 0, page_of(4 * t + 2 * (int)rank + 1));
           } else {
-            const int j = slot >> 2, q = slot & 3;  // PV MMA j, 32-token quarter q
+            // PV MMA j = i/8, tokens 32q..32q+31 of the tile with q = i%8
+            const int j = i >> 3, q = i & 7;
             const int q0 = 4 * j + 2 * (int)rank;   // this CTA's two 64-dim chunks
-            const int page = page_of(2 * t + (q >> 1));
-            tma_load_3d_pair(sV + slot * kSlot, &tm_v, fb, 64 * q0, 32 * (q & 1), page);
-            tma_load_3d_pair(sV + slot * kSlot + 4096, &tm_v, fb, 64 * (q0 + 1), 32 * (q & 1),
-                             page);
+            const int page = page_of(4 * t + (q >> 1));
+            uint8_t* dst = sV + slot * kVSlot;
+            tma_load_3d_pair(dst, &tm_v, fb, 64 * q0, 32 * (q & 1), page);
+            tma_load_3d_pair(dst + 4096, &tm_v, fb, 64 * (q0 + 1), 32 * (q & 1), page);
           }
         }
       }
@@ -216,33 +228,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         volatile int never = 0;
         if (is_k) mbar_wait<true>(&sh->q_full, 0, &never);
         for (int slot = 0; slot < nslots; slot++)
-          if (last_tile[slot] >= 0) mbar_wait<true>(&fullb[slot], last_tile[slot] & 1, &never);
+          if (last_use[slot] >= 0) mbar_wait<true>(&fullb[slot], last_use[slot] & 1, &never);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer (pair leader)
     if (leader && lane == 0) {
-      const uint32_t idesc_qk = make_idesc(128, 128, kFmtBF16, kFmtBF16, false, false);
+      const uint32_t idesc_qk = make_idesc(128, 256, kFmtBF16, kFmtBF16, false, false);
       const uint32_t idesc_pv = make_idesc(128, 256, kFmtBF16, kFmtBF16, false, true);
       const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       uint64_t* last_bar = nullptr;  // barrier of the last commit, for the drain
       int last_phase = 0;
+      int nk = 0, nv = 0;
       auto qk = [&](int it) -> bool {
         const int sb = it & 1;
         if (it >= 2 && !mbar_wait<true>(&sh->s_free[sb], ((it >> 1) - 1) & 1, abort)) return false;
         tc_fence_after();
-        for (int k = 0; k < kKSlots; k++) {
-          if (!mbar_wait<true>(&sh->kfull[k], it & 1, abort)) return false;
-          tc_fence_after();
+        for (int k = 0; k < kKPerTile; k++, nk++) {
+          const int slot = nk % kKSlots, u = nk / kKSlots;
+          if (!mbar_wait(&sh->kfull[slot], u & 1, abort)) return false;
 #pragma unroll
           for (int kk = 0; kk < 4; kk++)
-            mma_bf16_pair(tmem + kTmemS + sb * 64, make_sdesc(q_addr + k * kSlot + kk * 32, 16, 1024),
-                          make_sdesc(k_addr + k * kSlot + kk * 32, 16, 1024), idesc_qk,
+            mma_bf16_pair(tmem + kTmemS + sb * 128,
+                          make_sdesc(q_addr + k * 8192 + kk * 32, 16, 1024),
+                          make_sdesc(k_addr + slot * kKSlot + kk * 32, 16, 1024), idesc_qk,
                           (k | kk) != 0 ? 1u : 0u);
-          tc_commit_pair(&sh->kempty[k], 3);
-          last_bar = &sh->kempty[k];
-          last_phase = it & 1;
+          tc_commit_pair(&sh->kempty[slot], 3);
+          last_bar = &sh->kempty[slot];
+          last_phase = u & 1;
         }
         tc_commit_pair(&sh->s_full[sb], 3);
         return true;
@@ -250,26 +264,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       auto pv = [&](int it) -> bool {
         if (!mbar_wait<true>(&sh->p_full, it & 1, abort)) return false;
         tc_fence_after();
-        for (int slot = 0; slot < kVSlots; slot++) {
-          const int j = slot >> 2, q = slot & 3;
-          if (!mbar_wait<true>(&sh->vfull[slot], it & 1, abort)) return false;
-          tc_fence_after();
+        for (int i = 0; i < kVPerTile; i++, nv++) {
+          const int j = i >> 3, q = i & 7;
+          const int slot = nv % kVSlots, u = nv / kVSlots;
+          if (!mbar_wait(&sh->vfull[slot], u & 1, abort)) return false;
 #pragma unroll
           for (int kk = 0; kk < 2; kk++) {
             const int ks = 2 * q + kk;  // 16-token step within the tile
-            const uint64_t ad = make_sdesc(p_addr + (ks >> 2) * kSlot + (ks & 3) * 32, 16, 1024);
-            const uint64_t bd = make_sdesc(v_addr + slot * kSlot + kk * 2048, 4096, 1024);
+            const uint64_t ad = make_sdesc(p_addr + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024);
+            const uint64_t bd = make_sdesc(v_addr + slot * kVSlot + kk * 2048, 4096, 1024);
             mma_bf16_pair(tmem + kTmemO + j * 128, ad, bd, idesc_pv,
                           (it > 0 || q > 0 || kk > 0) ? 1u : 0u);
           }
           tc_commit_pair(&sh->vempty[slot], 3);
           last_bar = &sh->vempty[slot];
-          last_phase = it & 1;
+          last_phase = u & 1;
         }
         tc_commit_pair(&sh->p_free, 3);
         return true;
       };
-      bool ok = mbar_wait<true>(&sh->q_full, 0, abort);
+      bool ok = mbar_wait(&sh->q_full, 0, abort);
       tc_fence_after();
       if (ok) ok = qk(0);
       for (int it = 1; it < T && ok; it++) {
@@ -298,31 +312,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int it = 0; it < T && ok; it++) {
       const int sb = it & 1;
+      const uint32_t s_addr = tmem + lane_base + kTmemS + sb * 128;
+      const int tok0 = (t_begin + it) * kTile + half * 128;
+      const int nvalid = seqlen - tok0;  // tokens of this half that exist (may be <= 0 or > 128)
       if (!(ok = warp_wait(&sh->s_full[sb], (it >> 1) & 1, abort))) break;
       tc_fence_after();
-      float s[64];
-      {
-        float v0[32], v1[32];
-        tmem_ld32(tmem + lane_base + kTmemS + sb * 64, v0);
-        tmem_ld32(tmem + lane_base + kTmemS + sb * 64 + 32, v1);
+      // pass 1: tile max of this thread's 128 scores
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; c++) {
+        float v[32];
+        tmem_ld32(s_addr + c * 32, v);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-          s[i] = v0[i];
-          s[32 + i] = v1[i];
-        }
+        for (int i = 0; i < 32; i++)
+          if (c * 32 + i < nvalid) mx = fmaxf(mx, v[i]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_remote(s_free_l[sb]);
-
-      const int tok0 = (t_begin + it) * kTile + half * 64;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < 64; i++) {
-        s[i] = (tok0 + i < seqlen) ? s[i] * sl2 : -INFINITY;
-        mx = fmaxf(mx, s[i]);
-      }
+      mx = (mx == -INFINITY) ? -INFINITY : mx * sl2;
       sh->xmax[sb][row] = mx;
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh->xbar[sb]);
@@ -337,21 +343,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         m_run = tmax;
         resc = true;
       }
-      uint32_t pk[32];
-      float ps = 0.f;
-#pragma unroll
-      for (int i = 0; i < 32; i++) {
-        const float p0 = exp2f(s[2 * i] - m_run);
-        const float p1 = exp2f(s[2 * i + 1] - m_run);
-        ps += p0 + p1;
-        pk[i] = pack_bf16(p0, p1);
-      }
-      l_run = l_run * alpha + ps;
-
       // P(t) reuses the buffer of P(t-1), and O holds tiles < t, once PV(t-1) is done
       if (it >= 1 && !(ok = warp_wait(&sh->p_free, (it - 1) & 1, abort))) break;
+      // pass 2: P = exp2(s*scale - m) as bf16 into the swizzled P tile
+      float ps = 0.f;
+      uint8_t* pbase = sP + half * 2 * 8192 + hl * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; c++) {
+        float v[32];
+        tmem_ld32(s_addr + c * 32, v);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const int e = c * 32 + 2 * i;
+          const float p0 = (e < nvalid) ? exp2f(fmaf(v[2 * i], sl2, -m_run)) : 0.f;
+          const float p1 = (e + 1 < nvalid) ? exp2f(fmaf(v[2 * i + 1], sl2, -m_run)) : 0.f;
+          ps += p0 + p1;
+          pk[i] = pack_bf16(p0, p1);
+        }
+        // 32 tokens = 64 bytes = four 16-byte units of the 128-byte row of chunk c/2
+        uint8_t* prow = pbase + (c >> 1) * 8192;
+        const int u0 = (c & 1) * 4;
+#pragma unroll
+        for (int w = 0; w < 4; w++)
+          *reinterpret_cast<uint4*>(prow + (((u0 + w) ^ (hl & 7)) << 4)) =
+              make_uint4(pk[4 * w], pk[4 * w + 1], pk[4 * w + 2], pk[4 * w + 3]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(s_free_l[sb]);
+      l_run = l_run * alpha + ps;
       if (__any_sync(0xffffffffu, resc)) {
-        // rescale this warp's rows of O
+        // rescale this warp's rows of O (PV(t-1) is complete)
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 8; c++) {
@@ -365,11 +389,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         tmem_st_wait();
       }
-      uint8_t* prow = sP + half * kSlot + hl * 128;
-#pragma unroll
-      for (int c = 0; c < 8; c++)
-        *reinterpret_cast<uint4*>(prow + ((c ^ (hl & 7)) << 4)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
