@@ -50,6 +50,8 @@ constexpr int kQBytes = 9 * 8192;     // 64 heads x 576 bf16 (9 chunks of 64 row
 constexpr int kPBytes = 4 * 8192;     // 64 heads x 256 tokens bf16 (4 chunks of 64 tokens)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescale = 8.0f;      // raise the running max only beyond 2^8
+constexpr int kPrefetchTiles = 2;     // pages are prefetched into L2 this many tiles ahead
+constexpr uint32_t kPageBytes = 64 * 576 * 2;
 
 constexpr uint32_t kTmemO = 0;        // 2 accumulators x 128 columns
 constexpr uint32_t kTmemS = 256;      // 2 buffers x 128 columns
@@ -79,6 +81,7 @@ constexpr size_t kSmemBytes = 1024 + kQBytes + kPBytes + (size_t)kKSlots * kKSlo
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 struct DecodeParams {
+  const void* cache;  // [num_pages, 64, 576] bf16, for the L2 prefetch of whole pages
   const int32_t* table;
   const int32_t* seqlens;
   float* part_o;
@@ -197,10 +200,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int k = 0; k < 9; k++)
           tma_load_3d_pair(sQ + k * 8192, &tm_q, q_full_l, 64 * k, head0, (int)b);
       }
+      // L2 prefetch of this CTA's two pages of a tile (whole contiguous pages):
+      // the ring is too shallow to cover HBM latency, L2 hits are 2-3x closer
+      auto prefetch_tile = [&](int it) {
+        if (it >= T) return;
+        const int t = t_begin + it;
+        for (int pg = 0; pg < 2; pg++)
+          prefetch_l2_bulk(reinterpret_cast<const uint8_t*>(p.cache) +
+                               (size_t)page_of(4 * t + 2 * (int)rank + pg) * kPageBytes,
+                           kPageBytes);
+      };
+      if (is_k)
+        for (int it = 0; it < kPrefetchTiles && it < T; it++) prefetch_tile(it);
       int n = 0;
       bool ok = true;
       for (int it = 0; it < T && ok; it++) {
         const int t = t_begin + it;
+        if (is_k) prefetch_tile(it + kPrefetchTiles);
         for (int i = 0; i < per_tile; i++, n++) {
           const int slot = n % nslots, u = n / nslots;
           if (!(ok = mbar_wait(&emptyb[slot], (u & 1) ^ 1, abort))) break;
@@ -473,6 +489,7 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
       return cudaErrorInvalidValue;
   }
   DecodeParams p;
+  p.cache = a.kv;
   p.table = a.block_table;
   p.seqlens = a.seqlens;
   p.part_o = a.part_o;

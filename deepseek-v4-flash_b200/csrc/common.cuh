@@ -161,6 +161,11 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, uint64_t
       : "memory");
 }
 
+// Prefetch `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* gaddr, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gaddr), "r"(bytes) : "memory");
+}
+
 // Two-CTA form: the data lands in this CTA's shared memory, the transaction
 // count is signalled on the barrier at `bar_cluster_addr` (the pair leader's
 // barrier).  No multicast.
