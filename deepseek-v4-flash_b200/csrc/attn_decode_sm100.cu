@@ -21,15 +21,21 @@
 //        K = 256 tokens; A = bf16 P in shared memory, B = V rows given
 //        MN-major (CTA r supplies dims [256j + 128r, +128))
 //        -> O in TMEM: lanes 0-63 dims [256j, +128), lanes 64-127 the next 128
-// N = 256 keeps the pair MMAs at full rate (N = 128 runs at two thirds), and
-// the TMA barriers are waited with CTA scope and no tcgen05 fence per chunk
-// (a cluster-scope wait plus fence per chunk halves the MMA rate).
+// Issue-rate notes (measured on B200): pair MMAs with N = 128 run at two
+// thirds of the rate of N = 256; a blocking mbarrier wait in the issuing
+// thread costs hundreds of cycles even when the phase is complete, and the
+// tensor queue is shallow, so QK and PV are issued by two different threads
+// (one stream's waits are covered by the other's queued MMAs), every wait
+// guards at least 4 MMAs, and TMA barriers are waited with CTA scope and no
+// tcgen05 fence per chunk.
 // Shared memory: Q (64 heads x 576, 72 KB), P (64 heads x 256 tokens, 32 KB),
 // a K ring of 4 x 16 KB slots (one 64-dim chunk of the CTA's two pages) and a
-// V ring of 6 x 8 KB slots (32 tokens x the CTA's 128 dims of one PV MMA),
-// each ring with its own producer warp.
-// Warps: 0 K producer, 1 TMEM allocator + MMA issuer (pair leader only),
-// 2-5 softmax / O correction / epilogue (one TMEM lane each), 6 V producer.
+// V ring of 3 x 16 KB slots (one page x the CTA's 128 dims of one PV MMA),
+// each ring with its own producer warp.  Pages are prefetched into L2 two
+// tiles ahead.
+// Warps: 0 K producer, 1 TMEM allocator + QK issuer (pair leader), 2-5
+// softmax / O correction / epilogue (one TMEM lane each), 6 V producer,
+// 7 PV issuer (pair leader).
 // Every wait is bounded; a timeout raises QCAU_DEVERR_TIMEOUT, drains the
 // copies in flight, frees TMEM and returns.
 #include "common.cuh"
@@ -38,14 +44,14 @@
 namespace qcau {
 namespace {
 
-constexpr int kThreads = 224;
+constexpr int kThreads = 256;
 constexpr int kTile = 256;            // tokens per tile (four pages)
 constexpr int kKSlot = 16384;         // 128 tokens x 64 dims
 constexpr int kKSlots = 4;
 constexpr int kKPerTile = 9;          // 576 / 64
-constexpr int kVSlot = 8192;          // 32 tokens x 128 dims
-constexpr int kVSlots = 6;
-constexpr int kVPerTile = 16;         // 2 PV MMAs x 8 quarters of 32 tokens
+constexpr int kVSlot = 16384;         // 64 tokens x 128 dims
+constexpr int kVSlots = 3;
+constexpr int kVPerTile = 8;          // 2 PV MMAs x 4 pages
 constexpr int kQBytes = 9 * 8192;     // 64 heads x 576 bf16 (9 chunks of 64 rows)
 constexpr int kPBytes = 4 * 8192;     // 64 heads x 256 tokens bf16 (4 chunks of 64 tokens)
 constexpr float kLog2e = 1.4426950408889634f;
@@ -109,8 +115,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     decode_attn_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
-                             const __grid_constant__ CUtensorMap tm_k,
-                             const __grid_constant__ CUtensorMap tm_v, DecodeParams p) {
+                             const __grid_constant__ CUtensorMap tm_k, DecodeParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* sQ = smem_raw + pad;
@@ -192,8 +197,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint64_t* emptyb = is_k ? sh->kempty : sh->vempty;
       const int nslots = is_k ? kKSlots : kVSlots;
       const int per_tile = is_k ? kKPerTile : kVPerTile;
-      int last_use[kVSlots];  // per slot: last ring pass whose copy was issued
-      for (int i = 0; i < kVSlots; i++) last_use[i] = -1;
+      int last_use[kKSlots];  // per slot: last ring pass whose copy was issued
+      for (int i = 0; i < kKSlots; i++) last_use[i] = -1;
       if (is_k) {
         if (leader) mbar_arrive_expect_tx(&sh->q_full, 2 * kQBytes);
         const uint32_t q_full_l = mapa_shared(smem_u32(&sh->q_full), 0);
@@ -229,13 +234,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tma_load_3d_pair(dst, &tm_k, fb, 64 * i, 0, page_of(4 * t + 2 * (int)rank));
             tma_load_3d_pair(dst + 8192, &tm_k, fb, 64 * i, 0, page_of(4 * t + 2 * (int)rank + 1));
           } else {
-            // PV MMA j = i/8, tokens 32q..32q+31 of the tile with q = i%8
-            const int j = i >> 3, q = i & 7;
+            // PV MMA j = i/4 over page i%4 of the tile
+            const int j = i >> 2, pg = i & 3;
             const int q0 = 4 * j + 2 * (int)rank;   // this CTA's two 64-dim chunks
-            const int page = page_of(4 * t + (q >> 1));
+            const int page = page_of(4 * t + pg);
             uint8_t* dst = sV + slot * kVSlot;
-            tma_load_3d_pair(dst, &tm_v, fb, 64 * q0, 32 * (q & 1), page);
-            tma_load_3d_pair(dst + 4096, &tm_v, fb, 64 * (q0 + 1), 32 * (q & 1), page);
+            tma_load_3d_pair(dst, &tm_k, fb, 64 * q0, 0, page);
+            tma_load_3d_pair(dst + 8192, &tm_k, fb, 64 * (q0 + 1), 0, page);
           }
         }
       }
@@ -247,67 +252,65 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (last_use[slot] >= 0) mbar_wait<true>(&fullb[slot], last_use[slot] & 1, &never);
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer (pair leader)
+  } else if (warp == 1 || warp == 7) {
+    // ------------------------------------------------ MMA issuers (pair leader)
+    // warp 1 issues QK(0), QK(1), ...; warp 7 issues PV(0), PV(1), ...
     if (leader && lane == 0) {
-      const uint32_t idesc_qk = make_idesc(128, 256, kFmtBF16, kFmtBF16, false, false);
-      const uint32_t idesc_pv = make_idesc(128, 256, kFmtBF16, kFmtBF16, false, true);
       const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       uint64_t* last_bar = nullptr;  // barrier of the last commit, for the drain
       int last_phase = 0;
-      int nk = 0, nv = 0;
-      auto qk = [&](int it) -> bool {
-        const int sb = it & 1;
-        if (it >= 2 && !mbar_wait<true>(&sh->s_free[sb], ((it >> 1) - 1) & 1, abort)) return false;
-        tc_fence_after();
-        for (int k = 0; k < kKPerTile; k++, nk++) {
-          const int slot = nk % kKSlots, u = nk / kKSlots;
-          if (!mbar_wait(&sh->kfull[slot], u & 1, abort)) return false;
+      bool ok = true;
+      if (warp == 1) {
+        const uint32_t idesc_qk = make_idesc(128, 256, kFmtBF16, kFmtBF16, false, false);
+        int nk = 0;
+        ok = mbar_wait(&sh->q_full, 0, abort);
+        for (int it = 0; it < T && ok; it++) {
+          const int sb = it & 1;
+          if (it >= 2 && !(ok = mbar_wait<true>(&sh->s_free[sb], ((it >> 1) - 1) & 1, abort)))
+            break;
+          tc_fence_after();
+          for (int k = 0; k < kKPerTile; k++, nk++) {
+            const int slot = nk % kKSlots, u = nk / kKSlots;
+            if (!(ok = mbar_wait(&sh->kfull[slot], u & 1, abort))) break;
 #pragma unroll
-          for (int kk = 0; kk < 4; kk++)
-            mma_bf16_pair(tmem + kTmemS + sb * 128,
-                          make_sdesc(q_addr + k * 8192 + kk * 32, 16, 1024),
-                          make_sdesc(k_addr + slot * kKSlot + kk * 32, 16, 1024), idesc_qk,
-                          (k | kk) != 0 ? 1u : 0u);
-          tc_commit_pair(&sh->kempty[slot], 3);
-          last_bar = &sh->kempty[slot];
-          last_phase = u & 1;
-        }
-        tc_commit_pair(&sh->s_full[sb], 3);
-        return true;
-      };
-      auto pv = [&](int it) -> bool {
-        if (!mbar_wait<true>(&sh->p_full, it & 1, abort)) return false;
-        tc_fence_after();
-        for (int i = 0; i < kVPerTile; i++, nv++) {
-          const int j = i >> 3, q = i & 7;
-          const int slot = nv % kVSlots, u = nv / kVSlots;
-          if (!mbar_wait(&sh->vfull[slot], u & 1, abort)) return false;
-#pragma unroll
-          for (int kk = 0; kk < 2; kk++) {
-            const int ks = 2 * q + kk;  // 16-token step within the tile
-            const uint64_t ad = make_sdesc(p_addr + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024);
-            const uint64_t bd = make_sdesc(v_addr + slot * kVSlot + kk * 2048, 4096, 1024);
-            mma_bf16_pair(tmem + kTmemO + j * 128, ad, bd, idesc_pv,
-                          (it > 0 || q > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < 4; kk++)
+              mma_bf16_pair(tmem + kTmemS + sb * 128,
+                            make_sdesc(q_addr + k * 8192 + kk * 32, 16, 1024),
+                            make_sdesc(k_addr + slot * kKSlot + kk * 32, 16, 1024), idesc_qk,
+                            (k | kk) != 0 ? 1u : 0u);
+            tc_commit_pair(&sh->kempty[slot], 3);
+            last_bar = &sh->kempty[slot];
+            last_phase = u & 1;
           }
-          tc_commit_pair(&sh->vempty[slot], 3);
-          last_bar = &sh->vempty[slot];
-          last_phase = u & 1;
+          if (ok) tc_commit_pair(&sh->s_full[sb], 3);
         }
-        tc_commit_pair(&sh->p_free, 3);
-        return true;
-      };
-      bool ok = mbar_wait(&sh->q_full, 0, abort);
-      tc_fence_after();
-      if (ok) ok = qk(0);
-      for (int it = 1; it < T && ok; it++) {
-        ok = qk(it);
-        if (ok) ok = pv(it - 1);
+      } else {
+        const uint32_t idesc_pv = make_idesc(128, 256, kFmtBF16, kFmtBF16, false, true);
+        int nv = 0;
+        for (int it = 0; it < T && ok; it++) {
+          if (!(ok = mbar_wait<true>(&sh->p_full, it & 1, abort))) break;
+          tc_fence_after();
+          for (int i = 0; i < kVPerTile; i++, nv++) {
+            const int j = i >> 2, pg = i & 3;
+            const int slot = nv % kVSlots, u = nv / kVSlots;
+            if (!(ok = mbar_wait(&sh->vfull[slot], u & 1, abort))) break;
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+              // 16 tokens of page pg: P chunk pg, V slot rows 16kk..16kk+15
+              const uint64_t ad = make_sdesc(p_addr + pg * 8192 + kk * 32, 16, 1024);
+              const uint64_t bd = make_sdesc(v_addr + slot * kVSlot + kk * 2048, 8192, 1024);
+              mma_bf16_pair(tmem + kTmemO + j * 128, ad, bd, idesc_pv,
+                            (it > 0 || pg > 0 || kk > 0) ? 1u : 0u);
+            }
+            tc_commit_pair(&sh->vempty[slot], 3);
+            last_bar = &sh->vempty[slot];
+            last_phase = u & 1;
+          }
+          if (ok) tc_commit_pair(&sh->p_free, 3);
+        }
+        if (ok) tc_commit_pair(&sh->o_full, 3);
       }
-      if (ok) ok = pv(T - 1);
-      if (ok) tc_commit_pair(&sh->o_full, 3);
       if (*abort && last_bar != nullptr) {
         // the MMAs issued so far finish before TMEM and the slots go away
         volatile int never = 0;
@@ -468,7 +471,7 @@ bool decode_attn_sm100_supported(const AttnArgs& a) {
 cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   if (!decode_attn_sm100_supported(a)) return cudaErrorNotSupported;
   if (a.b == 0) return cudaSuccess;
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk;
   {
     const uint64_t dims[3] = {576, (uint64_t)a.h, (uint64_t)a.b};
     const uint64_t strides[2] = {1152, (uint64_t)a.h * 1152};
@@ -480,11 +483,8 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   {
     const uint64_t dims[3] = {576, 64, (uint64_t)a.num_pages};
     const uint64_t strides[2] = {1152, 64 * 1152};
-    const uint32_t box_k[3] = {64, 64, 1};
-    const uint32_t box_v[3] = {64, 32, 1};
-    if (!make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.kv, dims, strides, box_k,
-                   CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.kv, dims, strides, box_v,
+    const uint32_t box[3] = {64, 64, 1};
+    if (!make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.kv, dims, strides, box,
                    CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
   }
@@ -506,7 +506,7 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
                                        (int)kSmemBytes);
   if (e != cudaSuccess) return e;
   const int64_t units = a.b * a.splits * p.hgroups;
-  decode_attn_sm100_kernel<<<(unsigned)(2 * units), kThreads, kSmemBytes, st>>>(tq, tk, tv, p);
+  decode_attn_sm100_kernel<<<(unsigned)(2 * units), kThreads, kSmemBytes, st>>>(tq, tk, p);
   return cudaGetLastError();
 }
 

@@ -82,13 +82,38 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t addr, uint32_t pa
   return ok != 0;
 }
 
+template <bool kCluster>
+__device__ __forceinline__ bool mbar_test_wait(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  if constexpr (kCluster) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+  }
+  return ok != 0;
+}
+
 // Bounded wait.  Returns false (and sets *abort) if the barrier phase did not
 // complete within kWaitLimitCycles, or returns false at once if another
-// thread already aborted.
+// thread already aborted.  A non-blocking test comes first: a try_wait on an
+// already completed phase still costs hundreds of cycles, which starves the
+// tensor pipe when the waiting thread is the one issuing MMAs.
 template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const uint32_t a = smem_u32(bar);
-  if (kCluster ? mbar_try_wait_cluster(a, parity) : mbar_try_wait(a, parity)) return true;
+  if (mbar_test_wait<kCluster>(a, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (kCluster ? mbar_try_wait_cluster(a, parity) : mbar_try_wait(a, parity)) return true;
