@@ -403,6 +403,76 @@ int qcau_decode_attn_paged(const void* q, const void* cache, const int32_t* bloc
   return run_decode_attn(a, workspace, to_stream(stream));
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------- no-alloc decode scratch
+
+// Split-KV partials of qcau_decode_attn_paged_noalloc.  Module-scope device
+// storage: each device that loads the library holds it until the process exits.
+static __device__ __align__(256) uint8_t g_decode_scratch[QCAU_DECODE_STATIC_SCRATCH_BYTES];
+
+// Address of g_decode_scratch on the current device, resolved once per device
+// with that device current.
+static int decode_scratch_address(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  QCAU_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64)
+    return fail(QCAU_ERR_UNSUPPORTED, "decode_attn_paged_noalloc: device ordinal above 63");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    QCAU_CHECK_CUDA(cudaGetSymbolAddress(&p, g_decode_scratch));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return QCAU_OK;
+}
+
+extern "C" {
+
+int qcau_decode_attn_paged_noalloc(const void* q, const void* cache, const int32_t* block_table,
+                                   const int32_t* seqlens, const float* attn_sink, void* o,
+                                   int64_t b, int64_t h, int64_t d_qk, int64_t d_v, int64_t d_kv,
+                                   int64_t page_size, int64_t max_pages, int64_t num_pages,
+                                   int64_t max_seqlen, float softmax_scale, void* stream) {
+  QCAU_CHECK_ARG(q && cache && block_table && seqlens && o,
+                 "decode_attn_paged_noalloc: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && h > 0 && page_size > 0 && max_pages > 0 && num_pages > 0,
+                 "decode_attn_paged_noalloc: bad shape");
+  QCAU_CHECK_ARG(max_seqlen >= 0 && max_seqlen <= max_pages * page_size,
+                 "decode_attn_paged_noalloc: max_seqlen exceeds the block table");
+  int rc = check_attn_widths(d_qk, d_v, d_kv, "decode_attn_paged_noalloc");
+  if (rc) return rc;
+  const size_t need = qcau_decode_attn_workspace_size(b, h, d_v, max_seqlen);
+  if (need > QCAU_DECODE_STATIC_SCRATCH_BYTES)
+    return fail(QCAU_ERR_WORKSPACE,
+                "decode_attn_paged_noalloc: split-KV partials need " + std::to_string(need) +
+                    " bytes, more than the " +
+                    std::to_string((size_t)QCAU_DECODE_STATIC_SCRATCH_BYTES) +
+                    "-byte static scratch; use qcau_decode_attn_paged with a workspace");
+  if (b == 0) return QCAU_OK;
+  void* scratch = nullptr;
+  rc = decode_scratch_address(&scratch);
+  if (rc) return rc;
+  AttnArgs a{};
+  a.q = q;
+  a.q_row_stride = d_qk;
+  a.kv = cache;
+  a.block_table = block_table;
+  a.seqlens = seqlens;
+  a.sink = attn_sink;
+  a.o = o;
+  a.b = b; a.s = 1; a.h = h; a.d_qk = d_qk; a.d_v = d_v; a.d_kv = d_kv;
+  a.page_size = page_size;
+  a.max_pages = max_pages;
+  a.num_pages = num_pages;
+  a.max_len = max_seqlen;
+  a.scale = softmax_scale;
+  return run_decode_attn(a, scratch, to_stream(stream));
+}
+
 int qcau_dequant_fp8_weight(const void* w, const void* w_scale, int32_t scale_dtype, void* out_bf16,
                             int64_t rows, int64_t cols, void* stream) {
   QCAU_CHECK_ARG(w && w_scale && out_bf16, "dequant_fp8_weight: NULL pointer");

@@ -20,6 +20,8 @@ QCAU_ERR_UNSUPPORTED = -3
 QCAU_ERR_WORKSPACE = -4
 QCAU_ERR_DEVICE = -5
 
+DECODE_STATIC_SCRATCH_BYTES = 32 << 20  # QCAU_DECODE_STATIC_SCRATCH_BYTES
+
 SCALE_F32 = 0
 SCALE_E8M0 = 1
 OUT_BF16 = 0
@@ -65,6 +67,8 @@ SIGNATURES = {
     "qcau_decode_attn_workspace_size": ([_I64, _I64, _I64, _I64], _SZ),
     "qcau_decode_attn_paged": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
                                 _I64, _I64, _I64, _F, _P, _SZ, _P], ctypes.c_int),
+    "qcau_decode_attn_paged_noalloc": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
+                                        _I64, _I64, _I64, _I64, _F, _P], ctypes.c_int),
     "qcau_dequant_fp8_weight": ([_P, _P, _I32, _P, _I64, _I64, _P], ctypes.c_int),
     "qcau_mla_decode_workspace_size": ([ctypes.POINTER(MlaDims)], _SZ),
     "qcau_mla_decode": ([ctypes.POINTER(MlaDims), _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,

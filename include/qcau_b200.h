@@ -181,6 +181,35 @@ int qcau_decode_attn_paged(const void* q, const void* cache,
                            size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * decode_attn_paged_noalloc -- qcau_decode_attn_paged for callers that
+ * cannot allocate device memory.  No counterpart in the reference: its
+ * kernels allocate through PyTorch; this entry point exists only for the
+ * no-cudaMalloc case.
+ *   Same arguments, kernels, split counts and results as
+ *   qcau_decode_attn_paged, but the split-KV partials live in a file-scope
+ *   static device array of QCAU_DECODE_STATIC_SCRATCH_BYTES (32 MiB), which
+ *   every device that loads this library holds until the process exits.
+ *   Allocates nothing: no cudaMalloc/cudaFree and no allocating library call.
+ *   Inputs whose partials need more than that (qcau_decode_attn_workspace_size
+ *   > QCAU_DECODE_STATIC_SCRATCH_BYTES, e.g. batch 128 x 128 heads at 32K
+ *   context) are rejected with QCAU_ERR_WORKSPACE before any device work.
+ *   The scratch address is resolved once per device (cudaGetSymbolAddress
+ *   with that device current); make the first call on each device outside
+ *   any stream capture.  Nothing in the scratch must start at zero: every
+ *   partial row the combine reads is written earlier in the same call.
+ *   There is ONE scratch per device: calls whose executions overlap on the
+ *   same device (two streams, or two host threads) race on it and give
+ *   wrong results.  Calls ordered on one stream are safe.
+ * ---------------------------------------------------------------------- */
+#define QCAU_DECODE_STATIC_SCRATCH_BYTES ((size_t)32 << 20)
+int qcau_decode_attn_paged_noalloc(const void* q, const void* cache,
+                                   const int32_t* block_table, const int32_t* seqlens,
+                                   const float* attn_sink, void* o, int64_t b, int64_t h,
+                                   int64_t d_qk, int64_t d_v, int64_t d_kv,
+                                   int64_t page_size, int64_t max_pages, int64_t num_pages,
+                                   int64_t max_seqlen, float softmax_scale, void* stream);
+
+/* ------------------------------------------------------------------------
  * Absorbed-MLA decode layer (BASELINE decode configs; the reference's V4
  * attention has no wkv_b, so these extend its surface).  Weights:
  *   wq_b   [h*(d_nope+d_rope), dc] e4m3 + scale [.. /128, dc/128]
