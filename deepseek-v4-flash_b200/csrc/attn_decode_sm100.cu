@@ -31,8 +31,9 @@
 // Shared memory: Q (64 heads x 576, 72 KB), P (64 heads x 256 tokens, 32 KB),
 // a K ring of 4 x 16 KB slots (one 64-dim chunk of the CTA's two pages) and a
 // V ring of 3 x 16 KB slots (one page x the CTA's 128 dims of one PV MMA),
-// each ring with its own producer warp.  Pages are prefetched into L2 two
-// tiles ahead.
+// each ring with its own producer warp.  A bulk L2 prefetch of whole pages
+// ahead of the K reads was measured to add DRAM reads (the prefetched lines
+// were not the ones the TMA reads hit) and to cost ~20% of the time: none.
 // Warps: 0 K producer, 1 TMEM allocator + QK issuer (pair leader), 2-5
 // softmax / O correction / epilogue (one TMEM lane each), 6 V producer,
 // 7 PV issuer (pair leader).
@@ -56,8 +57,6 @@ constexpr int kQBytes = 9 * 8192;     // 64 heads x 576 bf16 (9 chunks of 64 row
 constexpr int kPBytes = 4 * 8192;     // 64 heads x 256 tokens bf16 (4 chunks of 64 tokens)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescale = 8.0f;      // raise the running max only beyond 2^8
-constexpr int kPrefetchTiles = 2;     // pages are prefetched into L2 this many tiles ahead
-constexpr uint32_t kPageBytes = 64 * 576 * 2;
 
 constexpr uint32_t kTmemO = 0;        // 2 accumulators x 128 columns
 constexpr uint32_t kTmemS = 256;      // 2 buffers x 128 columns
@@ -87,7 +86,6 @@ constexpr size_t kSmemBytes = 1024 + kQBytes + kPBytes + (size_t)kKSlots * kKSlo
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 struct DecodeParams {
-  const void* cache;  // [num_pages, 64, 576] bf16, for the L2 prefetch of whole pages
   const int32_t* table;
   const int32_t* seqlens;
   float* part_o;
@@ -205,23 +203,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int k = 0; k < 9; k++)
           tma_load_3d_pair(sQ + k * 8192, &tm_q, q_full_l, 64 * k, head0, (int)b);
       }
-      // L2 prefetch of this CTA's two pages of a tile (whole contiguous pages):
-      // the ring is too shallow to cover HBM latency, L2 hits are 2-3x closer
-      auto prefetch_tile = [&](int it) {
-        if (it >= T) return;
-        const int t = t_begin + it;
-        for (int pg = 0; pg < 2; pg++)
-          prefetch_l2_bulk(reinterpret_cast<const uint8_t*>(p.cache) +
-                               (size_t)page_of(4 * t + 2 * (int)rank + pg) * kPageBytes,
-                           kPageBytes);
-      };
-      if (is_k)
-        for (int it = 0; it < kPrefetchTiles && it < T; it++) prefetch_tile(it);
       int n = 0;
       bool ok = true;
       for (int it = 0; it < T && ok; it++) {
         const int t = t_begin + it;
-        if (is_k) prefetch_tile(it + kPrefetchTiles);
         for (int i = 0; i < per_tile; i++, n++) {
           const int slot = n % nslots, u = n / nslots;
           if (!(ok = mbar_wait(&emptyb[slot], (u & 1) ^ 1, abort))) break;
@@ -336,16 +321,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int nvalid = seqlen - tok0;  // tokens of this half that exist (may be <= 0 or > 128)
       if (!(ok = warp_wait(&sh->s_full[sb], (it >> 1) & 1, abort))) break;
       tc_fence_after();
-      // pass 1: tile max of this thread's 128 scores
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; c++) {
-        float v[32];
-        tmem_ld32(s_addr + c * 32, v);
-        tmem_ld_wait();
+      // this thread's 128 scores into registers; the S buffer is then free
+      float v[128];
 #pragma unroll
-        for (int i = 0; i < 32; i++)
-          if (c * 32 + i < nvalid) mx = fmaxf(mx, v[i]);
+      for (int c = 0; c < 4; c++)
+        tmem_ld32(s_addr + c * 32, *reinterpret_cast<float(*)[32]>(v + 32 * c));
+#pragma unroll
+      for (int c = 0; c < 4; c++) tmem_ld_wait_regs(v + 32 * c);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(s_free_l[sb]);
+      const bool full = nvalid >= 128;
+      // pass 1: tile max
+      float mx = -INFINITY;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < 128; i++) mx = fmaxf(mx, v[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; i++)
+          if (i < nvalid) mx = fmaxf(mx, v[i]);
       }
       mx = (mx == -INFINITY) ? -INFINITY : mx * sl2;
       sh->xmax[sb][row] = mx;
@@ -364,21 +359,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       // P(t) reuses the buffer of P(t-1), and O holds tiles < t, once PV(t-1) is done
       if (it >= 1 && !(ok = warp_wait(&sh->p_free, (it - 1) & 1, abort))) break;
-      // pass 2: P = exp2(s*scale - m) as bf16 into the swizzled P tile
-      float ps = 0.f;
+      // pass 2: P = 2^(s*scale*log2e - m) as bf16 into the swizzled P tile; the
+      // row sum is over the unrounded values
+      const uint64_t sc2 = f2_pack(sl2, sl2), nm2 = f2_pack(-m_run, -m_run);
+      uint64_t sum2 = f2_pack(0.f, 0.f);
       uint8_t* pbase = sP + half * 2 * 8192 + hl * 128;
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < 4; c++) {
-        float v[32];
-        tmem_ld32(s_addr + c * 32, v);
-        tmem_ld_wait();
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; i++) {
           const int e = c * 32 + 2 * i;
-          const float p0 = (e < nvalid) ? exp2f(fmaf(v[2 * i], sl2, -m_run)) : 0.f;
-          const float p1 = (e + 1 < nvalid) ? exp2f(fmaf(v[2 * i + 1], sl2, -m_run)) : 0.f;
-          ps += p0 + p1;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(v[e], v[e + 1]), sc2, nm2), x0, x1);
+          float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+          if (!full) {
+            p0 = (e < nvalid) ? p0 : 0.f;
+            p1 = (e + 1 < nvalid) ? p1 : 0.f;
+          }
+          sum2 = f2_add(sum2, f2_pack(p0, p1));
           pk[i] = pack_bf16(p0, p1);
         }
         // 32 tokens = 64 bytes = four 16-byte units of the 128-byte row of chunk c/2
@@ -389,9 +388,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint4*>(prow + (((u0 + w) ^ (hl & 7)) << 4)) =
               make_uint4(pk[4 * w], pk[4 * w + 1], pk[4 * w + 2], pk[4 * w + 3]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_remote(s_free_l[sb]);
+      float ps0, ps1;
+      f2_unpack(sum2, ps0, ps1);
+      const float ps = ps0 + ps1;
       l_run = l_run * alpha + ps;
       if (__any_sync(0xffffffffu, resc)) {
         // rescale this warp's rows of O (PV(t-1) is complete)
@@ -489,7 +488,6 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
       return cudaErrorInvalidValue;
   }
   DecodeParams p;
-  p.cache = a.kv;
   p.table = a.block_table;
   p.seqlens = a.seqlens;
   p.part_o = a.part_o;

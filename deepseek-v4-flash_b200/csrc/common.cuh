@@ -186,11 +186,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, uint64_t
       : "memory");
 }
 
-// Prefetch `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2.
-__device__ __forceinline__ void prefetch_l2_bulk(const void* gaddr, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gaddr), "r"(bytes) : "memory");
-}
-
 // Two-CTA form: the data lands in this CTA's shared memory, the transaction
 // count is signalled on the barrier at `bar_cluster_addr` (the pair leader's
 // barrier).  No multicast.
@@ -354,6 +349,46 @@ __device__ __forceinline__ void tmem_ld_wait() {
 }
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// tcgen05.wait::ld that also names the 32 registers of one tmem_ld32 as
+// in/out operands, so that no use of them is scheduled before the wait.
+#define QCAU_R4(a, i) "+f"(a[i]), "+f"(a[i + 1]), "+f"(a[i + 2]), "+f"(a[i + 3])
+__device__ __forceinline__ void tmem_ld_wait_regs(float* v) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : QCAU_R4(v, 0), QCAU_R4(v, 4), QCAU_R4(v, 8), QCAU_R4(v, 12), QCAU_R4(v, 16),
+                 QCAU_R4(v, 20), QCAU_R4(v, 24), QCAU_R4(v, 28)
+               :
+               : "memory");
+}
+#undef QCAU_R4
+
+// 2^x by the MUFU instruction (ex2.approx, relative error ~2^-22, flushes
+// subnormal results to zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Packed fp32 pair arithmetic (sm_100 f32x2 instructions).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
 
 // ------------------------------------------------------------ numbers
