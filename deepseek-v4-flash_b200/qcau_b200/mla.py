@@ -64,6 +64,30 @@ def quantize_weight_fp8(w: torch.Tensor, e8m0: bool = False):
     return q, (s.to(torch.float8_e8m0fnu) if e8m0 else s.contiguous())
 
 
+def shard_weights(cfg: MLAConfig, rank: int, world_size: int, wq_b, wq_b_scale, wkv_b,
+                  wkv_b_scale, wo, wo_scale):
+    """This rank's slice of the full FP8 weights and their 128x128 block scales.
+
+    Heads are split evenly: rows of wq_b [H*(d_nope+d_rope), dc] and of wkv_b
+    [H*(d_nope+d_v), kv_lora] (column-parallel, ColumnParallelLinear
+    model.py:155-163), columns of wo [dim, H*d_v] (row-parallel,
+    RowParallelLinear model.py:166-180, whose partial outputs are summed).
+    """
+    if cfg.n_heads % world_size:
+        raise ValueError("n_heads must be divisible by the number of ranks")
+    hl = cfg.n_heads // world_size
+    dq, dkv = cfg.d_nope + cfg.d_rope, cfg.d_nope + cfg.d_v
+    if (hl * dq) % 128 or (hl * dkv) % 128 or (hl * cfg.d_v) % 128:
+        raise ValueError("a head shard must cover whole 128-row/column scale blocks")
+    r = rank
+    return (wq_b[r * hl * dq:(r + 1) * hl * dq],
+            wq_b_scale[r * hl * dq // 128:(r + 1) * hl * dq // 128],
+            wkv_b[r * hl * dkv:(r + 1) * hl * dkv],
+            wkv_b_scale[r * hl * dkv // 128:(r + 1) * hl * dkv // 128],
+            wo[:, r * hl * cfg.d_v:(r + 1) * hl * cfg.d_v],
+            wo_scale[:, r * hl * cfg.d_v // 128:(r + 1) * hl * cfg.d_v // 128])
+
+
 def precompute_freqs_cis(rope_dim: int, npos: int, theta: float, device) -> torch.Tensor:
     """RoPE table [npos, rope_dim/2, 2] fp32 (re, im), model.py:198-228 without YaRN."""
     freqs = 1.0 / (theta ** (torch.arange(0, rope_dim, 2, dtype=torch.float32) / rope_dim))
@@ -98,15 +122,10 @@ class MLADecodeLayer:
         wq_b [H*(d_nope+d_rope), dc], wkv_b [H*(d_nope+d_v), kv_lora],
         wo [dim, H*d_v].  Scales are fp32 or float8_e8m0fnu.
         """
-        c, r, hl = self.cfg, self.rank, self.n_local
-        dq, dkv = c.d_nope + c.d_rope, c.d_nope + c.d_v
         if not sharded and self.world_size > 1:
-            wq_b = wq_b[r * hl * dq:(r + 1) * hl * dq]
-            wq_b_scale = wq_b_scale[r * hl * dq // 128:(r + 1) * hl * dq // 128]
-            wkv_b = wkv_b[r * hl * dkv:(r + 1) * hl * dkv]
-            wkv_b_scale = wkv_b_scale[r * hl * dkv // 128:(r + 1) * hl * dkv // 128]
-            wo = wo[:, r * hl * c.d_v:(r + 1) * hl * c.d_v]
-            wo_scale = wo_scale[:, r * hl * c.d_v // 128:(r + 1) * hl * c.d_v // 128]
+            wq_b, wq_b_scale, wkv_b, wkv_b_scale, wo, wo_scale = shard_weights(
+                self.cfg, self.rank, self.world_size, wq_b, wq_b_scale, wkv_b, wkv_b_scale, wo,
+                wo_scale)
         dev = self.device
         self.wq_b = wq_b.to(dev).contiguous()
         self.wq_b_scale = wq_b_scale.to(dev).contiguous()
