@@ -112,25 +112,34 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+SAMPLE_HEADS = 8  # heads of one decode token each CPU thread runs per step
+
+
 def cpu_reference(steps: int, warmup: int, threads: int):
-    """The reference's qcau_c C++ (oracle/_ref) on this host: one decode token of
-    the same workload per thread per step.  Returns (tok/s, sample text)."""
+    """The reference's qcau_c C++ (oracle/_ref) on this host.  One step = every
+    thread runs a head-shard sample of one decode token of the same workload:
+    SAMPLE_HEADS of the 128 heads (q-up rows, attention heads and o-proj input
+    columns of that shard), i.e. SAMPLE_HEADS/128 of the token's work, so a
+    step takes seconds instead of half a minute.  Returns (tok/s, sample)."""
     sys.path.insert(0, str(REPO / "oracle"))
     import oracle as O  # CPU checker / baseline only
 
     if not O.ref_available():
         return None, "oracle/_ref/qcau_ref not built"
-    args = (threads, threads, HEADS, WIDTH, CTX, DC, HEADS * 192, DIM)
+    hs = SAMPLE_HEADS
+    args = (threads, threads, hs, WIDTH, CTX, DC, hs * 192, DIM)
     for _ in range(warmup):
         O.ref_bench_decode(*args)
     secs = 0.0
     for _ in range(steps):
         secs += O.ref_bench_decode(*args)["seconds"]
-    sample = (f"{threads} tokens per step (one per thread), each: qcau_c quant_gemm q-up "
-              f"[1,{DC}]x[{HEADS * 192},{DC}], sparse_attention over {CTX} rows x {HEADS} "
-              f"heads x {WIDTH} (the C++ port has one width for K and V), quant_gemm o-proj "
-              f"[1,{HEADS * 128}]x[{DIM},{HEADS * 128}]; {steps} steps")
-    return threads * steps / secs, sample
+    frac = hs / HEADS
+    sample = (f"per step each of {threads} threads runs {hs} of the {HEADS} heads of one decode "
+              f"token ({frac:g} of its work): qcau_c quant_gemm q-up [1,{DC}]x[{hs * 192},{DC}], "
+              f"sparse_attention over {CTX} rows x {hs} heads x {WIDTH} (the C++ port has one "
+              f"width for K and V), quant_gemm o-proj [1,{hs * 128}]x[{DIM},{hs * 128}]; "
+              f"{steps} steps; tok/s = threads x {frac:g} / step time")
+    return threads * frac * steps / secs, sample
 
 
 def traffic_from_profiles():
@@ -156,7 +165,8 @@ def run_reference_arm(args, rank):
         return
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * threads / v,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * threads * SAMPLE_HEADS / HEADS / v,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "config": {"workload": "absorbed-MLA decode layer, batch 128, 128 heads, ctx 32768",
@@ -365,7 +375,7 @@ def main():
         }
         if ws == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
-            v, sample = cpu_reference(1, 0, threads)
+            v, sample = cpu_reference(3, 1, threads)
             line["cpu_baseline"] = ({"value": v, "unit": "tok/s", "cores": threads,
                                      "kind": "reference", "sample": sample}
                                     if v is not None else {"value": None, "unavailable": sample})

@@ -12,7 +12,10 @@
 //
 // Work unit = one CTA pair (cluster of 2) x one sequence x one KV split x 128
 // heads; tiles of 256 tokens (4 pages).  CTA r of the pair owns heads
-// [64r, 64r+64) of the group:
+// [64r, 64r+64) of the group.  With h = 64, 32 or 16 heads (a head shard of
+// 128) the pair owns all h heads, h/2 per CTA, and the remaining MMA rows of
+// each CTA are padding (Q rows of other heads, or zeros past h) whose outputs
+// are not written: the cache bytes, which bound the kernel, are the same.
 //   QK : tcgen05.mma.cta_group::2, M = 128 heads, N = 256 tokens (CTA r
 //        supplies pages 4t+2r and 4t+2r+1), K = 576 in 9 chunks of 64
 //        -> S in TMEM, 2x2 lane layout: lanes 0-63 tokens 0-127, lanes
@@ -29,8 +32,8 @@
 // guards at least 4 MMAs, and TMA barriers are waited with CTA scope and no
 // tcgen05 fence per chunk.
 // Shared memory: Q (64 heads x 576, 72 KB), P (64 heads x 256 tokens, 32 KB),
-// a K ring of 4 x 16 KB slots (one 64-dim chunk of the CTA's two pages) and a
-// V ring of 3 x 16 KB slots (one page x the CTA's 128 dims of one PV MMA),
+// a K ring of 3 x 16 KB slots (one 64-dim chunk of the CTA's two pages) and a
+// V ring of 4 x 16 KB slots (one page x the CTA's 128 dims of one PV MMA),
 // each ring with its own producer warp.  A bulk L2 prefetch of whole pages
 // ahead of the K reads was measured to add DRAM reads (the prefetched lines
 // were not the ones the TMA reads hit) and to cost ~20% of the time: none.
@@ -48,10 +51,10 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kTile = 256;            // tokens per tile (four pages)
 constexpr int kKSlot = 16384;         // 128 tokens x 64 dims
-constexpr int kKSlots = 4;
+constexpr int kKSlots = 3;
 constexpr int kKPerTile = 9;          // 576 / 64
 constexpr int kVSlot = 16384;         // 64 tokens x 128 dims
-constexpr int kVSlots = 3;
+constexpr int kVSlots = 4;
 constexpr int kVPerTile = 8;          // 2 PV MMAs x 4 pages
 constexpr int kQBytes = 9 * 8192;     // 64 heads x 576 bf16 (9 chunks of 64 rows)
 constexpr int kPBytes = 4 * 8192;     // 64 heads x 256 tokens bf16 (4 chunks of 64 tokens)
@@ -93,6 +96,7 @@ struct DecodeParams {
   int* err;
   int64_t max_pages, num_pages;
   int h, hgroups, splits;
+  int cta_heads;  // heads each CTA owns: 64, or h/2 when h < 128 (the other MMA rows are padding)
   float scale;
 };
 
@@ -136,10 +140,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int t_begin = (int)((int64_t)ntiles * split / p.splits);
   const int t_end = (int)((int64_t)ntiles * (split + 1) / p.splits);
   const int T = t_end - t_begin;
-  const int head0 = hg * 128 + (int)rank * 64;
+  const int head0 = hg * 2 * p.cta_heads + (int)rank * p.cta_heads;
 
   if (T <= 0) {  // both CTAs of the pair take this branch together
-    for (int i = threadIdx.x; i < 64; i += blockDim.x) {
+    for (int i = threadIdx.x; i < p.cta_heads; i += blockDim.x) {
       const int64_t prow = (b * p.splits + split) * p.h + head0 + i;
       p.part_ml[prow * 2] = -INFINITY;
       p.part_ml[prow * 2 + 1] = 0.f;
@@ -195,8 +199,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint64_t* emptyb = is_k ? sh->kempty : sh->vempty;
       const int nslots = is_k ? kKSlots : kVSlots;
       const int per_tile = is_k ? kKPerTile : kVPerTile;
-      int last_use[kKSlots];  // per slot: last ring pass whose copy was issued
-      for (int i = 0; i < kKSlots; i++) last_use[i] = -1;
+      constexpr int kMaxSlots = kKSlots > kVSlots ? kKSlots : kVSlots;
+      int last_use[kMaxSlots];  // per slot: last ring pass whose copy was issued
+      for (int i = 0; i < kMaxSlots; i++) last_use[i] = -1;
       if (is_k) {
         if (leader) mbar_arrive_expect_tx(&sh->q_full, 2 * kQBytes);
         const uint32_t q_full_l = mapa_shared(smem_u32(&sh->q_full), 0);
@@ -357,40 +362,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         m_run = tmax;
         resc = true;
       }
-      // P(t) reuses the buffer of P(t-1), and O holds tiles < t, once PV(t-1) is done
-      if (it >= 1 && !(ok = warp_wait(&sh->p_free, (it - 1) & 1, abort))) break;
-      // pass 2: P = 2^(s*scale*log2e - m) as bf16 into the swizzled P tile; the
+      // pass 2 into registers: P = 2^(s*scale*log2e - m) as bf16 pairs; the
       // row sum is over the unrounded values
       const uint64_t sc2 = f2_pack(sl2, sl2), nm2 = f2_pack(-m_run, -m_run);
       uint64_t sum2 = f2_pack(0.f, 0.f);
-      uint8_t* pbase = sP + half * 2 * 8192 + hl * 128;
+      uint32_t pk[64];
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const int e = c * 32 + 2 * i;
-          float x0, x1;
-          f2_unpack(f2_fma(f2_pack(v[e], v[e + 1]), sc2, nm2), x0, x1);
-          float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
-          if (!full) {
-            p0 = (e < nvalid) ? p0 : 0.f;
-            p1 = (e + 1 < nvalid) ? p1 : 0.f;
-          }
-          sum2 = f2_add(sum2, f2_pack(p0, p1));
-          pk[i] = pack_bf16(p0, p1);
+      for (int i = 0; i < 64; i++) {
+        const int e = 2 * i;
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(v[e], v[e + 1]), sc2, nm2), x0, x1);
+        float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+        if (!full) {
+          p0 = (e < nvalid) ? p0 : 0.f;
+          p1 = (e + 1 < nvalid) ? p1 : 0.f;
         }
-        // 32 tokens = 64 bytes = four 16-byte units of the 128-byte row of chunk c/2
-        uint8_t* prow = pbase + (c >> 1) * 8192;
-        const int u0 = (c & 1) * 4;
-#pragma unroll
-        for (int w = 0; w < 4; w++)
-          *reinterpret_cast<uint4*>(prow + (((u0 + w) ^ (hl & 7)) << 4)) =
-              make_uint4(pk[4 * w], pk[4 * w + 1], pk[4 * w + 2], pk[4 * w + 3]);
+        sum2 = f2_add(sum2, f2_pack(p0, p1));
+        pk[i] = pack_bf16(p0, p1);
       }
       float ps0, ps1;
       f2_unpack(sum2, ps0, ps1);
       const float ps = ps0 + ps1;
+      // P(t) reuses the buffer of P(t-1), and O holds tiles < t, once PV(t-1) is done
+      if (it >= 1 && !(ok = warp_wait(&sh->p_free, (it - 1) & 1, abort))) break;
+      // 128 tokens = 256 bytes = two 128-byte rows (chunks half*2, half*2+1) of
+      // sixteen-byte units, swizzled
+      uint8_t* pbase = sP + half * 2 * 8192 + hl * 128;
+#pragma unroll
+      for (int u = 0; u < 16; u++)
+        *reinterpret_cast<uint4*>(pbase + (u >> 3) * 8192 + (((u & 7) ^ (hl & 7)) << 4)) =
+            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
       l_run = l_run * alpha + ps;
       if (__any_sync(0xffffffffu, resc)) {
         // rescale this warp's rows of O (PV(t-1) is complete)
@@ -428,11 +429,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem + lane_base + kTmemO + c * 32, v);
         tmem_ld_wait();
         float4* dst = reinterpret_cast<float4*>(po + (c >> 2) * 256 + (c & 3) * 32);
+        if (hl < p.cta_heads) {
 #pragma unroll
-        for (int i = 0; i < 8; i++)
-          dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          for (int i = 0; i < 8; i++)
+            dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
       }
-      if (half == 0) {
+      if (half == 0 && hl < p.cta_heads) {
         p.part_ml[prow * 2] = m_run;
         p.part_ml[prow * 2 + 1] = l_tot;
       }
@@ -461,7 +464,8 @@ bool is_sm100_device() {
 
 bool decode_attn_sm100_supported(const AttnArgs& a) {
   return a.block_table != nullptr && a.seqlens != nullptr && a.s == 1 && a.d_qk == 576 &&
-         a.d_v == 512 && a.d_kv == 576 && a.page_size == 64 && a.h % 128 == 0 &&
+         a.d_v == 512 && a.d_kv == 576 && a.page_size == 64 &&
+         (a.h % 128 == 0 || a.h == 64 || a.h == 32 || a.h == 16) &&
          a.q_row_stride == 576 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 &&
          (reinterpret_cast<uintptr_t>(a.kv) & 15) == 0 && a.num_pages < (1LL << 31) &&
          a.max_pages < (1LL << 30) && is_sm100_device();
@@ -496,7 +500,8 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   p.max_pages = a.max_pages;
   p.num_pages = a.num_pages;
   p.h = (int)a.h;
-  p.hgroups = (int)(a.h / 128);
+  p.cta_heads = a.h >= 128 ? 64 : (int)(a.h / 2);
+  p.hgroups = (int)(a.h / (2 * p.cta_heads));
   p.splits = a.splits;
   p.scale = a.scale;
   cudaError_t e = cudaFuncSetAttribute(decode_attn_sm100_kernel,

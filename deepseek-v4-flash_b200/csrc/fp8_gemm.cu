@@ -21,7 +21,7 @@ namespace qcau {
 namespace {
 
 constexpr int BM = 128, BN = 128, BK = 128;
-constexpr int kStages = 4;
+constexpr int kStages = 6;
 constexpr int kTileBytes = BM * BK;  // fp8: 16 KB per operand tile
 constexpr int kStageBytes = 2 * kTileBytes;
 constexpr int kThreads = 192;
@@ -127,48 +127,67 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_local = quarter * 32 + lane;
     const int64_t row = m0 + row_local;
     const int64_t nblk = n0 / 128;
-    float acc[BN];
+    // the two scales of K-block kb, loaded kPre blocks ahead: a global load
+    // per block would otherwise stall every promotion
+    constexpr int kPre = 4;
+    auto scale_of = [&](int kb) -> float {
+      if (kb >= KB) return 0.f;
+      const float s_a = row < m ? load_scale(sa, row * KB + kb, a_e8m0) : 0.f;
+      return s_a * load_scale(sb, nblk * KB + kb, b_e8m0);
+    };
+    float sc0 = scale_of(0), sc1 = scale_of(1), sc2 = scale_of(2), sc3 = scale_of(3);
+    uint64_t acc[BN / 2];  // packed fp32 pairs
 #pragma unroll
-    for (int i = 0; i < BN; i++) acc[i] = 0.f;
+    for (int i = 0; i < BN / 2; i++) acc[i] = 0ull;
     bool ok = true;
     for (int kb = 0; kb < KB; kb++) {
       const int ab = kb & 1;
       const int ua = kb >> 1;
+      const float sc = sc0;
+      sc0 = sc1;
+      sc1 = sc2;
+      sc2 = sc3;
+      sc3 = scale_of(kb + kPre);
       if (!mbar_wait(&sh->tfull[ab], ua & 1, abort)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const float s_a = row < m ? load_scale(sa, row * KB + kb, a_e8m0) : 0.f;
-      const float sc = s_a * load_scale(sb, nblk * KB + kb, b_e8m0);
+      const uint64_t sc2x = f2_pack(sc, sc);
       const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + ab * BN;
 #pragma unroll
-      for (int c4 = 0; c4 < BN / 32; c4++) {
-        float v[32];
-        tmem_ld32(taddr + c4 * 32, v);
-        tmem_ld_wait();
+      for (int h = 0; h < 2; h++) {
+        float v[64];
+        tmem_ld32(taddr + h * 64, *reinterpret_cast<float(*)[32]>(v));
+        tmem_ld32(taddr + h * 64 + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+        tmem_ld_wait_regs(v);
+        tmem_ld_wait_regs(v + 32);
 #pragma unroll
-        for (int i = 0; i < 32; i++) acc[c4 * 32 + i] = fmaf(v[i], sc, acc[c4 * 32 + i]);
+        for (int i = 0; i < 32; i++)
+          acc[h * 32 + i] = f2_fma(f2_pack(v[2 * i], v[2 * i + 1]), sc2x, acc[h * 32 + i]);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh->tempty[ab]);
     }
     if (ok && row < m) {
+      float out[BN];
+#pragma unroll
+      for (int i = 0; i < BN / 2; i++) f2_unpack(acc[i], out[2 * i], out[2 * i + 1]);
       if (out_f32) {
         float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(c) + row * n + n0);
 #pragma unroll
         for (int j = 0; j < BN / 4; j++)
-          dst[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+          dst[j] = make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
       } else {
         uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(c) + row * n + n0);
 #pragma unroll
         for (int j = 0; j < BN / 8; j++) {
           uint4 pk;
-          __nv_bfloat162 h0 = __floats2bfloat162_rn(acc[8 * j + 0], acc[8 * j + 1]);
-          __nv_bfloat162 h1 = __floats2bfloat162_rn(acc[8 * j + 2], acc[8 * j + 3]);
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(acc[8 * j + 4], acc[8 * j + 5]);
-          __nv_bfloat162 h3 = __floats2bfloat162_rn(acc[8 * j + 6], acc[8 * j + 7]);
+          __nv_bfloat162 h0 = __floats2bfloat162_rn(out[8 * j + 0], out[8 * j + 1]);
+          __nv_bfloat162 h1 = __floats2bfloat162_rn(out[8 * j + 2], out[8 * j + 3]);
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(out[8 * j + 4], out[8 * j + 5]);
+          __nv_bfloat162 h3 = __floats2bfloat162_rn(out[8 * j + 6], out[8 * j + 7]);
           pk.x = *reinterpret_cast<uint32_t*>(&h0);
           pk.y = *reinterpret_cast<uint32_t*>(&h1);
           pk.z = *reinterpret_cast<uint32_t*>(&h2);

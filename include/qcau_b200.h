@@ -166,7 +166,8 @@ int qcau_forward(const void* c_q, const void* wq_b, const void* wq_b_scale,
  *   o [b, h, d_v] bf16 (V = cache row[:d_v]).
  *   Split-KV: partial results go to the workspace and a combine kernel
  *   merges them (workspace >= qcau_decode_attn_workspace_size(...)).
- *   On sm_100a with h % 64 == 0, d_qk == 576, d_v == 512, page_size == 64
+ *   On sm_100a with h a multiple of 128 or h in {16, 32, 64}, d_qk == 576,
+ *   d_v == 512, page_size == 64
  *   this runs the tcgen05 two-CTA kernel; other shapes run the general
  *   split-KV kernel.
  * ---------------------------------------------------------------------- */

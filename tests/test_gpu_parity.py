@@ -224,8 +224,9 @@ def _decode_abi(q, cache, table, seqlens, sink, scale, d_v, max_seqlen):
     return o
 
 
-@pytest.mark.parametrize("h,seqlens", [(16, [1, 100, 1000]), (128, [4096, 64, 777]),
-                                       (64, [0, 2000, 513])])
+# 8 and 48 heads run the general split-KV kernel, 128 the tcgen05 pair kernel
+@pytest.mark.parametrize("h,seqlens", [(8, [1, 100, 1000]), (128, [4096, 64, 777]),
+                                       (48, [0, 2000, 513])])
 def test_decode_paged_vs_oracle(h, seqlens):
     gen = torch.Generator(device="cuda").manual_seed(h)
     B, page, width = len(seqlens), 64, 576
@@ -289,9 +290,11 @@ def test_mla_decode_layer_vs_oracle():
 # ------------------------------------------------------------------ tcgen05 two-CTA decode kernel
 
 @pytest.mark.parametrize("h,seqlens", [(128, [4096, 64, 777, 1]), (128, [0, 130, 2000]),
-                                       (256, [513, 128, 3000])])
+                                       (256, [513, 128, 3000]), (64, [1000, 1, 3000, 256]),
+                                       (32, [513, 0, 2048]), (16, [77, 4096])])
 def test_decode_paged_two_cta_vs_oracle(h, seqlens):
-    """h % 128 == 0 with 576/512 widths and 64-token pages runs the tcgen05 pair kernel."""
+    """h a multiple of 128 (or a head shard of 64, 32 or 16) with 576/512
+    widths and 64-token pages runs the tcgen05 pair kernel."""
     gen = torch.Generator(device="cuda").manual_seed(7 + h + len(seqlens))
     B, page, width = len(seqlens), 64, 576
     max_pages = (max(seqlens) + page - 1) // page
