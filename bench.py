@@ -204,6 +204,54 @@ def attn_only(batch: int, ctx: int, local: int):
     print(json.dumps({"attn_only": True, "batch": batch, "ctx": ctx}))
 
 
+def gemm_only(local: int):
+    """A small FP8 GEMM case for ncu and tuning: the decode layer's q-up
+    ([128,1536] x [24576,1536]) and o-proj ([128,16384] x [7168,16384]) with
+    fp32 128x128 block scales; 3 warm-up and 5 timed launches of each.  The
+    two weights (155 MB) exceed L2 and are read alternately."""
+    from qcau_b200 import _lib
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev).manual_seed(3)
+    L = _lib.lib()
+    shapes = {"q_up": (BATCH, HEADS * 192, DC), "o_proj": (BATCH, DIM, HEADS * 128)}
+    ops = {}
+    for name, (m, n, k) in shapes.items():
+        a = torch.randn(m, k, device=dev, generator=gen).to(torch.float8_e4m3fn)
+        b = torch.randn(n, k, device=dev, generator=gen).to(torch.float8_e4m3fn)
+        sa = torch.rand(m, k // 128, device=dev, generator=gen) + 0.5
+        sb = torch.rand(n // 128, k // 128, device=dev, generator=gen) + 0.5
+        c = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        ops[name] = (a, sa, b, sb, c, m, n, k)
+
+    def run(name):
+        a, sa, b, sb, c, m, n, k = ops[name]
+        _lib.check(L.qcau_fp8_gemm(a.data_ptr(), sa.data_ptr(), b.data_ptr(), sb.data_ptr(),
+                                   c.data_ptr(), m, n, k, _lib.SCALE_F32, _lib.OUT_BF16,
+                                   _lib.stream_ptr(dev)), name)
+
+    for _ in range(3):
+        for name in ops:
+            run(name)
+    res = {}
+    for name, (a, sa, b, sb, c, m, n, k) in ops.items():
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        times = []
+        for _ in range(5):
+            run("q_up" if name == "o_proj" else "o_proj")  # evict this weight from L2
+            ev[0].record()
+            run(name)
+            ev[1].record()
+            torch.cuda.synchronize(dev)
+            times.append(ev[0].elapsed_time(ev[1]))
+        t = sorted(times)[len(times) // 2] * 1e-3
+        nbytes = n * k + m * k + m * n * 2 + (n // 128) * (k // 128) * 4 + m * (k // 128) * 4
+        res[name] = {"us": t * 1e6, "GB/s": nbytes / t / 1e9, "TFLOP/s": 2.0 * m * n * k / t / 1e12}
+    assert _lib.device_error() == 0
+    print(json.dumps({"gemm_only": True, **res}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -213,12 +261,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--attn-only", action="store_true",
                     help="profiling case: only the decode attention, --batch x --ctx, 5 launches")
+    ap.add_argument("--gemm-only", action="store_true",
+                    help="profiling case: the layer's two FP8 GEMMs at batch 128")
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--ctx", type=int, default=4096)
     args = ap.parse_args()
     ws, rank, local = dist_env()
     if args.attn_only:
         attn_only(args.batch, args.ctx, local)
+        return
+    if args.gemm_only:
+        gemm_only(local)
         return
     if args.impl == "reference":
         run_reference_arm(args, rank)

@@ -8,12 +8,14 @@
 // then promoted with its two scales into a register accumulator
 // (kernel.py:246-250).  Scales may be fp32 or E8M0.
 //
-// CTA = 128 x 128 output tile, 192 threads:
+// CTA = 128 x 128 output tile, 320 threads:
 //   warp 0     TMA producer (A and B tiles, 128-byte swizzle, kStages ring)
 //   warp 1     TMEM allocator + single-thread MMA issuer
-//   warps 2-5  epilogue: TMEM -> registers, scale promotion, bf16/fp32 store
-// Two TMEM accumulators (2 x 128 columns) let the MMA of block kb+1 run
-// while the epilogue promotes block kb.
+//   warps 2-9  epilogue: TMEM -> registers, scale promotion, bf16/fp32 store;
+//              two warps per TMEM lane quarter, 64 columns each, so that one
+//              64-column load and one wait per K-block feed 32 packed FMAs
+// Four TMEM accumulators (4 x 128 columns) let the MMA run up to three
+// K-blocks ahead of the promotion.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -24,14 +26,17 @@ constexpr int BM = 128, BN = 128, BK = 128;
 constexpr int kStages = 6;
 constexpr int kTileBytes = BM * BK;  // fp8: 16 KB per operand tile
 constexpr int kStageBytes = 2 * kTileBytes;
-constexpr int kThreads = 192;
-constexpr int kTmemCols = 2 * BN;
+constexpr int kAcc = 4;              // TMEM accumulators (the MMA runs up to 3 K-blocks ahead)
+constexpr int kEpiWarps = 8;         // two per TMEM lane quarter, 64 columns each
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kTmemCols = kAcc * BN;
+constexpr int64_t kNumSmsGemm = 148;
 
 struct GemmShared {
   uint64_t full[kStages];
   uint64_t empty[kStages];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t tfull[kAcc];
+  uint64_t tempty[kAcc];
   uint32_t tmem_base;
   int abort;
 };
@@ -41,7 +46,8 @@ constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + sizeof(Gemm
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                     const void* __restrict__ sa, const void* __restrict__ sb, void* __restrict__ c,
-                    int64_t m, int64_t n, int64_t k, int a_e8m0, int b_e8m0, int out_f32, int* err) {
+                    int64_t m, int64_t n, int64_t k, int a_e8m0, int b_e8m0, int out_f32,
+                    int splits, int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* tiles = smem_raw + pad;
@@ -51,15 +57,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t n0 = (int64_t)blockIdx.x * BN, m0 = (int64_t)blockIdx.y * BM;
   const int KB = (int)(k / BK);
+  // split-K: CTA z of a cluster of `splits` runs K-blocks [kb0, kb1)
+  const int z = (int)blockIdx.z;
+  const int kb0 = (int)((int64_t)KB * z / splits), kb1 = (int)((int64_t)KB * (z + 1) / splits);
+  const int NKB = kb1 - kb0;
+  // epilogue role: TMEM lane quarter and 64-column half of the tile
+  const int quarter = warp & 3;
+  const int half = (warp - 2) >> 2;
+  const int row_local = quarter * 32 + lane;
+  const int64_t row = m0 + row_local;
+  uint64_t acc[32];  // epilogue: packed fp32 pairs of this thread's 64 columns
+  bool epi_ok = false;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; s++) {
       mbar_init(&sh->full[s], 1);
       mbar_init(&sh->empty[s], 1);
     }
-    for (int b = 0; b < 2; b++) {
+    for (int b = 0; b < kAcc; b++) {
       mbar_init(&sh->tfull[b], 1);
-      mbar_init(&sh->tempty[b], 4);
+      mbar_init(&sh->tempty[b], kEpiWarps);
     }
     sh->abort = 0;
     fence_barrier_init();
@@ -76,9 +93,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- producer
     int last_use[kStages];
     for (int s = 0; s < kStages; s++) last_use[s] = -1;
-    for (int kb = 0; kb < KB; kb++) {
-      const int s = kb % kStages;
-      const int u = kb / kStages;
+    for (int j = 0; j < NKB; j++) {
+      const int kb = kb0 + j;
+      const int s = j % kStages;
+      const int u = j / kStages;
       if (!mbar_wait(&sh->empty[s], (u & 1) ^ 1, abort)) break;
       mbar_arrive_expect_tx(&sh->full[s], kStageBytes);
       uint8_t* st = tiles + (size_t)s * kStageBytes;
@@ -96,11 +114,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer
     const uint32_t idesc = make_idesc(BM, BN, kFmtE4M3, kFmtE4M3, false, false);
     int committed = -1;
-    for (int kb = 0; kb < KB; kb++) {
-      const int s = kb % kStages;
-      const int u = kb / kStages;
-      const int ab = kb & 1;
-      const int ua = kb >> 1;
+    for (int j = 0; j < NKB; j++) {
+      const int s = j % kStages;
+      const int u = j / kStages;
+      const int ab = j % kAcc;
+      const int ua = j / kAcc;
       if (!mbar_wait(&sh->full[s], u & 1, abort)) break;
       if (!mbar_wait(&sh->tempty[ab], (ua & 1) ^ 1, abort)) break;
       tc_fence_after();
@@ -114,94 +132,117 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_commit(&sh->empty[s]);
       tc_commit(&sh->tfull[ab]);
-      committed = kb;
+      committed = j;
     }
     if (*abort && committed >= 0) {
       // let the issued MMAs finish before TMEM is released
       volatile int never = 0;
-      mbar_wait(&sh->tfull[committed & 1], (committed >> 1) & 1, &never);
+      mbar_wait(&sh->tfull[committed % kAcc], (committed / kAcc) & 1, &never);
     }
   } else if (warp >= 2) {
-    // ---------------- epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_local = quarter * 32 + lane;
-    const int64_t row = m0 + row_local;
+    // ---------------- epilogue: warp w owns TMEM lane quarter w % 4 and the
+    // 64 columns [64 * half, +64) of the tile
     const int64_t nblk = n0 / 128;
     // the two scales of K-block kb, loaded kPre blocks ahead: a global load
     // per block would otherwise stall every promotion
     constexpr int kPre = 4;
-    auto scale_of = [&](int kb) -> float {
-      if (kb >= KB) return 0.f;
+    auto scale_of = [&](int j) -> float {
+      if (j >= NKB) return 0.f;
+      const int kb = kb0 + j;
       const float s_a = row < m ? load_scale(sa, row * KB + kb, a_e8m0) : 0.f;
       return s_a * load_scale(sb, nblk * KB + kb, b_e8m0);
     };
     float sc0 = scale_of(0), sc1 = scale_of(1), sc2 = scale_of(2), sc3 = scale_of(3);
-    uint64_t acc[BN / 2];  // packed fp32 pairs
 #pragma unroll
-    for (int i = 0; i < BN / 2; i++) acc[i] = 0ull;
+    for (int i = 0; i < 32; i++) acc[i] = 0ull;
     bool ok = true;
-    for (int kb = 0; kb < KB; kb++) {
-      const int ab = kb & 1;
-      const int ua = kb >> 1;
+    for (int j = 0; j < NKB; j++) {
+      const int ab = j % kAcc;
+      const int ua = j / kAcc;
       const float sc = sc0;
       sc0 = sc1;
       sc1 = sc2;
       sc2 = sc3;
-      sc3 = scale_of(kb + kPre);
+      sc3 = scale_of(j + kPre);
       if (!mbar_wait(&sh->tfull[ab], ua & 1, abort)) {
         ok = false;
         break;
       }
       tc_fence_after();
       const uint64_t sc2x = f2_pack(sc, sc);
-      const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + ab * BN;
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        float v[64];
-        tmem_ld32(taddr + h * 64, *reinterpret_cast<float(*)[32]>(v));
-        tmem_ld32(taddr + h * 64 + 32, *reinterpret_cast<float(*)[32]>(v + 32));
-        tmem_ld_wait_regs(v);
-        tmem_ld_wait_regs(v + 32);
-#pragma unroll
-        for (int i = 0; i < 32; i++)
-          acc[h * 32 + i] = f2_fma(f2_pack(v[2 * i], v[2 * i + 1]), sc2x, acc[h * 32 + i]);
-      }
+      float v[64];
+      tmem_ld64(tmem + ((uint32_t)(quarter * 32) << 16) + ab * BN + half * 64, v);
+      tmem_ld_wait_regs(v);
+      tmem_ld_wait_regs(v + 32);
+      // the accumulator may be reused once every epilogue warp has read it
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh->tempty[ab]);
+#pragma unroll
+      for (int i = 0; i < 32; i++) acc[i] = f2_fma(f2_pack(v[2 * i], v[2 * i + 1]), sc2x, acc[i]);
     }
-    if (ok && row < m) {
-      float out[BN];
-#pragma unroll
-      for (int i = 0; i < BN / 2; i++) f2_unpack(acc[i], out[2 * i], out[2 * i + 1]);
-      if (out_f32) {
-        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(c) + row * n + n0);
-#pragma unroll
-        for (int j = 0; j < BN / 4; j++)
-          dst[j] = make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
-      } else {
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(c) + row * n + n0);
-#pragma unroll
-        for (int j = 0; j < BN / 8; j++) {
-          uint4 pk;
-          __nv_bfloat162 h0 = __floats2bfloat162_rn(out[8 * j + 0], out[8 * j + 1]);
-          __nv_bfloat162 h1 = __floats2bfloat162_rn(out[8 * j + 2], out[8 * j + 3]);
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(out[8 * j + 4], out[8 * j + 5]);
-          __nv_bfloat162 h3 = __floats2bfloat162_rn(out[8 * j + 6], out[8 * j + 7]);
-          pk.x = *reinterpret_cast<uint32_t*>(&h0);
-          pk.y = *reinterpret_cast<uint32_t*>(&h1);
-          pk.z = *reinterpret_cast<uint32_t*>(&h2);
-          pk.w = *reinterpret_cast<uint32_t*>(&h3);
-          dst[j] = pk;
-        }
-      }
-    }
+    epi_ok = ok;
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc<1>(tmem, kTmemCols);
+  }
+  __syncwarp();
+  if (splits > 1) {
+    // the other CTAs of the cluster park their fp32 partial tile in their
+    // (now idle) stage buffers; CTA 0 adds them in cluster-rank order
+    float* red = reinterpret_cast<float*>(tiles) + row_local * BN + 64 * half;
+    if (warp >= 2 && epi_ok && z > 0) {
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        float a0, a1, a2, a3;
+        f2_unpack(acc[2 * i], a0, a1);
+        f2_unpack(acc[2 * i + 1], a2, a3);
+        reinterpret_cast<float4*>(red)[i] = make_float4(a0, a1, a2, a3);
+      }
+    }
+    cluster_sync();
+    if (warp >= 2 && epi_ok && z == 0) {
+      for (int zz = 1; zz < splits; zz++) {
+        const uint32_t src = mapa_shared(smem_u32(red), (uint32_t)zz);
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          const float a0 = ld_shared_cluster_f32(src + 8 * i);
+          const float a1 = ld_shared_cluster_f32(src + 8 * i + 4);
+          acc[i] = f2_add(acc[i], f2_pack(a0, a1));
+        }
+      }
+    }
+    cluster_sync();
+  }
+  if (warp >= 2 && epi_ok && z == 0 && row < m) {
+    float out[64];
+#pragma unroll
+    for (int i = 0; i < 32; i++) f2_unpack(acc[i], out[2 * i], out[2 * i + 1]);
+    const int64_t col0 = n0 + 64 * half;
+    if (out_f32) {
+      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(c) + row * n + col0);
+#pragma unroll
+      for (int j = 0; j < 16; j++)
+        dst[j] = make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+    } else {
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(c) + row * n + col0);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        uint4 pk;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(out[8 * j + 0], out[8 * j + 1]);
+        __nv_bfloat162 h1 = __floats2bfloat162_rn(out[8 * j + 2], out[8 * j + 3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(out[8 * j + 4], out[8 * j + 5]);
+        __nv_bfloat162 h3 = __floats2bfloat162_rn(out[8 * j + 6], out[8 * j + 7]);
+        pk.x = *reinterpret_cast<uint32_t*>(&h0);
+        pk.y = *reinterpret_cast<uint32_t*>(&h1);
+        pk.z = *reinterpret_cast<uint32_t*>(&h2);
+        pk.w = *reinterpret_cast<uint32_t*>(&h3);
+        dst[j] = pk;
+      }
+    }
   }
   if (threadIdx.x == 0 && *abort) raise_dev_error(err, QCAU_DEVERR_TIMEOUT);
 }
@@ -225,10 +266,28 @@ cudaError_t launch_fp8_gemm(const void* a, const void* a_s, const void* b, const
   cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBytes);
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)(n / BN), (unsigned)((m + BM - 1) / BM));
-  fp8_gemm_kernel<<<grid, kThreads, kSmemBytes, st>>>(ta, tb, a_s, b_s, c, m, n, k, a_e8m0,
-                                                      b_e8m0, out_f32, device_error_word());
-  return cudaGetLastError();
+  // few output tiles (decode-size m): split K over a cluster so that every SM
+  // streams weights; the partial tiles are summed through distributed shared
+  // memory, in a fixed order
+  const int64_t tiles = (n / BN) * ((m + BM - 1) / BM);
+  const int64_t kblocks = k / BK;
+  int splits = 1;
+  if (tiles * 4 <= kNumSmsGemm && kblocks >= 16) splits = 4;
+  else if (tiles * 2 <= kNumSmsGemm && kblocks >= 8) splits = 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(n / BN), (unsigned)((m + BM - 1) / BM), (unsigned)splits);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = (unsigned)splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fp8_gemm_kernel, ta, tb, a_s, b_s, c, m, n, k, a_e8m0, b_e8m0,
+                            out_f32, splits, device_error_word());
 }
 
 }  // namespace qcau
