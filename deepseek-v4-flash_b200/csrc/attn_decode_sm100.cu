@@ -93,11 +93,15 @@ struct DecodeParams {
   const int32_t* seqlens;
   float* part_o;
   float* part_ml;
+  __nv_bfloat16* out;  // direct mode (one split): final output [rows, h, 512]
+  const float* sink;   // direct mode: attention sink [h] or nullptr
   int* err;
   int64_t max_pages, num_pages;
   int h, hgroups, splits;
   int cta_heads;  // heads each CTA owns: 64, or h/2 when h < 128 (the other MMA rows are padding)
   float scale;
+  int qlen;    // query tokens per sequence (1 = decode; > 1 = causal prefill / chunk)
+  int direct;  // 1: one split, the epilogue normalises and writes `out`
 };
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -134,8 +138,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int hg = (int)(unit % p.hgroups);
   const int64_t rest = unit / p.hgroups;
   const int split = (int)(rest % p.splits);
+  // query row r = (sequence bs, token t of qlen): token t sees the cached
+  // prefix up to its own position, seqlens[bs] - (qlen - 1 - t) tokens
   const int64_t b = rest / p.splits;
-  const int seqlen = p.seqlens[b];
+  const int64_t bs = b / p.qlen;
+  const int seqlen = p.seqlens[bs] - (p.qlen - 1 - (int)(b % p.qlen));
   const int ntiles = (seqlen + kTile - 1) / kTile;
   const int t_begin = (int)((int64_t)ntiles * split / p.splits);
   const int t_end = (int)((int64_t)ntiles * (split + 1) / p.splits);
@@ -143,6 +150,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int head0 = hg * 2 * p.cta_heads + (int)rank * p.cta_heads;
 
   if (T <= 0) {  // both CTAs of the pair take this branch together
+    if (p.direct) {  // no visible token: the output rows are zero
+      uint4* o4 = reinterpret_cast<uint4*>(p.out + (b * p.h + head0) * 512);
+      for (int i = threadIdx.x; i < p.cta_heads * 64; i += blockDim.x)
+        o4[i] = make_uint4(0u, 0u, 0u, 0u);
+      return;
+    }
     for (int i = threadIdx.x; i < p.cta_heads; i += blockDim.x) {
       const int64_t prow = (b * p.splits + split) * p.h + head0 + i;
       p.part_ml[prow * 2] = -INFINITY;
@@ -182,7 +195,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int pages_used = (seqlen + 63) / 64;
   auto page_of = [&](int pidx) -> int {
     if (pidx >= pages_used) pidx = pages_used - 1;  // masked tokens: any valid page
-    const int64_t e = p.table[b * p.max_pages + pidx];
+    const int64_t e = p.table[bs * p.max_pages + pidx];
     if (e < 0 || e >= p.num_pages) {
       raise_dev_error(p.err, QCAU_DEVERR_INDEX);
       return 0;
@@ -418,7 +431,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(&sh->lbar);
     if (ok) ok = warp_wait(&sh->lbar, 0, abort);
-    if (ok) {
+    if (ok && p.direct) {
+      // one split: sink and normalisation as attn_combine does for one part,
+      // O / (l + 2^(sink*log2e - m)), rounded to bf16
+      tc_fence_after();
+      const float l_tot = l_run + sh->xsum[row ^ 64];
+      float den;
+      const float sk = (p.sink && hl < p.cta_heads) ? p.sink[head0 + hl] * kLog2e : -INFINITY;
+      if (m_run != -INFINITY)
+        den = l_tot + exp2f(sk - m_run);
+      else
+        den = l_tot + ((p.sink && hl < p.cta_heads && isfinite(p.sink[head0 + hl])) ? 1.f : 0.f);
+      const float inv = 1.f / fmaxf(den, 1.17549435e-38f);
+      __nv_bfloat16* po = p.out + (b * p.h + head0 + hl) * 512 + 128 * half;
+#pragma unroll 1
+      for (int c = 0; c < 8; c++) {
+        float v[32];
+        tmem_ld32(tmem + lane_base + kTmemO + c * 32, v);
+        tmem_ld_wait();
+        uint4* dst = reinterpret_cast<uint4*>(po + (c >> 2) * 256 + (c & 3) * 32);
+        if (hl < p.cta_heads) {
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+            dst[i] = make_uint4(pack_bf16(v[8 * i] * inv, v[8 * i + 1] * inv),
+                                pack_bf16(v[8 * i + 2] * inv, v[8 * i + 3] * inv),
+                                pack_bf16(v[8 * i + 4] * inv, v[8 * i + 5] * inv),
+                                pack_bf16(v[8 * i + 6] * inv, v[8 * i + 7] * inv));
+        }
+      }
+    } else if (ok) {
       tc_fence_after();
       const float l_tot = l_run + sh->xsum[row ^ 64];
       const int64_t prow = (b * p.splits + split) * p.h + head0 + hl;
@@ -463,7 +504,7 @@ bool is_sm100_device() {
 }  // namespace
 
 bool decode_attn_sm100_supported(const AttnArgs& a) {
-  return a.block_table != nullptr && a.seqlens != nullptr && a.s == 1 && a.d_qk == 576 &&
+  return a.block_table != nullptr && a.seqlens != nullptr && a.s >= 1 && a.d_qk == 576 &&
          a.d_v == 512 && a.d_kv == 576 && a.page_size == 64 &&
          (a.h % 128 == 0 || a.h == 64 || a.h == 32 || a.h == 16) &&
          a.q_row_stride == 576 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 &&
@@ -476,7 +517,7 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   if (a.b == 0) return cudaSuccess;
   CUtensorMap tq, tk;
   {
-    const uint64_t dims[3] = {576, (uint64_t)a.h, (uint64_t)a.b};
+    const uint64_t dims[3] = {576, (uint64_t)a.h, (uint64_t)(a.b * a.s)};
     const uint64_t strides[2] = {1152, (uint64_t)a.h * 1152};
     const uint32_t box[3] = {64, 64, 1};
     if (!make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.q, dims, strides, box,
@@ -496,6 +537,10 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   p.seqlens = a.seqlens;
   p.part_o = a.part_o;
   p.part_ml = a.part_ml;
+  p.out = reinterpret_cast<__nv_bfloat16*>(a.o);
+  p.sink = a.sink;
+  p.qlen = (int)a.s;
+  p.direct = a.splits == 1 ? 1 : 0;
   p.err = device_error_word();
   p.max_pages = a.max_pages;
   p.num_pages = a.num_pages;
@@ -508,7 +553,7 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBytes);
   if (e != cudaSuccess) return e;
-  const int64_t units = a.b * a.splits * p.hgroups;
+  const int64_t units = a.b * a.s * a.splits * p.hgroups;
   decode_attn_sm100_kernel<<<(unsigned)(2 * units), kThreads, kSmemBytes, st>>>(tq, tk, p);
   return cudaGetLastError();
 }

@@ -112,7 +112,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) attn_general_kernel(AttnArgs p
   const bool paged = p.block_table != nullptr;
 
   // key list length and this split's tile range
-  const int64_t len = paged ? (int64_t)p.seqlens[bidx] : p.topk;
+  // paged: query t of s sees the cached prefix up to its own position
+  const int64_t len = paged ? (int64_t)p.seqlens[bidx] - (p.s - 1 - tpos) : p.topk;
   const int64_t ntiles = (len + kTileKeys - 1) / kTileKeys;
   const int64_t t_begin = ntiles * split / p.splits;
   const int64_t t_end = ntiles * (split + 1) / p.splits;

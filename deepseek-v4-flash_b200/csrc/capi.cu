@@ -142,32 +142,37 @@ int sm100_splits(int64_t b, int64_t h, int64_t max_len) {
   return best;
 }
 
-size_t attn_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int splits, bool always = false) {
-  if (splits <= 1 && !always) return 0;
+size_t attn_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int splits) {
+  if (splits <= 1) return 0;
   return align256((size_t)rows * splits * h * d_v * 4) + align256((size_t)rows * splits * h * 2 * 4);
 }
 
-// Runs paged decode attention with partials in `ws` (size checked by caller).
+// Runs paged attention for a.b sequences x a.s query tokens (s = 1: decode;
+// s > 1: token t sees the prefix up to its own position) with partials in
+// `ws` when the KV range is split (size checked by the caller).
 int run_decode_attn(AttnArgs a, void* ws, cudaStream_t st) {
   const bool sm100 = decode_attn_sm100_supported(a);
-  a.splits = sm100 ? sm100_splits(a.b, a.h, a.max_len) : general_splits(a.b, a.h, a.max_len);
-  if (a.splits > 1 || sm100) {
+  const int64_t rows = a.b * a.s;
+  a.splits = sm100 ? sm100_splits(rows, a.h, a.max_len) : general_splits(rows, a.h, a.max_len);
+  const bool partials = a.splits > 1;
+  if (partials) {
     a.part_o = reinterpret_cast<float*>(ws);
     a.part_ml = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) +
-                                         align256((size_t)a.b * a.splits * a.h * a.d_v * 4));
+                                         align256((size_t)rows * a.splits * a.h * a.d_v * 4));
   }
   if (sm100) {
     QCAU_CHECK_CUDA(launch_decode_attn_sm100(a, st));
   } else {
     QCAU_CHECK_CUDA(launch_attn_general(a, st));
   }
-  if (a.splits > 1 || sm100) QCAU_CHECK_CUDA(launch_attn_combine(a, st));
+  if (partials) QCAU_CHECK_CUDA(launch_attn_combine(a, st));
   return QCAU_OK;
 }
 
-size_t decode_ws_bytes(int64_t b, int64_t h, int64_t d_v, int64_t max_len) {
-  const size_t w1 = attn_ws_bytes(b, h, d_v, general_splits(b, h, max_len));
-  const size_t w2 = attn_ws_bytes(b, h, d_v, sm100_splits(b, h, max_len), true);
+// Workspace of run_decode_attn for `rows` query tokens, whichever kernel runs.
+size_t decode_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int64_t max_len) {
+  const size_t w1 = attn_ws_bytes(rows, h, d_v, general_splits(rows, h, max_len));
+  const size_t w2 = attn_ws_bytes(rows, h, d_v, sm100_splits(rows, h, max_len));
   return w1 > w2 ? w1 : w2;
 }
 
@@ -395,6 +400,47 @@ int qcau_decode_attn_paged(const void* q, const void* cache, const int32_t* bloc
   a.sink = attn_sink;
   a.o = o;
   a.b = b; a.s = 1; a.h = h; a.d_qk = d_qk; a.d_v = d_v; a.d_kv = d_kv;
+  a.page_size = page_size;
+  a.max_pages = max_pages;
+  a.num_pages = num_pages;
+  a.max_len = max_seqlen;
+  a.scale = softmax_scale;
+  return run_decode_attn(a, workspace, to_stream(stream));
+}
+
+size_t qcau_prefill_attn_workspace_size(int64_t b, int64_t s, int64_t h, int64_t d_v,
+                                        int64_t max_seqlen) {
+  return decode_ws_bytes(b * s, h, d_v, max_seqlen);
+}
+
+int qcau_prefill_attn_paged(const void* q, const void* cache, const int32_t* block_table,
+                            const int32_t* seqlens, const float* attn_sink, void* o, int64_t b,
+                            int64_t s, int64_t h, int64_t d_qk, int64_t d_v, int64_t d_kv,
+                            int64_t page_size, int64_t max_pages, int64_t num_pages,
+                            int64_t max_seqlen, float softmax_scale, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  QCAU_CHECK_ARG(q && cache && block_table && seqlens && o, "prefill_attn_paged: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && s >= 1 && h > 0 && page_size > 0 && max_pages > 0 && num_pages > 0,
+                 "prefill_attn_paged: bad shape");
+  QCAU_CHECK_ARG(max_seqlen >= s, "prefill_attn_paged: max_seqlen must cover the s new tokens");
+  QCAU_CHECK_ARG(max_seqlen <= max_pages * page_size,
+                 "prefill_attn_paged: max_seqlen exceeds the block table");
+  int rc = check_attn_widths(d_qk, d_v, d_kv, "prefill_attn_paged");
+  if (rc) return rc;
+  const size_t need = qcau_prefill_attn_workspace_size(b, s, h, d_v, max_seqlen);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(QCAU_ERR_WORKSPACE, "prefill_attn_paged: workspace too small (need " +
+                                        std::to_string(need) + " bytes)");
+  if (b == 0) return QCAU_OK;
+  AttnArgs a{};
+  a.q = q;
+  a.q_row_stride = d_qk;
+  a.kv = cache;
+  a.block_table = block_table;
+  a.seqlens = seqlens;
+  a.sink = attn_sink;
+  a.o = o;
+  a.b = b; a.s = s; a.h = h; a.d_qk = d_qk; a.d_v = d_v; a.d_kv = d_kv;
   a.page_size = page_size;
   a.max_pages = max_pages;
   a.num_pages = num_pages;

@@ -182,6 +182,31 @@ int qcau_decode_attn_paged(const void* q, const void* cache,
                            size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * prefill_attn_paged -- causal attention of s new query tokens per sequence
+ * over the paged latent cache that already holds them (prefill, chunked
+ * prefill, multi-token decode): the prefill branch of Attention.forward
+ * (model.py:484-543), whose causal window index lists
+ * (get_window_topk_idxs, model.py:254-264) become "every cached token up to
+ * the query's position"; same numerics as sparse_attn.
+ *   q [b, s, h, d_qk] bf16; o [b, s, h, d_v] bf16; cache / block_table as
+ *   decode_attn_paged; seqlens [b] = cached tokens of each sequence,
+ *   including its s new ones (>= s).  Token t of sequence i attends to
+ *   cache positions [0, seqlens[i] - s + t].
+ *   workspace >= qcau_prefill_attn_workspace_size(...) (zero when the KV
+ *   range is not split, e.g. at prefill sizes: the kernel then normalises and
+ *   writes o itself).  Kernels as decode_attn_paged.
+ * ---------------------------------------------------------------------- */
+size_t qcau_prefill_attn_workspace_size(int64_t b, int64_t s, int64_t h, int64_t d_v,
+                                        int64_t max_seqlen);
+int qcau_prefill_attn_paged(const void* q, const void* cache,
+                            const int32_t* block_table, const int32_t* seqlens,
+                            const float* attn_sink, void* o, int64_t b, int64_t s,
+                            int64_t h, int64_t d_qk, int64_t d_v, int64_t d_kv,
+                            int64_t page_size, int64_t max_pages, int64_t num_pages,
+                            int64_t max_seqlen, float softmax_scale, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * decode_attn_paged_noalloc -- qcau_decode_attn_paged for callers that
  * cannot allocate device memory.  No counterpart in the reference: its
  * kernels allocate through PyTorch; this entry point exists only for the

@@ -313,6 +313,84 @@ def test_decode_paged_two_cta_vs_oracle(h, seqlens):
     assert_close_attn(f32(n_bf16(o)), f32(O.f32_to_bf16(ref)), f"two-cta h{h} {seqlens}")
 
 
+# ------------------------------------------------------------------ causal prefill (paged)
+
+def _prefill_abi(q, cache, table, seqlens, sink, scale, max_seqlen):
+    B, S, H, dqk = q.shape
+    o = torch.empty(B, S, H, 512, device="cuda", dtype=torch.bfloat16)
+    L = _lib.lib()
+    need = L.qcau_prefill_attn_workspace_size(B, S, H, 512, max_seqlen)
+    ws = torch.empty(max(need, 1), device="cuda", dtype=torch.uint8)
+    _lib.check(L.qcau_prefill_attn_paged(q.data_ptr(), cache.data_ptr(), table.data_ptr(),
+                                         seqlens.data_ptr(),
+                                         None if sink is None else sink.data_ptr(), o.data_ptr(),
+                                         B, S, H, dqk, 512, cache.size(-1), cache.size(1),
+                                         table.size(1), cache.size(0), max_seqlen, float(scale),
+                                         ws.data_ptr(), need, _lib.stream_ptr()),
+               "prefill_attn_paged")
+    return o
+
+
+def _prefill_oracle(q, cache, table, seqlens, sink, scale, rows):
+    """Oracle of query rows [(b, t)]: row (b, t) is a decode row over the
+    first seqlens[b] - S + 1 + t cached tokens of sequence b."""
+    S = q.shape[1]
+    qn = n_bf16(q)
+    tb, sl = table.cpu().numpy(), seqlens.cpu().numpy()
+    q_rows = np.stack([qn[b, t] for b, t in rows])
+    t_rows = np.stack([tb[b] for b, _ in rows]).astype(np.int32)
+    l_rows = np.array([sl[b] - (S - 1 - t) for b, t in rows], dtype=np.int32)
+    return O.paged_decode_attn(q_rows, n_bf16(cache), t_rows, l_rows,
+                               None if sink is None else sink.cpu().numpy(), scale, 512)
+
+
+# 128 heads run the tcgen05 pair kernel, 48 the general kernel
+@pytest.mark.parametrize("h", [128, 48])
+def test_prefill_paged_vs_oracle(h):
+    """Causal prefill of 200 new tokens: sequence 0 holds only them, sequence
+    1 has 100 tokens already cached before them."""
+    gen = torch.Generator(device="cuda").manual_seed(31 + h)
+    B, S, page, width = 2, 200, 64, 576
+    seqlens_l = [200, 300]
+    max_pages = (max(seqlens_l) + page - 1) // page
+    pages = B * max_pages + 2
+    cache = torch.randn(pages, page, width, device="cuda", generator=gen)
+    cache = (cache * torch.rsqrt(cache.square().mean(-1, keepdim=True))).to(torch.bfloat16)
+    table = torch.randperm(pages, device="cuda", generator=gen)[:B * max_pages]
+    table = table.view(B, max_pages).to(torch.int32).contiguous()
+    sl = torch.tensor(seqlens_l, device="cuda", dtype=torch.int32)
+    q = torch.randn(B, S, h, width, device="cuda", generator=gen).to(torch.bfloat16)
+    sink = torch.randn(h, device="cuda", generator=gen)
+    scale = 192 ** -0.5
+    o = _prefill_abi(q, cache, table, sl, sink, scale, max(seqlens_l))
+    assert _lib.device_error() == 0
+    rows = [(b, t) for b in range(B) for t in range(S)]
+    ref = _prefill_oracle(q, cache, table, sl, sink, scale, rows)
+    got = f32(n_bf16(o)).reshape(B * S, h, 512)
+    assert_close_attn(got, f32(O.f32_to_bf16(ref)), f"prefill h{h}")
+
+
+def test_prefill_full_size_sampled_rows():
+    """The causal prefill configuration at full size (batch 4 x 4096 tokens x
+    128 heads, 576-wide paged cache): every output row is finite and sampled
+    rows (first token, tile edges, last token) match the oracle."""
+    gen = torch.Generator(device="cuda").manual_seed(4096)
+    B, S, H, page, width = 4, 4096, 128, 64, 576
+    from qcau_b200.mla import make_paged_cache
+    cache, table, sl = make_paged_cache(B, S, page, width, "cuda", seed=9)
+    q = torch.randn(B, S, H, width, device="cuda", generator=gen)
+    q = (q * torch.rsqrt(q.square().mean(-1, keepdim=True))).to(torch.bfloat16)
+    sink = torch.randn(H, device="cuda", generator=gen)
+    scale = 192 ** -0.5
+    o = _prefill_abi(q, cache, table, sl, sink, scale, S)
+    assert _lib.device_error() == 0
+    assert bool(torch.isfinite(o.float()).all())
+    rows = [(0, 0), (0, 255), (1, 256), (2, 2047), (3, 4095), (1, 3000)]
+    ref = _prefill_oracle(q, cache, table, sl, sink, scale, rows)
+    got = np.stack([f32(n_bf16(o[b, t])) for b, t in rows])
+    assert_close_attn(got, f32(O.f32_to_bf16(ref)), "prefill full size")
+
+
 def _mla_ws_views(layer, B):
     """Views of the decode layer's intermediates inside its workspace (the
     layout of qcau_mla_decode: x_q, s_q, q, q_abs, o_lat, o_v, x_o, s_o, ...)."""
