@@ -68,6 +68,24 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Eight e4m3 codes times a row scale, as eight bf16 (e4m3 -> f16 is exact).
+__device__ __forceinline__ uint4 e4m3x8_scaled_bf16(uint2 raw, float s) {
+  uint32_t out[4];
+  const uint32_t w[2] = {raw.x, raw.y};
+#pragma unroll
+  for (int k = 0; k < 2; k++)
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const uint16_t two = (uint16_t)(w[k] >> (16 * h));
+      uint32_t f16x2;
+      asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(f16x2) : "h"(two));
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&f16x2));
+      __nv_bfloat162 b = __floats2bfloat162_rn(f.x * s, f.y * s);
+      out[2 * k + h] = *reinterpret_cast<uint32_t*>(&b);
+    }
+  return make_uint4(out[0], out[1], out[2], out[3]);
+}
+
 // Inverse RoPE of one (re, im) pair of a bf16 output row (QCAU.py:313-319):
 // the reference rotates the bf16 attention output, so round first.
 __device__ __forceinline__ void inv_rope_pair(float& x, float& y, float2 cs) {
@@ -163,6 +181,55 @@ __global__ void __launch_bounds__(kWarps * 32, 1) attn_general_kernel(AttnArgs p
     cp_async_commit();
   };
 
+  // FP8 latent rows (gather mode): the e4m3 codes of tile t+1 are loaded
+  // into registers before tile t is computed and converted to bf16 after it,
+  // so the gather latency overlaps the math; the rope part goes by cp.async
+  const bool fp8 = DQK == 576 && p.kv_fp8 != nullptr;  // 576 = 512 codes + 64 rope
+  constexpr int kFp8Chunks = kTileKeys * 64 / (kWarps * 32);  // 8-code chunks per thread
+  uint2 fraw[kFp8Chunks];
+  float fsc[kFp8Chunks];
+  auto fp8_row = [&](int64_t t, int r) -> int64_t {
+    const int64_t j = t * kTileKeys + r;
+    if (j >= len) return -1;
+    const int64_t id = p.idx[qrow * p.topk + j];
+    return (id >= 0 && id < p.n_kv) ? bidx * p.n_kv + id : -1;
+  };
+  auto issue_fp8 = [&](int64_t t, int buf) {
+    __nv_bfloat16* dst = sKV + (size_t)buf * kTileKeys * C::kRow;
+    int* vld = sValid + buf * kTileKeys;
+#pragma unroll
+    for (int k = 0; k < kFp8Chunks; k++) {
+      const int i = tid + k * kWarps * 32, r = i >> 6, c = i & 63;
+      const int64_t row = fp8_row(t, r);
+      if (c == 0) vld[r] = row >= 0;
+      if (row >= 0) {
+        fraw[k] = __ldg(reinterpret_cast<const uint2*>(p.kv_fp8 + row * 512 + c * 8));
+        fsc[k] = __ldg(p.kv_scale + row);
+      } else {
+        fraw[k] = make_uint2(0u, 0u);
+        fsc[k] = 0.f;
+      }
+    }
+    for (int i = tid; i < kTileKeys * 8; i += kWarps * 32) {
+      const int r = i >> 3, c = i & 7;
+      const int64_t row = fp8_row(t, r);
+      const uint32_t d = smem_u32(dst + r * C::kRow + 512 + c * 8);
+      if (row >= 0)
+        cp_async16(d, reinterpret_cast<const __nv_bfloat16*>(p.kv_rope) + row * 64 + c * 8);
+      else
+        *reinterpret_cast<uint4*>(dst + r * C::kRow + 512 + c * 8) = make_uint4(0, 0, 0, 0);
+    }
+    cp_async_commit();
+  };
+  auto finish_fp8 = [&](int buf) {
+    __nv_bfloat16* dst = sKV + (size_t)buf * kTileKeys * C::kRow;
+#pragma unroll
+    for (int k = 0; k < kFp8Chunks; k++) {
+      const int i = tid + k * kWarps * 32, r = i >> 6, c = i & 63;
+      *reinterpret_cast<uint4*>(dst + r * C::kRow + c * 8) = e4m3x8_scaled_bf16(fraw[k], fsc[k]);
+    }
+  };
+
   // running state: this thread's two rows (lane/4 and lane/4 + 8)
   float m_run[2] = {-INFINITY, -INFINITY};
   float l_part[2] = {0.f, 0.f};  // this warp's share of the denominator
@@ -172,11 +239,21 @@ __global__ void __launch_bounds__(kWarps * 32, 1) attn_general_kernel(AttnArgs p
   const float sl2 = p.scale * kLog2e;
   const int r0 = lane >> 2, cq = (lane & 3) * 2;
 
-  if (t_begin < t_end) load_tile(t_begin, 0);
+  if (t_begin < t_end) {
+    if (fp8) {
+      issue_fp8(t_begin, 0);
+      finish_fp8(0);
+    } else {
+      load_tile(t_begin, 0);
+    }
+  }
   for (int64_t t = t_begin; t < t_end; t++) {
     const int buf = (int)((t - t_begin) & 1);
     if (t + 1 < t_end) {
-      load_tile(t + 1, buf ^ 1);
+      if (fp8)
+        issue_fp8(t + 1, buf ^ 1);
+      else
+        load_tile(t + 1, buf ^ 1);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
@@ -259,6 +336,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) attn_general_kernel(AttnArgs p
         }
       }
     }
+    if (fp8 && t + 1 < t_end) finish_fp8(buf ^ 1);
     __syncthreads();  // sP and the KV buffer are rewritten next iteration
   }
 

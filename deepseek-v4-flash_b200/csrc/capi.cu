@@ -408,6 +408,54 @@ int qcau_decode_attn_paged(const void* q, const void* cache, const int32_t* bloc
   return run_decode_attn(a, workspace, to_stream(stream));
 }
 
+size_t qcau_sparse_attn_fp8_workspace_size(int64_t b, int64_t s, int64_t h, int64_t topk) {
+  return attn_ws_bytes(b * s, h, 512, general_splits(b * s, h, topk));
+}
+
+int qcau_sparse_attn_fp8(const void* q, const void* kv_latent, const float* kv_scale,
+                         const void* kv_rope, const float* attn_sink, const int32_t* topk_idxs,
+                         void* o, int64_t b, int64_t s, int64_t h, int64_t n_kv, int64_t topk,
+                         float softmax_scale, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  QCAU_CHECK_ARG(q && kv_latent && kv_scale && kv_rope && topk_idxs && o,
+                 "sparse_attn_fp8: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && s >= 0 && h > 0 && topk > 0, "sparse_attn_fp8: bad shape");
+  QCAU_CHECK_ARG(n_kv > 0, "sparse_attn_fp8: kv must contain at least one latent row");
+  QCAU_CHECK_ARG((reinterpret_cast<uintptr_t>(kv_latent) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(kv_rope) & 15) == 0,
+                 "sparse_attn_fp8: kv_latent and kv_rope must be 16-byte aligned");
+  const size_t need = qcau_sparse_attn_fp8_workspace_size(b, s, h, topk);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(QCAU_ERR_WORKSPACE, "sparse_attn_fp8: workspace too small (need " +
+                                        std::to_string(need) + " bytes)");
+  if (b == 0 || s == 0) return QCAU_OK;
+  AttnArgs a{};
+  a.q = q;
+  a.q_row_stride = 576;
+  a.idx = topk_idxs;
+  a.sink = attn_sink;
+  a.o = o;
+  a.b = b; a.s = s; a.h = h; a.d_qk = 576; a.d_v = 512; a.d_kv = 576;
+  a.n_kv = n_kv;
+  a.topk = topk;
+  a.max_len = topk;
+  a.scale = softmax_scale;
+  a.kv_fp8 = reinterpret_cast<const uint8_t*>(kv_latent);
+  a.kv_scale = kv_scale;
+  a.kv_rope = kv_rope;
+  a.kv = kv_latent;
+  cudaStream_t st = to_stream(stream);
+  a.splits = general_splits(b * s, h, topk);
+  if (a.splits > 1) {
+    a.part_o = reinterpret_cast<float*>(workspace);
+    a.part_ml = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
+                                         align256((size_t)b * s * a.splits * h * 512 * 4));
+  }
+  QCAU_CHECK_CUDA(launch_attn_general(a, st));
+  if (a.splits > 1) QCAU_CHECK_CUDA(launch_attn_combine(a, st));
+  return QCAU_OK;
+}
+
 size_t qcau_prefill_attn_workspace_size(int64_t b, int64_t s, int64_t h, int64_t d_v,
                                         int64_t max_seqlen) {
   return decode_ws_bytes(b * s, h, d_v, max_seqlen);

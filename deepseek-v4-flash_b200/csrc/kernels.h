@@ -74,6 +74,12 @@ struct AttnArgs {
   int inv_rope;
   int rope_dim;
   int64_t pos0;
+  // FP8 latent cache (gather mode, 576-wide rows): kv_fp8 [b, n_kv, 512]
+  // e4m3, kv_scale [b, n_kv] fp32 per row, kv_rope [b, n_kv, 64] bf16; a
+  // row's value is bf16(e4m3 * scale) followed by its rope part.  kv is unused.
+  const uint8_t* kv_fp8;
+  const float* kv_scale;
+  const void* kv_rope;
 };
 
 // General split-KV kernel, mma.sync 16-head tiles (attn_general.cu).

@@ -67,6 +67,9 @@ SIGNATURES = {
     "qcau_decode_attn_workspace_size": ([_I64, _I64, _I64, _I64], _SZ),
     "qcau_decode_attn_paged": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
                                 _I64, _I64, _I64, _F, _P, _SZ, _P], ctypes.c_int),
+    "qcau_sparse_attn_fp8_workspace_size": ([_I64, _I64, _I64, _I64], _SZ),
+    "qcau_sparse_attn_fp8": ([_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P,
+                              _SZ, _P], ctypes.c_int),
     "qcau_prefill_attn_workspace_size": ([_I64, _I64, _I64, _I64, _I64], _SZ),
     "qcau_prefill_attn_paged": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
                                  _I64, _I64, _I64, _I64, _F, _P, _SZ, _P], ctypes.c_int),

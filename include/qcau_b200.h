@@ -182,6 +182,27 @@ int qcau_decode_attn_paged(const void* q, const void* cache,
                            size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * sparse_attn_fp8 -- sparse_attn (kernel.py:355-368) over an FP8 latent
+ * cache: top-k gather decode at long context with the latent part stored as
+ * e4m3 codes and one fp32 scale per row, the rope part in bf16.  The
+ * reference keeps its FP8 round trip in a bf16 cache (act_quant inplace,
+ * model.py:505); this layout stores the codes themselves (644 bytes per row
+ * instead of 1152) and dequantises each gathered row to
+ * bf16(e4m3 * scale) before the same attention as sparse_attn (576-wide K,
+ * V = the 512 latent values, bf16 P, sink once, index -1 skipped).
+ *   q [b, s, h, 576] bf16; kv_latent [b, n_kv, 512] e4m3 (16-byte aligned);
+ *   kv_scale [b, n_kv] fp32; kv_rope [b, n_kv, 64] bf16 (16-byte aligned);
+ *   topk_idxs [b, s, topk] int32; o [b, s, h, 512] bf16;
+ *   workspace >= qcau_sparse_attn_fp8_workspace_size(...) (split-KV partials).
+ * ---------------------------------------------------------------------- */
+size_t qcau_sparse_attn_fp8_workspace_size(int64_t b, int64_t s, int64_t h, int64_t topk);
+int qcau_sparse_attn_fp8(const void* q, const void* kv_latent, const float* kv_scale,
+                         const void* kv_rope, const float* attn_sink,
+                         const int32_t* topk_idxs, void* o, int64_t b, int64_t s,
+                         int64_t h, int64_t n_kv, int64_t topk, float softmax_scale,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * prefill_attn_paged -- causal attention of s new query tokens per sequence
  * over the paged latent cache that already holds them (prefill, chunked
  * prefill, multi-token decode): the prefill branch of Attention.forward

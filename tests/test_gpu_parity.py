@@ -156,6 +156,107 @@ def test_sparse_attn_shapes_vs_oracle(h, topk, n):
     assert_close_attn(got, f32(O.f32_to_bf16(ref)), f"h{h} k{topk}")
 
 
+# ------------------------------------------------------------------ FP8 latent cache (top-k gather)
+
+def _fp8_cache(B, N, gen, device="cuda"):
+    """Random FP8 latent cache: e4m3 codes (no NaN code), one fp32 scale per
+    row, bf16 rope part."""
+    mag = torch.randint(0, 0x7F, (B, N, 512), device=device, generator=gen, dtype=torch.uint8)
+    sign = torch.randint(0, 2, (B, N, 512), device=device, generator=gen, dtype=torch.uint8) << 7
+    codes = (mag | sign).contiguous()
+    scale = (torch.rand(B, N, device=device, generator=gen) * 0.01 + 1e-3).contiguous()
+    rope = torch.randn(B, N, 64, device=device, generator=gen).to(torch.bfloat16).contiguous()
+    return codes, scale, rope
+
+
+def _fp8_rows_bf16(codes_u8, scale, rope_u16):
+    """The rows' values as the kernel sees them: bf16(e4m3 * scale) ‖ rope."""
+    lat = O.f32_to_bf16(O.e4m3_to_f32(codes_u8) * scale[..., None].astype(np.float32))
+    return np.concatenate([lat, rope_u16], axis=-1)
+
+
+def _sparse_fp8_abi(q, codes, scale, rope, sink, idx, sm_scale):
+    B, S, H, _ = q.shape
+    o = torch.empty(B, S, H, 512, device="cuda", dtype=torch.bfloat16)
+    L = _lib.lib()
+    need = L.qcau_sparse_attn_fp8_workspace_size(B, S, H, idx.size(-1))
+    ws = torch.empty(max(need, 1), device="cuda", dtype=torch.uint8)
+    _lib.check(L.qcau_sparse_attn_fp8(q.data_ptr(), codes.data_ptr(), scale.data_ptr(),
+                                      rope.data_ptr(), None if sink is None else sink.data_ptr(),
+                                      idx.data_ptr(), o.data_ptr(), B, S, H, codes.size(1),
+                                      idx.size(-1), float(sm_scale), ws.data_ptr(), need,
+                                      _lib.stream_ptr()), "sparse_attn_fp8")
+    return o
+
+
+@pytest.mark.parametrize("h", [16, 128])
+def test_sparse_attn_fp8_vs_oracle(h):
+    gen = torch.Generator(device="cuda").manual_seed(77 + h)
+    B, S, N, K = 2, 2, 5000, 2048
+    codes, scale, rope = _fp8_cache(B, N, gen)
+    q = torch.randn(B, S, h, 576, device="cuda", generator=gen).to(torch.bfloat16)
+    idx = torch.randint(-1, N, (B, S, K), device="cuda", generator=gen, dtype=torch.int32)
+    idx[1, 1, :] = -1  # a query with no valid key -> zeros
+    sink = torch.randn(h, device="cuda", generator=gen)
+    o = _sparse_fp8_abi(q, codes, scale, rope, sink, idx, 192 ** -0.5)
+    assert _lib.device_error() == 0
+    kv = _fp8_rows_bf16(n_u8(codes), scale.cpu().numpy(), n_bf16(rope))
+    ref = O.sparse_attn(n_bf16(q), kv, sink.cpu().numpy(), idx.cpu().numpy(), 192 ** -0.5, 512)
+    got = f32(n_bf16(o))
+    assert np.all(got[1, 1] == 0)
+    assert_close_attn(got, f32(O.f32_to_bf16(ref)), f"fp8 sparse h{h}")
+
+
+def test_sparse_attn_fp8_long_context_sampled():
+    """The long-context sparse decode configuration at its per-rank shape of
+    an 8-GPU head shard: batch 64, 131072 cached rows per sequence (FP8
+    latent + fp32 row scale + bf16 rope), top-2048 indices drawn without
+    replacement, 16 heads; sampled sequences against the oracle."""
+    gen = torch.Generator(device="cuda").manual_seed(131072)
+    B, N, K, H = 64, 131072, 2048, 16
+    codes, scale, rope = _fp8_cache(B, N, gen)
+    q = torch.randn(B, 1, H, 576, device="cuda", generator=gen)
+    q = (q * torch.rsqrt(q.square().mean(-1, keepdim=True))).to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(N, device="cuda", generator=gen)[:K] for _ in range(B)])
+    idx = idx.to(torch.int32).view(B, 1, K).contiguous()
+    sink = torch.randn(H, device="cuda", generator=gen)
+    o = _sparse_fp8_abi(q, codes, scale, rope, sink, idx, 192 ** -0.5)
+    assert _lib.device_error() == 0
+    assert bool(torch.isfinite(o.float()).all())
+    for b in (0, 31, 63):
+        rows = idx[b, 0].long()
+        kv = _fp8_rows_bf16(n_u8(codes[b, rows]), scale[b, rows].cpu().numpy(),
+                            n_bf16(rope[b, rows]))[None]
+        local = np.arange(K, dtype=np.int32).reshape(1, 1, K)
+        ref = O.sparse_attn(n_bf16(q[b:b + 1]), kv, sink.cpu().numpy(), local, 192 ** -0.5, 512)
+        assert_close_attn(f32(n_bf16(o[b:b + 1])), f32(O.f32_to_bf16(ref)), f"long ctx b{b}")
+
+
+def test_sparse_attn_reference_fp8_roundtrip_cache():
+    """The reference's own FP8 cache: the 512 non-rope values of each row go
+    through act_quant(block 64, UE8M0, inplace) and stay bf16 (model.py:505);
+    sparse_attn then reads that bf16 cache."""
+    gen = torch.Generator(device="cuda").manual_seed(505)
+    B, S, N, K, H = 2, 1, 3000, 512, 64
+    kv = torch.randn(B, N, 576, device="cuda", generator=gen).to(torch.bfloat16)
+    kv0 = n_bf16(kv).copy()
+    lat = kv[..., :512].contiguous()
+    kernel.act_quant(lat, 64, "ue8m0", torch.float8_e8m0fnu, inplace=True)
+    kv[..., :512] = lat
+    q = torch.randn(B, S, H, 576, device="cuda", generator=gen).to(torch.bfloat16)
+    idx = torch.randint(-1, N, (B, S, K), device="cuda", generator=gen, dtype=torch.int32)
+    sink = torch.randn(H, device="cuda", generator=gen)
+    o = torch.empty(B, S, H, 512, device="cuda", dtype=torch.bfloat16)
+    _lib.check(_lib.lib().qcau_sparse_attn(
+        q.data_ptr(), kv.data_ptr(), sink.data_ptr(), idx.data_ptr(), o.data_ptr(), B, S, H, 576,
+        512, 576, N, K, float(192 ** -0.5), 0, None, 64, 0, 0, _lib.stream_ptr()), "sparse_attn")
+    kv_ref = kv0.copy()
+    kv_ref[..., :512] = O.act_quant_inplace(kv0[..., :512].copy(), 64, True)
+    assert np.array_equal(kv_ref, n_bf16(kv))  # the round trip is bit-exact
+    ref = O.sparse_attn(n_bf16(q), kv_ref, sink.cpu().numpy(), idx.cpu().numpy(), 192 ** -0.5, 512)
+    assert_close_attn(f32(n_bf16(o)), f32(O.f32_to_bf16(ref)), "reference fp8 cache")
+
+
 # ------------------------------------------------------------------ QCAU block
 
 def _qcau_inputs(golden_dir):
