@@ -252,6 +252,82 @@ def gemm_only(local: int):
     print(json.dumps({"gemm_only": True, **res}))
 
 
+def _time_ms(fn, warmup=2, reps=5):
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ev[0].record()
+    for _ in range(reps):
+        fn()
+    ev[1].record()
+    torch.cuda.synchronize()
+    return ev[0].elapsed_time(ev[1]) / reps
+
+
+def prefill_only(local: int):
+    """Causal prefill attention, batch 4 x 4096 new tokens x 128 heads over the
+    paged 576-wide cache (qcau_prefill_attn_paged); device time per call."""
+    from qcau_b200 import _lib
+    from qcau_b200.mla import make_paged_cache
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, S = 4, 4096
+    cache, table, sl = make_paged_cache(B, S, PAGE, WIDTH, dev, seed=0)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    q = torch.randn(B, S, HEADS, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
+    o = torch.empty(B, S, HEADS, 512, device=dev, dtype=torch.bfloat16)
+    L = _lib.lib()
+    need = L.qcau_prefill_attn_workspace_size(B, S, HEADS, 512, S)
+    ws = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+
+    def run():
+        _lib.check(L.qcau_prefill_attn_paged(q.data_ptr(), cache.data_ptr(), table.data_ptr(),
+                                             sl.data_ptr(), None, o.data_ptr(), B, S, HEADS,
+                                             WIDTH, 512, WIDTH, PAGE, table.size(1),
+                                             cache.size(0), S, 192 ** -0.5, ws.data_ptr(), need,
+                                             _lib.stream_ptr(dev)), "prefill")
+    ms = _time_ms(run)
+    assert _lib.device_error() == 0
+    flops = 2.0 * B * HEADS * (S * (S + 1) / 2) * (WIDTH + 512)
+    print(json.dumps({"prefill_only": True, "batch": B, "seq": S, "heads": HEADS, "ms": ms,
+                      "TFLOP/s": flops / ms / 1e9, "workspace_bytes": need}))
+
+
+def sparse_fp8_only(local: int, heads: int):
+    """Long-context sparse decode over an FP8 latent cache: batch 64, 131072
+    rows per sequence (e4m3 latent + fp32 row scale + bf16 rope), top-2048
+    indices, `heads` heads (16 = one rank of an 8-way head shard)."""
+    from qcau_b200 import _lib
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, N, K = 64, 131072, 2048
+    gen = torch.Generator(device=dev).manual_seed(2)
+    codes = torch.randint(0, 0x7F, (B, N, 512), device=dev, generator=gen, dtype=torch.uint8)
+    scale = torch.rand(B, N, device=dev, generator=gen) * 0.01 + 1e-3
+    rope = torch.randn(B, N, 64, device=dev, generator=gen).to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(N, device=dev, generator=gen)[:K] for _ in range(B)])
+    idx = idx.to(torch.int32).view(B, 1, K).contiguous()
+    q = torch.randn(B, 1, heads, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
+    o = torch.empty(B, 1, heads, 512, device=dev, dtype=torch.bfloat16)
+    L = _lib.lib()
+    need = L.qcau_sparse_attn_fp8_workspace_size(B, 1, heads, K)
+    ws = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+
+    def run():
+        _lib.check(L.qcau_sparse_attn_fp8(q.data_ptr(), codes.data_ptr(), scale.data_ptr(),
+                                          rope.data_ptr(), None, idx.data_ptr(), o.data_ptr(), B,
+                                          1, heads, N, K, 192 ** -0.5, ws.data_ptr(), need,
+                                          _lib.stream_ptr(dev)), "sparse_fp8")
+    ms = _time_ms(run)
+    assert _lib.device_error() == 0
+    nbytes = B * K * (512 + 4 + 128) + B * K * 4 + B * heads * (WIDTH + 512) * 2
+    print(json.dumps({"sparse_fp8_only": True, "batch": B, "rows": N, "topk": K, "heads": heads,
+                      "us": ms * 1e3, "GB/s": nbytes / ms / 1e6, "algorithmic_bytes": nbytes}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -263,6 +339,10 @@ def main():
                     help="profiling case: only the decode attention, --batch x --ctx, 5 launches")
     ap.add_argument("--gemm-only", action="store_true",
                     help="profiling case: the layer's two FP8 GEMMs at batch 128")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="time the causal prefill attention, batch 4 x 4096 x 128 heads")
+    ap.add_argument("--sparse-fp8-only", type=int, default=0, metavar="HEADS",
+                    help="time the FP8-cache top-k sparse decode (batch 64, 131072 rows) at HEADS")
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--ctx", type=int, default=4096)
     args = ap.parse_args()
@@ -272,6 +352,12 @@ def main():
         return
     if args.gemm_only:
         gemm_only(local)
+        return
+    if args.prefill_only:
+        prefill_only(local)
+        return
+    if args.sparse_fp8_only:
+        sparse_fp8_only(local, args.sparse_fp8_only)
         return
     if args.impl == "reference":
         run_reference_arm(args, rank)

@@ -19,11 +19,13 @@ namespace qcau {
 namespace {
 
 constexpr int BM = 128, BN = 128, BK = 64;  // BK bf16 = 128-byte rows
-constexpr int kStages = 4;
 constexpr int kTileBytes = 128 * BK * 2;   // 16 KB
 constexpr int kStageBytes = 2 * kTileBytes;
 constexpr int kThreads = 192;
 
+// Stages of the TMA ring: 2 (66 KB, three CTAs per SM) when K fits in two
+// steps, as in the absorb (K = 128); 4 for longer K (the v-up, K = 512).
+template <int kStages>
 struct BmmShared {
   uint64_t full[kStages];
   uint64_t empty[kStages];
@@ -31,8 +33,12 @@ struct BmmShared {
   uint32_t tmem_base;
   int abort;
 };
-constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + sizeof(BmmShared);
+template <int kStages>
+constexpr size_t smem_bytes() {
+  return 1024 + (size_t)kStages * kStageBytes + sizeof(BmmShared<kStages>);
+}
 
+template <int kStages>
 __global__ void __launch_bounds__(kThreads, 1)
     bmm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                int b_kmajor, __nv_bfloat16* __restrict__ c, int64_t c_bstride, int64_t c_rstride,
@@ -40,7 +46,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* tiles = smem_raw + pad;
-  BmmShared* sh = reinterpret_cast<BmmShared*>(tiles + (size_t)kStages * kStageBytes);
+  BmmShared<kStages>* sh =
+      reinterpret_cast<BmmShared<kStages>*>(tiles + (size_t)kStages * kStageBytes);
   volatile int* abort = &sh->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, g = blockIdx.z;
@@ -177,15 +184,17 @@ cudaError_t launch_bf16_bmm(const BmmArgs& p, cudaStream_t st) {
                    CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
   }
-  cudaError_t e = cudaFuncSetAttribute(bmm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kSmemBytes);
-  if (e != cudaSuccess) return e;
   dim3 grid((unsigned)(p.n / BN), (unsigned)((p.m + BM - 1) / BM), (unsigned)p.batch);
-  bmm_kernel<<<grid, kThreads, kSmemBytes, st>>>(ta, tb, p.b_kmajor,
-                                                 reinterpret_cast<__nv_bfloat16*>(p.c),
-                                                 p.c_bstride, p.c_rstride, p.m, p.k,
-                                                 device_error_word());
-  return cudaGetLastError();
+  auto go = [&](auto kern, size_t smem) -> cudaError_t {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, kThreads, smem, st>>>(ta, tb, p.b_kmajor, reinterpret_cast<__nv_bfloat16*>(p.c),
+                                       p.c_bstride, p.c_rstride, p.m, p.k, device_error_word());
+    return cudaGetLastError();
+  };
+  if (p.k / BK <= 2) return go(bmm_kernel<2>, smem_bytes<2>());
+  return go(bmm_kernel<4>, smem_bytes<4>());
 }
 
 }  // namespace qcau

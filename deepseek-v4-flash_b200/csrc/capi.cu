@@ -643,9 +643,10 @@ int qcau_mla_decode(const qcau_mla_dims* d, const void* q_lora, const void* wq_b
                                    d->act_round_scale, a_e8, 0, st));
   QCAU_CHECK_CUDA(launch_fp8_gemm(ws + w.xq, ws + w.sq, wq_b, wq_b_scale, ws + w.q, B, H * dq,
                                   d->dc, a_e8, w_e8, 0, st));
-  // RoPE on q_rope (last 64 of each head) at each sequence's position
-  QCAU_CHECK_CUDA(launch_head_norm_rope(ws + w.q, nullptr, freqs, positions, B, 1, H, (int)dq, dq,
-                                        (int)d->d_rope, 0, 0.f, 0, 1, 0, st));
+  // RoPE on q_rope (last 64 of each head) at each sequence's position, in
+  // place and into the rope slot of q_abs (q_abs[:, :, kv_lora:])
+  QCAU_CHECK_CUDA(launch_rope_pairs(ws + w.q + d->d_nope * 2, dq, ws + w.qabs + d->kv_lora * 2,
+                                    dabs, freqs, positions, B, 1, H, (int)d->d_rope, 0, 0, st));
   // q_abs[:, :, :512] = q_nope . W_UK ;  q_abs[:, :, 512:] = q_rope
   {
     BmmArgs m{};
@@ -664,9 +665,6 @@ int qcau_mla_decode(const qcau_mla_dims* d, const void* q_lora, const void* wq_b
     m.n = d->kv_lora;
     m.k = d->d_nope;
     QCAU_CHECK_CUDA(launch_bf16_bmm(m, st));
-    QCAU_CHECK_CUDA(cudaMemcpy2DAsync(ws + w.qabs + d->kv_lora * 2, dabs * 2,
-                                      ws + w.q + d->d_nope * 2, dq * 2, d->d_rope * 2,
-                                      (size_t)(B * H), cudaMemcpyDeviceToDevice, st));
   }
   // o_lat = attention over the paged latent cache (V = first 512 of each row)
   {

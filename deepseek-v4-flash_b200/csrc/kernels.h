@@ -23,6 +23,13 @@ cudaError_t launch_act_quant(const void* x, void* y, void* s, int64_t m, int64_t
 cudaError_t launch_dequant_fp8_weight(const void* w, const void* s, int scale_e8m0, void* out,
                                       int64_t rows, int64_t cols, cudaStream_t st);
 
+// RoPE of the rope part of rows (x points at the first rope value of row 0),
+// in place, optionally also stored to `copy` rows; one thread per pair.
+cudaError_t launch_rope_pairs(void* x, int64_t x_stride, void* copy, int64_t copy_stride,
+                              const float* freqs, const int32_t* positions, int64_t b, int64_t s,
+                              int64_t h, int rope_dim, int64_t pos0, int inverse,
+                              cudaStream_t st);
+
 cudaError_t launch_head_norm_rope(void* q, const void* gamma, const float* freqs,
                                   const int32_t* positions, int64_t b, int64_t s, int64_t h,
                                   int d, int64_t row_stride, int rope_dim, int64_t pos0,

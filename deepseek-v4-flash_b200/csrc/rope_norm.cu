@@ -100,4 +100,45 @@ cudaError_t launch_head_norm_rope(void* q, const void* gamma, const float* freqs
   return cudaGetLastError();
 }
 
+// RoPE of the rope part only: one thread per (re, im) pair of a row, the
+// rotated pair written back in place and, when `copy` is given, also to the
+// matching pair of another row layout (the absorbed query's rope slot), so
+// that the rope part is read once.  Same arithmetic as head_norm_rope_kernel.
+__global__ void rope_pairs_kernel(__nv_bfloat16* __restrict__ x, int64_t x_stride,
+                                  __nv_bfloat16* __restrict__ copy, int64_t copy_stride,
+                                  const float* __restrict__ freqs,
+                                  const int32_t* __restrict__ positions, int64_t rows,
+                                  int64_t seqlen, int64_t heads, int pairs, int64_t pos0,
+                                  int inverse) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * pairs) return;
+  const int64_t r = i / pairs;
+  const int j = (int)(i % pairs);
+  const int64_t bt = r / heads, b = bt / seqlen, t = bt % seqlen;
+  const int64_t pos = positions ? (int64_t)positions[b * seqlen + t] : pos0 + t;
+  const float2 cs = reinterpret_cast<const float2*>(freqs)[pos * pairs + j];
+  const float sn = inverse ? -cs.y : cs.y;
+  __nv_bfloat162* px = reinterpret_cast<__nv_bfloat162*>(x + r * x_stride) + j;
+  const float2 v = __bfloat1622float2(*px);
+  const __nv_bfloat162 o = __floats2bfloat162_rn(__fsub_rn(__fmul_rn(v.x, cs.x), __fmul_rn(v.y, sn)),
+                                                 __fadd_rn(__fmul_rn(v.x, sn), __fmul_rn(v.y, cs.x)));
+  *px = o;
+  if (copy) reinterpret_cast<__nv_bfloat162*>(copy + r * copy_stride)[j] = o;
+}
+
+cudaError_t launch_rope_pairs(void* x, int64_t x_stride, void* copy, int64_t copy_stride,
+                              const float* freqs, const int32_t* positions, int64_t b, int64_t s,
+                              int64_t h, int rope_dim, int64_t pos0, int inverse,
+                              cudaStream_t st) {
+  const int64_t rows = b * s * h;
+  if (rows == 0) return cudaSuccess;
+  if (rope_dim <= 0 || (rope_dim & 1)) return cudaErrorInvalidValue;
+  const int pairs = rope_dim / 2;
+  const int64_t n = rows * pairs;
+  rope_pairs_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+      reinterpret_cast<__nv_bfloat16*>(x), x_stride, reinterpret_cast<__nv_bfloat16*>(copy),
+      copy_stride, freqs, positions, rows, s, h, pairs, pos0, inverse);
+  return cudaGetLastError();
+}
+
 }  // namespace qcau
