@@ -11,32 +11,37 @@
 // same quotient and P stays <= 2^8 (bf16 rounding is scale-free).
 //
 // Work unit = one CTA pair (cluster of 2) x one sequence x one KV split x 128
-// heads; tiles of 256 tokens (4 pages).  CTA r of the pair owns heads
+// heads; tiles of 128 tokens (2 pages).  CTA r of the pair owns heads
 // [64r, 64r+64) of the group.  With h = 64, 32 or 16 heads (a head shard of
 // 128) the pair owns all h heads, h/2 per CTA, and the remaining MMA rows of
 // each CTA are padding (Q rows of other heads, or zeros past h) whose outputs
 // are not written: the cache bytes, which bound the kernel, are the same.
-//   QK : tcgen05.mma.cta_group::2, M = 128 heads, N = 256 tokens (CTA r
-//        supplies pages 4t+2r and 4t+2r+1), K = 576 in 9 chunks of 64
-//        -> S in TMEM, 2x2 lane layout: lanes 0-63 tokens 0-127, lanes
-//        64-127 tokens 128-255 of the CTA's 64 heads (128 columns, two buffers)
+//   QK : tcgen05.mma.cta_group::2, M = 128 heads, N = 128 tokens (CTA r
+//        supplies page 2t+r), K = 576 in 9 chunks of 64
+//        -> S in TMEM, 2x2 lane layout: lanes 0-63 tokens 0-63, lanes
+//        64-127 tokens 64-127 of the CTA's 64 heads (64 columns, two buffers)
 //   PV : cta_group::2, M = 128 heads, N = 256 dims (two MMAs cover 512),
-//        K = 256 tokens; A = bf16 P in shared memory, B = V rows given
-//        MN-major (CTA r supplies dims [256j + 128r, +128))
-//        -> O in TMEM: lanes 0-63 dims [256j, +128), lanes 64-127 the next 128
+//        K = 128 tokens; A = bf16 P in shared memory, B = V rows given
+//        MN-major (for MMA j, CTA r supplies dims [256r + 128j, +128))
+//        -> O in TMEM, MMA j at columns [128j, +128): lanes 0-63 dims
+//        [128j, +128), lanes 64-127 dims [256 + 128j, +128)
 // Issue-rate notes (measured on B200): pair MMAs with N = 128 run at two
 // thirds of the rate of N = 256; a blocking mbarrier wait in the issuing
 // thread costs hundreds of cycles even when the phase is complete, and the
 // tensor queue is shallow, so QK and PV are issued by two different threads
 // (one stream's waits are covered by the other's queued MMAs), every wait
-// guards at least 4 MMAs, and TMA barriers are waited with CTA scope and no
+// guards at least 8 MMAs, and TMA barriers are waited with CTA scope and no
 // tcgen05 fence per chunk.
-// Shared memory: Q (64 heads x 576, 72 KB), P (64 heads x 256 tokens, 32 KB),
-// a K ring of 3 x 16 KB slots (one 64-dim chunk of the CTA's two pages) and a
-// V ring of 4 x 16 KB slots (one page x the CTA's 128 dims of one PV MMA),
-// each ring with its own producer warp.  A bulk L2 prefetch of whole pages
-// ahead of the K reads was measured to add DRAM reads (the prefetched lines
-// were not the ones the TMA reads hit) and to cost ~20% of the time: none.
+// Shared memory: Q (64 heads x 576, 72 KB), P (64 heads x 128 tokens, 16 KB),
+// a K ring of 3 x 24 KB slots (three 64-dim chunks of the CTA's page) and a
+// V ring of 2 x 32 KB slots (one page x the CTA's 256 dims), each ring with
+// its own producer warp.  The TMA engine's cost is per box (8 KB boxes of
+// 128-byte rows cap a CTA at ~32 GB/s, 24-32 KB boxes reach HBM bandwidth),
+// so K and V come in multi-chunk boxes of one page from a 4-D view of the
+// cache [pages][64 tokens][9 chunks][64 values]; the 128-token tile is what
+// lets each CTA's QK operand be a single page.  A bulk L2 prefetch of whole
+// pages ahead of the K reads was measured to add DRAM reads and to cost ~20%
+// of the time: none.
 // Warps: 0 K producer, 1 TMEM allocator + QK issuer (pair leader), 2-5
 // softmax / O correction / epilogue (one TMEM lane each), 6 V producer,
 // 7 PV issuer (pair leader).
@@ -49,20 +54,20 @@ namespace qcau {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kTile = 256;            // tokens per tile (four pages)
-constexpr int kKSlot = 16384;         // 128 tokens x 64 dims
+constexpr int kTile = 128;            // tokens per tile (two pages, one per CTA for K)
+constexpr int kKSlot = 24576;         // this CTA's page x 3 chunks of 64 dims (one box)
 constexpr int kKSlots = 3;
-constexpr int kKPerTile = 9;          // 576 / 64
-constexpr int kVSlot = 16384;         // 64 tokens x 128 dims
-constexpr int kVSlots = 4;
-constexpr int kVPerTile = 8;          // 2 PV MMAs x 4 pages
+constexpr int kKPerTile = 3;          // 9 chunks = 576 dims in 3 boxes
+constexpr int kVSlot = 32768;         // one page x this CTA's 256 dims (4 chunks, one box)
+constexpr int kVSlots = 2;
+constexpr int kVPerTile = 2;          // the tile's 2 pages
 constexpr int kQBytes = 9 * 8192;     // 64 heads x 576 bf16 (9 chunks of 64 rows)
-constexpr int kPBytes = 4 * 8192;     // 64 heads x 256 tokens bf16 (4 chunks of 64 tokens)
+constexpr int kPBytes = 2 * 8192;     // 64 heads x 128 tokens bf16 (2 chunks of 64 tokens)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescale = 8.0f;      // raise the running max only beyond 2^8
 
 constexpr uint32_t kTmemO = 0;        // 2 accumulators x 128 columns
-constexpr uint32_t kTmemS = 256;      // 2 buffers x 128 columns
+constexpr uint32_t kTmemS = 256;      // 2 buffers x 64 columns
 constexpr uint32_t kTmemCols = 512;
 
 struct DecodeShared {
@@ -121,7 +126,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     decode_attn_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
-                             const __grid_constant__ CUtensorMap tm_k, DecodeParams p) {
+                             const __grid_constant__ CUtensorMap tm_k,
+                             const __grid_constant__ CUtensorMap tm_v, DecodeParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* sQ = smem_raw + pad;
@@ -205,7 +211,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   if (warp == 0 || warp == 6) {
     // ------------------------------------------------ TMA producers (both CTAs)
-    // warp 0: Q, then the K chunks of tiles 0, 1, ...; warp 6: the V quarters.
+    // warp 0: Q, then the K boxes of tiles 0, 1, ...; warp 6: the V pages.
     if (lane == 0) {
       const bool is_k = warp == 0;
       uint64_t* fullb = is_k ? sh->kfull : sh->vfull;
@@ -232,18 +238,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           last_use[slot] = u;
           const uint32_t fb = mapa_shared(smem_u32(&fullb[slot]), 0);
           if (is_k) {
-            // chunk i (dims 64i..64i+63) of this CTA's two pages
-            uint8_t* dst = sK + slot * kKSlot;
-            tma_load_3d_pair(dst, &tm_k, fb, 64 * i, 0, page_of(4 * t + 2 * (int)rank));
-            tma_load_3d_pair(dst + 8192, &tm_k, fb, 64 * i, 0, page_of(4 * t + 2 * (int)rank + 1));
+            // chunks 3i..3i+2 (dims 192i..192i+191) of this CTA's page of the tile
+            tma_load_4d_pair(sK + slot * kKSlot, &tm_k, fb, 0, 0, 3 * i,
+                             page_of(2 * t + (int)rank));
           } else {
-            // PV MMA j = i/4 over page i%4 of the tile
-            const int j = i >> 2, pg = i & 3;
-            const int q0 = 4 * j + 2 * (int)rank;   // this CTA's two 64-dim chunks
-            const int page = page_of(4 * t + pg);
-            uint8_t* dst = sV + slot * kVSlot;
-            tma_load_3d_pair(dst, &tm_k, fb, 64 * q0, 0, page);
-            tma_load_3d_pair(dst + 8192, &tm_k, fb, 64 * (q0 + 1), 0, page);
+            // page i of the tile: this CTA's dims [256r, 256r+256), 4 chunks in one box
+            tma_load_4d_pair(sV + slot * kVSlot, &tm_v, fb, 0, 0, 4 * (int)rank,
+                             page_of(2 * t + i));
           }
         }
       }
@@ -265,7 +266,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int last_phase = 0;
       bool ok = true;
       if (warp == 1) {
-        const uint32_t idesc_qk = make_idesc(128, 256, kFmtBF16, kFmtBF16, false, false);
+        const uint32_t idesc_qk = make_idesc(128, 128, kFmtBF16, kFmtBF16, false, false);
         int nk = 0;
         ok = mbar_wait(&sh->q_full, 0, abort);
         for (int it = 0; it < T && ok; it++) {
@@ -273,15 +274,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (it >= 2 && !(ok = mbar_wait<true>(&sh->s_free[sb], ((it >> 1) - 1) & 1, abort)))
             break;
           tc_fence_after();
-          for (int k = 0; k < kKPerTile; k++, nk++) {
+          for (int g = 0; g < kKPerTile; g++, nk++) {
             const int slot = nk % kKSlots, u = nk / kKSlots;
             if (!(ok = mbar_wait(&sh->kfull[slot], u & 1, abort))) break;
+            // chunk k = 3g + c: 4 MMAs of 16 dims, B = this CTA's 64 tokens (N = 128)
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++)
-              mma_bf16_pair(tmem + kTmemS + sb * 128,
-                            make_sdesc(q_addr + k * 8192 + kk * 32, 16, 1024),
-                            make_sdesc(k_addr + slot * kKSlot + kk * 32, 16, 1024), idesc_qk,
-                            (k | kk) != 0 ? 1u : 0u);
+            for (int c = 0; c < 3; c++)
+#pragma unroll
+              for (int kk = 0; kk < 4; kk++)
+                mma_bf16_pair(tmem + kTmemS + sb * 64,
+                              make_sdesc(q_addr + (3 * g + c) * 8192 + kk * 32, 16, 1024),
+                              make_sdesc(k_addr + slot * kKSlot + c * 8192 + kk * 32, 16, 1024),
+                              idesc_qk, (g | c | kk) != 0 ? 1u : 0u);
             tc_commit_pair(&sh->kempty[slot], 3);
             last_bar = &sh->kempty[slot];
             last_phase = u & 1;
@@ -294,18 +298,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int it = 0; it < T && ok; it++) {
           if (!(ok = mbar_wait<true>(&sh->p_full, it & 1, abort))) break;
           tc_fence_after();
-          for (int i = 0; i < kVPerTile; i++, nv++) {
-            const int j = i >> 2, pg = i & 3;
+          for (int pg = 0; pg < kVPerTile; pg++, nv++) {
             const int slot = nv % kVSlots, u = nv / kVSlots;
             if (!(ok = mbar_wait(&sh->vfull[slot], u & 1, abort))) break;
+            // PV MMA j takes chunks 2j, 2j+1 of each CTA's slot: its output
+            // columns are dims 256r + 128j + [0, 128) of CTA r's half
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-              // 16 tokens of page pg: P chunk pg, V slot rows 16kk..16kk+15
-              const uint64_t ad = make_sdesc(p_addr + pg * 8192 + kk * 32, 16, 1024);
-              const uint64_t bd = make_sdesc(v_addr + slot * kVSlot + kk * 2048, 8192, 1024);
-              mma_bf16_pair(tmem + kTmemO + j * 128, ad, bd, idesc_pv,
-                            (it > 0 || pg > 0 || kk > 0) ? 1u : 0u);
-            }
+            for (int j = 0; j < 2; j++)
+#pragma unroll
+              for (int kk = 0; kk < 4; kk++) {
+                // 16 tokens of page pg: P chunk pg, V slot rows 16kk..16kk+15
+                const uint64_t ad = make_sdesc(p_addr + pg * 8192 + kk * 32, 16, 1024);
+                const uint64_t bd =
+                    make_sdesc(v_addr + slot * kVSlot + j * 16384 + kk * 2048, 8192, 1024);
+                mma_bf16_pair(tmem + kTmemO + j * 128, ad, bd, idesc_pv,
+                              (it > 0 || pg > 0 || kk > 0) ? 1u : 0u);
+              }
             tc_commit_pair(&sh->vempty[slot], 3);
             last_bar = &sh->vempty[slot];
             last_phase = u & 1;
@@ -334,30 +342,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int it = 0; it < T && ok; it++) {
       const int sb = it & 1;
-      const uint32_t s_addr = tmem + lane_base + kTmemS + sb * 128;
-      const int tok0 = (t_begin + it) * kTile + half * 128;
-      const int nvalid = seqlen - tok0;  // tokens of this half that exist (may be <= 0 or > 128)
+      const uint32_t s_addr = tmem + lane_base + kTmemS + sb * 64;
+      const int tok0 = (t_begin + it) * kTile + half * 64;
+      const int nvalid = seqlen - tok0;  // tokens of this half that exist (may be <= 0 or > 64)
       if (!(ok = warp_wait(&sh->s_full[sb], (it >> 1) & 1, abort))) break;
       tc_fence_after();
-      // this thread's 128 scores into registers; the S buffer is then free
-      float v[128];
+      // this thread's 64 scores into registers; the S buffer is then free
+      float v[64];
 #pragma unroll
-      for (int c = 0; c < 4; c++)
+      for (int c = 0; c < 2; c++)
         tmem_ld32(s_addr + c * 32, *reinterpret_cast<float(*)[32]>(v + 32 * c));
 #pragma unroll
-      for (int c = 0; c < 4; c++) tmem_ld_wait_regs(v + 32 * c);
+      for (int c = 0; c < 2; c++) tmem_ld_wait_regs(v + 32 * c);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(s_free_l[sb]);
-      const bool full = nvalid >= 128;
+      const bool full = nvalid >= 64;
       // pass 1: tile max
       float mx = -INFINITY;
       if (full) {
 #pragma unroll
-        for (int i = 0; i < 128; i++) mx = fmaxf(mx, v[i]);
+        for (int i = 0; i < 64; i++) mx = fmaxf(mx, v[i]);
       } else {
 #pragma unroll
-        for (int i = 0; i < 128; i++)
+        for (int i = 0; i < 64; i++)
           if (i < nvalid) mx = fmaxf(mx, v[i]);
       }
       mx = (mx == -INFINITY) ? -INFINITY : mx * sl2;
@@ -379,9 +387,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // row sum is over the unrounded values
       const uint64_t sc2 = f2_pack(sl2, sl2), nm2 = f2_pack(-m_run, -m_run);
       uint64_t sum2 = f2_pack(0.f, 0.f);
-      uint32_t pk[64];
+      uint32_t pk[32];
 #pragma unroll
-      for (int i = 0; i < 64; i++) {
+      for (int i = 0; i < 32; i++) {
         const int e = 2 * i;
         float x0, x1;
         f2_unpack(f2_fma(f2_pack(v[e], v[e + 1]), sc2, nm2), x0, x1);
@@ -398,12 +406,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const float ps = ps0 + ps1;
       // P(t) reuses the buffer of P(t-1), and O holds tiles < t, once PV(t-1) is done
       if (it >= 1 && !(ok = warp_wait(&sh->p_free, (it - 1) & 1, abort))) break;
-      // 128 tokens = 256 bytes = two 128-byte rows (chunks half*2, half*2+1) of
-      // sixteen-byte units, swizzled
-      uint8_t* pbase = sP + half * 2 * 8192 + hl * 128;
+      // 64 tokens = one 128-byte row (chunk `half`, the page of CTA `half`)
+      // of eight sixteen-byte units, swizzled
+      uint8_t* pbase = sP + half * 8192 + hl * 128;
 #pragma unroll
-      for (int u = 0; u < 16; u++)
-        *reinterpret_cast<uint4*>(pbase + (u >> 3) * 8192 + (((u & 7) ^ (hl & 7)) << 4)) =
+      for (int u = 0; u < 8; u++)
+        *reinterpret_cast<uint4*>(pbase + ((u ^ (hl & 7)) << 4)) =
             make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
       l_run = l_run * alpha + ps;
       if (__any_sync(0xffffffffu, resc)) {
@@ -443,13 +451,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       else
         den = l_tot + ((p.sink && hl < p.cta_heads && isfinite(p.sink[head0 + hl])) ? 1.f : 0.f);
       const float inv = 1.f / fmaxf(den, 1.17549435e-38f);
-      __nv_bfloat16* po = p.out + (b * p.h + head0 + hl) * 512 + 128 * half;
+      __nv_bfloat16* po = p.out + (b * p.h + head0 + hl) * 512 + 256 * half;
 #pragma unroll 1
       for (int c = 0; c < 8; c++) {
         float v[32];
         tmem_ld32(tmem + lane_base + kTmemO + c * 32, v);
         tmem_ld_wait();
-        uint4* dst = reinterpret_cast<uint4*>(po + (c >> 2) * 256 + (c & 3) * 32);
+        uint4* dst = reinterpret_cast<uint4*>(po + (c >> 2) * 128 + (c & 3) * 32);
         if (hl < p.cta_heads) {
 #pragma unroll
           for (int i = 0; i < 4; i++)
@@ -463,13 +471,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float l_tot = l_run + sh->xsum[row ^ 64];
       const int64_t prow = (b * p.splits + split) * p.h + head0 + hl;
-      float* po = p.part_o + prow * 512 + 128 * half;
+      float* po = p.part_o + prow * 512 + 256 * half;
 #pragma unroll 1
       for (int c = 0; c < 8; c++) {
         float v[32];
         tmem_ld32(tmem + lane_base + kTmemO + c * 32, v);
         tmem_ld_wait();
-        float4* dst = reinterpret_cast<float4*>(po + (c >> 2) * 256 + (c & 3) * 32);
+        float4* dst = reinterpret_cast<float4*>(po + (c >> 2) * 128 + (c & 3) * 32);
         if (hl < p.cta_heads) {
 #pragma unroll
           for (int i = 0; i < 8; i++)
@@ -515,6 +523,9 @@ bool decode_attn_sm100_supported(const AttnArgs& a) {
 cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   if (!decode_attn_sm100_supported(a)) return cudaErrorNotSupported;
   if (a.b == 0) return cudaSuccess;
+  // K and V are read through a 4-D view of the cache [pages][64 tokens][9
+  // chunks][64 values], so that one box carries several chunks of a page: the
+  // TMA engine's cost is per box, and 8 KB boxes cap a CTA at ~32 GB/s
   CUtensorMap tq, tk;
   {
     const uint64_t dims[3] = {576, (uint64_t)a.h, (uint64_t)(a.b * a.s)};
@@ -525,10 +536,21 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
       return cudaErrorInvalidValue;
   }
   {
-    const uint64_t dims[3] = {576, 64, (uint64_t)a.num_pages};
-    const uint64_t strides[2] = {1152, 64 * 1152};
-    const uint32_t box[3] = {64, 64, 1};
-    if (!make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.kv, dims, strides, box,
+    // K: the same 4-D view, 3 chunks (24 KB) of one page per box
+    const uint64_t dims[4] = {64, 64, 9, (uint64_t)a.num_pages};
+    const uint64_t strides[3] = {1152, 128, 64 * 1152};
+    const uint32_t box[4] = {64, 64, 3, 1};
+    if (!make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, a.kv, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+  }
+  // V: the same 4-D view, 4 chunks (32 KB) of one page per box
+  CUtensorMap tv;
+  {
+    const uint64_t dims[4] = {64, 64, 9, (uint64_t)a.num_pages};
+    const uint64_t strides[3] = {1152, 128, 64 * 1152};
+    const uint32_t box[4] = {64, 64, 4, 1};
+    if (!make_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, a.kv, dims, strides, box,
                    CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
   }
@@ -554,7 +576,7 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
                                        (int)kSmemBytes);
   if (e != cudaSuccess) return e;
   const int64_t units = a.b * a.s * a.splits * p.hgroups;
-  decode_attn_sm100_kernel<<<(unsigned)(2 * units), kThreads, kSmemBytes, st>>>(tq, tk, p);
+  decode_attn_sm100_kernel<<<(unsigned)(2 * units), kThreads, kSmemBytes, st>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }
 

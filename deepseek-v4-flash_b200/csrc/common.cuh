@@ -203,6 +203,18 @@ __device__ __forceinline__ void tma_load_3d_pair(void* dst, const void* map,
       : "memory");
 }
 
+// 4-D two-CTA form (several 64-value chunks of one row block in one box).
+// No multicast.
+__device__ __forceinline__ void tma_load_4d_pair(void* dst, const void* map,
+                                                 uint32_t bar_cluster_addr, int x, int y, int z,
+                                                 int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar_cluster_addr), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
 // ------------------------------------------------------------ tcgen05
 
 template <int kCtaGroup>
