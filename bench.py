@@ -343,6 +343,10 @@ def main():
                     help="time the causal prefill attention, batch 4 x 4096 x 128 heads")
     ap.add_argument("--sparse-fp8-only", type=int, default=0, metavar="HEADS",
                     help="time the FP8-cache top-k sparse decode (batch 64, 131072 rows) at HEADS")
+    ap.add_argument("--attn-split", default="context", choices=["context", "heads"],
+                    help="N > 1: split the attention of the head-sharded layer by context "
+                         "(each rank streams 1/N of the cache) or by heads (each rank "
+                         "streams all of it)")
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--ctx", type=int, default=4096)
     args = ap.parse_args()
@@ -374,7 +378,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=dev)
     cfg = MLAConfig(n_heads=HEADS, dc=DC, dim=DIM)
-    layer = MLADecodeLayer(cfg, dev, rank=rank, world_size=ws)
+    layer = MLADecodeLayer(cfg, dev, rank=rank, world_size=ws, attn_split=args.attn_split)
+    cp = ws > 1 and args.attn_split == "context"
     layer.random_weights(seed=0)
     cache, table, seqlens = make_paged_cache(BATCH, CTX, PAGE, WIDTH, dev, seed=0)
     positions = seqlens.clone()
@@ -421,17 +426,31 @@ def main():
     # ---- dominant kernel alone: the decode attention, timed on its stream
     L = _lib.lib()
     H = layer.n_local
-    q_abs = torch.randn(BATCH, H, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
-    o_lat = torch.empty(BATCH, H, 512, device=dev, dtype=torch.bfloat16)
-    need = L.qcau_decode_attn_workspace_size(BATCH, H, 512, CTX)
-    wsb = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+    if cp:
+        # this rank's context-parallel attention: all heads over 1/N of every
+        # sequence's tiles, partials for the exchange
+        q_all = torch.randn(ws, BATCH, H, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
+        part_o = torch.empty(ws, BATCH, H, 512, device=dev)
+        part_ml = torch.empty(ws, BATCH, H, 2, device=dev)
 
-    def attn():
-        _lib.check(L.qcau_decode_attn_paged(q_abs.data_ptr(), cache.data_ptr(), table.data_ptr(),
-                                            seqlens.data_ptr(), None, o_lat.data_ptr(), BATCH, H,
-                                            WIDTH, 512, WIDTH, PAGE, table.size(1), cache.size(0),
-                                            CTX, cfg.softmax_scale, wsb.data_ptr(), need,
-                                            _lib.stream_ptr(dev)), "attn")
+        def attn():
+            _lib.check(L.qcau_decode_attn_paged_cp(
+                q_all.data_ptr(), cache.data_ptr(), table.data_ptr(), seqlens.data_ptr(),
+                part_o.data_ptr(), part_ml.data_ptr(), BATCH, HEADS, ws, rank, WIDTH, 512, WIDTH,
+                PAGE, table.size(1), cache.size(0), CTX, cfg.softmax_scale,
+                _lib.stream_ptr(dev)), "attn_cp")
+    else:
+        q_abs = torch.randn(BATCH, H, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
+        o_lat = torch.empty(BATCH, H, 512, device=dev, dtype=torch.bfloat16)
+        need = L.qcau_decode_attn_workspace_size(BATCH, H, 512, CTX)
+        wsb = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+
+        def attn():
+            _lib.check(L.qcau_decode_attn_paged(
+                q_abs.data_ptr(), cache.data_ptr(), table.data_ptr(), seqlens.data_ptr(), None,
+                o_lat.data_ptr(), BATCH, H, WIDTH, 512, WIDTH, PAGE, table.size(1),
+                cache.size(0), CTX, cfg.softmax_scale, wsb.data_ptr(), need,
+                _lib.stream_ptr(dev)), "attn")
 
     for _ in range(3):
         attn()
@@ -446,8 +465,16 @@ def main():
     torch.cuda.synchronize(dev)
     attn_ms = a0.elapsed_time(a1) / n_attn
     cache_bytes = BATCH * CTX * WIDTH * 2
-    attn_bytes = cache_bytes + BATCH * H * (WIDTH + 512) * 2 + table.numel() * 4
-    attn_flops = 2.0 * BATCH * CTX * H * (WIDTH + 512)
+    full_bytes = cache_bytes + BATCH * HEADS * (WIDTH + 512) * 2 + table.numel() * 4
+    if cp:
+        # 1/N of the cache and block table (the ranks' tile ranges are equal
+        # here: 256 tiles per sequence), q of all heads, fp32 partials out
+        attn_bytes = (cache_bytes + table.numel() * 4) // ws + BATCH * HEADS * WIDTH * 2 + \
+            BATCH * HEADS * (512 + 2) * 4
+        attn_flops = 2.0 * BATCH * (CTX // ws) * HEADS * (WIDTH + 512)
+    else:
+        attn_bytes = cache_bytes + BATCH * H * (WIDTH + 512) * 2 + table.numel() * 4
+        attn_flops = 2.0 * BATCH * CTX * H * (WIDTH + 512)
     hbm, tflops, peak_kind = peaks()
     t_bw = attn_bytes / (hbm * 1e9)
     t_tc = attn_flops / (tflops * 1e12)
@@ -458,8 +485,16 @@ def main():
         roof = {"bound": "tensor", "achieved": attn_flops / (attn_ms * 1e-3) / 1e12,
                 "peak": tflops, "unit": "TFLOP/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["traffic"] = traffic_from_profiles()
-    roof["kernel"] = "decode attention (split-KV + combine), per launch"
+    traffic = traffic_from_profiles()
+    if cp:
+        # the one-GPU capture's DRAM bytes per algorithmic byte, applied to this launch
+        roof["traffic"] = traffic * attn_bytes / full_bytes if traffic else None
+        roof["traffic_note"] = "scaled from the 1-GPU full-launch capture by algorithmic bytes"
+        roof["kernel"] = ("context-parallel decode attention: all heads over this rank's 1/N "
+                          "of the tiles, partials out; per launch")
+    else:
+        roof["traffic"] = traffic
+        roof["kernel"] = "decode attention (split-KV + combine), per launch"
     roof["ms_per_launch"] = attn_ms
     roof["peak_source"] = f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured" else peak_kind
     roof["algorithmic_bytes"] = attn_bytes
@@ -503,7 +538,9 @@ def main():
                                    "cache page 64, FP8 block-scaled wq_b/wo, bf16 all-reduce "
                                    "[128,7168]",
                        "global_batch": BATCH, "seq_len": CTX, "heads_per_rank": H,
-                       "parallelism": f"head-shard tp{ws}",
+                       "parallelism": (f"head-shard tp{ws}, attention split by context "
+                                       "(q all-gather, partial all-to-all)" if cp else
+                                       f"head-shard tp{ws}"),
                        "l2": "inputs (4.83 GB cache) larger than L2; no flush"},
             "roofline": roof,
             "e2e": {"value": e2e_val, "unit": "tok/s",

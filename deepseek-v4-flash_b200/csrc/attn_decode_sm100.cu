@@ -107,6 +107,13 @@ struct DecodeParams {
   float scale;
   int qlen;    // query tokens per sequence (1 = decode; > 1 = causal prefill / chunk)
   int direct;  // 1: one split, the epilogue normalises and writes `out`
+  // context-parallel decode over ranks: Q boxes of q_box heads from blocks of
+  // q_hblock heads; splits [split_base, +splits) of splits_total; partials
+  // in blocks of part_hblock heads, [block][rows][splits][part_hblock]
+  int q_hblock, q_box;
+  int split_base, splits_total;
+  int part_hblock;
+  int64_t rows;
 };
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -150,10 +157,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int64_t bs = b / p.qlen;
   const int seqlen = p.seqlens[bs] - (p.qlen - 1 - (int)(b % p.qlen));
   const int ntiles = (seqlen + kTile - 1) / kTile;
-  const int t_begin = (int)((int64_t)ntiles * split / p.splits);
-  const int t_end = (int)((int64_t)ntiles * (split + 1) / p.splits);
+  const int gsplit = p.split_base + split;  // this split among splits_total
+  const int t_begin = (int)((int64_t)ntiles * gsplit / p.splits_total);
+  const int t_end = (int)((int64_t)ntiles * (gsplit + 1) / p.splits_total);
   const int T = t_end - t_begin;
   const int head0 = hg * 2 * p.cta_heads + (int)rank * p.cta_heads;
+  // partial row of (row b, this split, head): block head / part_hblock
+  auto part_row = [&](int head) -> int64_t {
+    const int blk = head / p.part_hblock;
+    return (((int64_t)blk * p.rows + b) * p.splits + split) * p.part_hblock + (head - blk * p.part_hblock);
+  };
 
   if (T <= 0) {  // both CTAs of the pair take this branch together
     if (p.direct) {  // no visible token: the output rows are zero
@@ -163,7 +176,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       return;
     }
     for (int i = threadIdx.x; i < p.cta_heads; i += blockDim.x) {
-      const int64_t prow = (b * p.splits + split) * p.h + head0 + i;
+      const int64_t prow = part_row(head0 + i);
       p.part_ml[prow * 2] = -INFINITY;
       p.part_ml[prow * 2 + 1] = 0.f;
     }
@@ -224,8 +237,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (is_k) {
         if (leader) mbar_arrive_expect_tx(&sh->q_full, 2 * kQBytes);
         const uint32_t q_full_l = mapa_shared(smem_u32(&sh->q_full), 0);
+        // 64 head rows per chunk, in boxes of q_box heads of one block
+        // (rows past the last head are zero-filled padding)
         for (int k = 0; k < 9; k++)
-          tma_load_3d_pair(sQ + k * 8192, &tm_q, q_full_l, 64 * k, head0, (int)b);
+          for (int m = 0; m < 64; m += p.q_box) {
+            const int hd = head0 + m;
+            tma_load_4d_pair(sQ + k * 8192 + m * 128, &tm_q, q_full_l, 64 * k, hd % p.q_hblock,
+                             (int)b, hd / p.q_hblock);
+          }
       }
       int n = 0;
       bool ok = true;
@@ -470,7 +489,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else if (ok) {
       tc_fence_after();
       const float l_tot = l_run + sh->xsum[row ^ 64];
-      const int64_t prow = (b * p.splits + split) * p.h + head0 + hl;
+      const int64_t prow = part_row(head0 + hl);
       float* po = p.part_o + prow * 512 + 256 * half;
 #pragma unroll 1
       for (int c = 0; c < 8; c++) {
@@ -512,7 +531,15 @@ bool is_sm100_device() {
 }  // namespace
 
 bool decode_attn_sm100_supported(const AttnArgs& a) {
-  return a.block_table != nullptr && a.seqlens != nullptr && a.s >= 1 && a.d_qk == 576 &&
+  // head blocks of q: the whole h, or divisors of 64 (8, 16, 32) and
+  // multiples of 64 that divide h (the 1024-byte swizzle atom is 8 rows)
+  const int64_t qhb = a.q_hblock > 0 ? a.q_hblock : a.h;
+  const bool qblocks = qhb == a.h || (a.h % qhb == 0 && (qhb % 64 == 0 || (64 % qhb == 0 && qhb >= 8)));
+  const bool parts = a.part_hblock <= 0 || a.h % a.part_hblock == 0;
+  const bool ranges = a.splits_total <= 0 ||
+                      (a.split_base >= 0 && a.split_base + a.splits <= a.splits_total);
+  return qblocks && parts && ranges && a.block_table != nullptr && a.seqlens != nullptr &&
+         a.s >= 1 && a.d_qk == 576 &&
          a.d_v == 512 && a.d_kv == 576 && a.page_size == 64 &&
          (a.h % 128 == 0 || a.h == 64 || a.h == 32 || a.h == 16) &&
          a.q_row_stride == 576 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 &&
@@ -527,11 +554,16 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   // chunks][64 values], so that one box carries several chunks of a page: the
   // TMA engine's cost is per box, and 8 KB boxes cap a CTA at ~32 GB/s
   CUtensorMap tq, tk;
+  // Q as [blocks][rows][q_hblock][576]: one block of h heads, or the ranks'
+  // all-gathered head blocks (context-parallel decode)
+  const int64_t rows = a.b * a.s;
+  const int64_t qhb = a.q_hblock > 0 ? a.q_hblock : a.h;
+  const int q_box = qhb < 64 ? (int)qhb : 64;
   {
-    const uint64_t dims[3] = {576, (uint64_t)a.h, (uint64_t)(a.b * a.s)};
-    const uint64_t strides[2] = {1152, (uint64_t)a.h * 1152};
-    const uint32_t box[3] = {64, 64, 1};
-    if (!make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.q, dims, strides, box,
+    const uint64_t dims[4] = {576, (uint64_t)qhb, (uint64_t)rows, (uint64_t)(a.h / qhb)};
+    const uint64_t strides[3] = {1152, (uint64_t)qhb * 1152, (uint64_t)(rows * qhb) * 1152};
+    const uint32_t box[4] = {64, (uint32_t)q_box, 1, 1};
+    if (!make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, a.q, dims, strides, box,
                    CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
   }
@@ -562,7 +594,14 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   p.out = reinterpret_cast<__nv_bfloat16*>(a.o);
   p.sink = a.sink;
   p.qlen = (int)a.s;
-  p.direct = a.splits == 1 ? 1 : 0;
+  p.q_hblock = (int)qhb;
+  p.q_box = q_box;
+  p.split_base = a.splits_total > 0 ? a.split_base : 0;
+  p.splits_total = a.splits_total > 0 ? a.splits_total : a.splits;
+  p.part_hblock = a.part_hblock > 0 ? (int)a.part_hblock : (int)a.h;
+  p.rows = rows;
+  // one split and no partial buffers: the epilogue normalises and writes o
+  p.direct = (a.splits == 1 && a.part_o == nullptr) ? 1 : 0;
   p.err = device_error_word();
   p.max_pages = a.max_pages;
   p.num_pages = a.num_pages;

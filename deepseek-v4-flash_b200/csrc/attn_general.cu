@@ -406,7 +406,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1) attn_general_kernel(AttnArgs p
 }
 
 // Merge split-KV partials: M = max m_i, L = sum l_i 2^(m_i-M) + sink term,
-// O = sum acc_i 2^(m_i-M) / L.  One warp per (query, head).
+// O = sum acc_i 2^(m_i-M) / L.  One warp per (query, head).  Partials are
+// [rows][splits][h], or [splits][rows][h] with part_split_major (the ranks'
+// blocks of a context-parallel decode, after their exchange).
 __global__ void attn_combine_kernel(AttnArgs p) {
   const int lane = threadIdx.x & 31;
   const int64_t task = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -414,8 +416,10 @@ __global__ void attn_combine_kernel(AttnArgs p) {
   if (task >= rows * p.h) return;
   const int64_t qrow = task / p.h, hh = task % p.h;
   const int64_t tpos = qrow % p.s;
-  const float* ml = p.part_ml + (qrow * p.splits * p.h + hh) * 2;
-  const int64_t ml_stride = p.h * 2;
+  const int64_t prow0 = p.part_split_major ? qrow * p.h + hh : qrow * p.splits * p.h + hh;
+  const int64_t pstride = p.part_split_major ? rows * p.h : p.h;  // between splits, in rows
+  const float* ml = p.part_ml + prow0 * 2;
+  const int64_t ml_stride = pstride * 2;
   float M = -INFINITY;
   for (int i = 0; i < p.splits; i++) M = fmaxf(M, ml[i * ml_stride]);
   float L = 0.f;
@@ -430,8 +434,8 @@ __global__ void attn_combine_kernel(AttnArgs p) {
     L += (p.sink && isfinite(p.sink[hh])) ? 1.f : 0.f;
   const float inv = 1.f / fmaxf(L, 1.17549435e-38f);
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.o) + (qrow * p.h + hh) * p.d_v;
-  const float* po = p.part_o + (qrow * p.splits * p.h + hh) * p.d_v;
-  const int64_t po_stride = p.h * p.d_v;
+  const float* po = p.part_o + prow0 * p.d_v;
+  const int64_t po_stride = pstride * p.d_v;
   for (int c = lane * 4; c < p.d_v; c += 128) {
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i = 0; i < p.splits; i++) {

@@ -605,39 +605,31 @@ size_t qcau_mla_decode_workspace_size(const qcau_mla_dims* dims) {
   return dims ? mla_ws(dims).total : 0;
 }
 
-int qcau_mla_decode(const qcau_mla_dims* d, const void* q_lora, const void* wq_b,
-                    const void* wq_b_scale, const void* wkv_b_bf16, const void* wo,
-                    const void* wo_scale, const void* cache, const int32_t* block_table,
-                    const int32_t* seqlens, const int32_t* positions, const float* freqs, void* y,
-                    void* workspace, size_t workspace_bytes, void* stream) {
-  QCAU_CHECK_ARG(d != nullptr, "mla_decode: dims is NULL");
-  QCAU_CHECK_ARG(q_lora && wq_b && wq_b_scale && wkv_b_bf16 && wo && wo_scale && cache &&
-                     block_table && seqlens && positions && freqs && y,
-                 "mla_decode: NULL pointer");
-  QCAU_CHECK_ARG(d->batch >= 0 && d->n_heads > 0 && d->dc > 0 && d->dim > 0,
-                 "mla_decode: bad shape");
+// Checks of the layer dimensions shared by the layer entry points.
+static int check_mla_dims(const qcau_mla_dims* d, const char* what) {
+  const std::string w = what;
+  QCAU_CHECK_ARG(d != nullptr, w + ": dims is NULL");
+  QCAU_CHECK_ARG(d->batch >= 0 && d->n_heads > 0 && d->dc > 0 && d->dim > 0, w + ": bad shape");
   QCAU_CHECK_ARG(d->d_nope == 128 && d->d_rope == 64 && d->kv_lora == 512 && d->d_v == 128,
-                 "mla_decode: supported head layout is d_nope 128, d_rope 64, kv_lora 512, d_v 128");
+                 w + ": supported head layout is d_nope 128, d_rope 64, kv_lora 512, d_v 128");
   QCAU_CHECK_ARG(d->dc % 128 == 0 && d->dim % 128 == 0 && (d->n_heads * d->d_v) % 128 == 0 &&
                      (d->n_heads * (d->d_nope + d->d_rope)) % 128 == 0,
-                 "mla_decode: widths must be multiples of 128");
-  QCAU_CHECK_ARG(d->max_seqlen >= 0 && d->max_seqlen <= d->max_pages * d->page_size,
-                 "mla_decode: max_seqlen exceeds the block table");
+                 w + ": widths must be multiples of 128");
   QCAU_CHECK_ARG(d->w_scale_dtype == QCAU_SCALE_F32 || d->w_scale_dtype == QCAU_SCALE_E8M0,
-                 "mla_decode: bad scale dtype");
-  const MlaWs w = mla_ws(d);
-  if (workspace_bytes < w.total || !workspace)
-    return fail(QCAU_ERR_WORKSPACE, "mla_decode: workspace too small (need " +
-                                        std::to_string(w.total) + " bytes)");
-  if (d->batch == 0) return QCAU_OK;
-  cudaStream_t st = to_stream(stream);
-  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+                 w + ": bad scale dtype");
+  return QCAU_OK;
+}
+
+// q side of the layer: q_abs [B, H, kv_lora + d_rope] bf16 at `qabs`.
+static int mla_q_stage(const qcau_mla_dims* d, const void* q_lora, const void* wq_b,
+                       const void* wq_b_scale, const void* wkv_b_bf16, const int32_t* positions,
+                       const float* freqs, void* qabs, uint8_t* ws, const MlaWs& w,
+                       cudaStream_t st) {
   const int64_t B = d->batch, H = d->n_heads;
   const int64_t dq = d->d_nope + d->d_rope;
   const int64_t dabs = d->kv_lora + d->d_rope;
   const int a_e8 = d->act_round_scale ? 1 : 0;
   const int w_e8 = d->w_scale_dtype == QCAU_SCALE_E8M0;
-
   // q = wq_b(act_quant(q_lora))
   QCAU_CHECK_CUDA(launch_act_quant(q_lora, ws + w.xq, ws + w.sq, B, d->dc, 128,
                                    d->act_round_scale, a_e8, 0, st));
@@ -645,27 +637,84 @@ int qcau_mla_decode(const qcau_mla_dims* d, const void* q_lora, const void* wq_b
                                   d->dc, a_e8, w_e8, 0, st));
   // RoPE on q_rope (last 64 of each head) at each sequence's position, in
   // place and into the rope slot of q_abs (q_abs[:, :, kv_lora:])
-  QCAU_CHECK_CUDA(launch_rope_pairs(ws + w.q + d->d_nope * 2, dq, ws + w.qabs + d->kv_lora * 2,
-                                    dabs, freqs, positions, B, 1, H, (int)d->d_rope, 0, 0, st));
+  uint8_t* qa = reinterpret_cast<uint8_t*>(qabs);
+  QCAU_CHECK_CUDA(launch_rope_pairs(ws + w.q + d->d_nope * 2, dq, qa + d->kv_lora * 2, dabs,
+                                    freqs, positions, B, 1, H, (int)d->d_rope, 0, 0, st));
   // q_abs[:, :, :512] = q_nope . W_UK ;  q_abs[:, :, 512:] = q_rope
-  {
-    BmmArgs m{};
-    m.a = ws + w.q;
-    m.a_bstride = dq;
-    m.a_rstride = H * dq;
-    m.b = wkv_b_bf16;
-    m.b_bstride = (d->d_nope + d->d_v) * d->kv_lora;
-    m.b_rstride = d->kv_lora;
-    m.b_kmajor = 0;
-    m.c = ws + w.qabs;
-    m.c_bstride = dabs;
-    m.c_rstride = H * dabs;
-    m.batch = H;
-    m.m = B;
-    m.n = d->kv_lora;
-    m.k = d->d_nope;
-    QCAU_CHECK_CUDA(launch_bf16_bmm(m, st));
-  }
+  BmmArgs m{};
+  m.a = ws + w.q;
+  m.a_bstride = dq;
+  m.a_rstride = H * dq;
+  m.b = wkv_b_bf16;
+  m.b_bstride = (d->d_nope + d->d_v) * d->kv_lora;
+  m.b_rstride = d->kv_lora;
+  m.b_kmajor = 0;
+  m.c = qa;
+  m.c_bstride = dabs;
+  m.c_rstride = H * dabs;
+  m.batch = H;
+  m.m = B;
+  m.n = d->kv_lora;
+  m.k = d->d_nope;
+  QCAU_CHECK_CUDA(launch_bf16_bmm(m, st));
+  return QCAU_OK;
+}
+
+// Output side of the layer: o_lat [B, H, kv_lora] bf16 -> y.
+static int mla_out_stage(const qcau_mla_dims* d, const void* olat, const void* wkv_b_bf16,
+                         const void* wo, const void* wo_scale, void* y, uint8_t* ws,
+                         const MlaWs& w, cudaStream_t st) {
+  const int64_t B = d->batch, H = d->n_heads;
+  const int a_e8 = d->act_round_scale ? 1 : 0;
+  const int w_e8 = d->w_scale_dtype == QCAU_SCALE_E8M0;
+  // o_v = o_lat . W_UV^T
+  BmmArgs m{};
+  m.a = olat;
+  m.a_bstride = d->kv_lora;
+  m.a_rstride = H * d->kv_lora;
+  m.b = reinterpret_cast<const uint8_t*>(wkv_b_bf16) + d->d_nope * d->kv_lora * 2;
+  m.b_bstride = (d->d_nope + d->d_v) * d->kv_lora;
+  m.b_rstride = d->kv_lora;
+  m.b_kmajor = 1;
+  m.c = ws + w.ov;
+  m.c_bstride = d->d_v;
+  m.c_rstride = H * d->d_v;
+  m.batch = H;
+  m.m = B;
+  m.n = d->d_v;
+  m.k = d->kv_lora;
+  QCAU_CHECK_CUDA(launch_bf16_bmm(m, st));
+  // y = wo(act_quant(o_v))   (row-parallel partial; the caller all-reduces)
+  QCAU_CHECK_CUDA(launch_act_quant(ws + w.ov, ws + w.xo, ws + w.so, B, H * d->d_v, 128,
+                                   d->act_round_scale, a_e8, 0, st));
+  QCAU_CHECK_CUDA(launch_fp8_gemm(ws + w.xo, ws + w.so, wo, wo_scale, y, B, d->dim, H * d->d_v,
+                                  a_e8, w_e8, d->out_dtype == QCAU_OUT_F32, st));
+  return QCAU_OK;
+}
+
+int qcau_mla_decode(const qcau_mla_dims* d, const void* q_lora, const void* wq_b,
+                    const void* wq_b_scale, const void* wkv_b_bf16, const void* wo,
+                    const void* wo_scale, const void* cache, const int32_t* block_table,
+                    const int32_t* seqlens, const int32_t* positions, const float* freqs, void* y,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_mla_dims(d, "mla_decode");
+  if (rc) return rc;
+  QCAU_CHECK_ARG(q_lora && wq_b && wq_b_scale && wkv_b_bf16 && wo && wo_scale && cache &&
+                     block_table && seqlens && positions && freqs && y,
+                 "mla_decode: NULL pointer");
+  QCAU_CHECK_ARG(d->max_seqlen >= 0 && d->max_seqlen <= d->max_pages * d->page_size,
+                 "mla_decode: max_seqlen exceeds the block table");
+  const MlaWs w = mla_ws(d);
+  if (workspace_bytes < w.total || !workspace)
+    return fail(QCAU_ERR_WORKSPACE, "mla_decode: workspace too small (need " +
+                                        std::to_string(w.total) + " bytes)");
+  if (d->batch == 0) return QCAU_OK;
+  cudaStream_t st = to_stream(stream);
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  const int64_t dabs = d->kv_lora + d->d_rope;
+  rc = mla_q_stage(d, q_lora, wq_b, wq_b_scale, wkv_b_bf16, positions, freqs, ws + w.qabs, ws, w,
+                   st);
+  if (rc) return rc;
   // o_lat = attention over the paged latent cache (V = first 512 of each row)
   {
     AttnArgs a{};
@@ -676,39 +725,109 @@ int qcau_mla_decode(const qcau_mla_dims* d, const void* q_lora, const void* wq_b
     a.seqlens = seqlens;
     a.sink = nullptr;
     a.o = ws + w.olat;
-    a.b = B; a.s = 1; a.h = H; a.d_qk = dabs; a.d_v = d->kv_lora; a.d_kv = dabs;
+    a.b = d->batch; a.s = 1; a.h = d->n_heads; a.d_qk = dabs; a.d_v = d->kv_lora; a.d_kv = dabs;
     a.page_size = d->page_size;
     a.max_pages = d->max_pages;
     a.num_pages = d->num_pages;
     a.max_len = d->max_seqlen;
     a.scale = d->softmax_scale;
-    int rc = run_decode_attn(a, ws + w.attn, st);
+    rc = run_decode_attn(a, ws + w.attn, st);
     if (rc) return rc;
   }
-  // o_v = o_lat . W_UV^T
-  {
-    BmmArgs m{};
-    m.a = ws + w.olat;
-    m.a_bstride = d->kv_lora;
-    m.a_rstride = H * d->kv_lora;
-    m.b = reinterpret_cast<const uint8_t*>(wkv_b_bf16) + d->d_nope * d->kv_lora * 2;
-    m.b_bstride = (d->d_nope + d->d_v) * d->kv_lora;
-    m.b_rstride = d->kv_lora;
-    m.b_kmajor = 1;
-    m.c = ws + w.ov;
-    m.c_bstride = d->d_v;
-    m.c_rstride = H * d->d_v;
-    m.batch = H;
-    m.m = B;
-    m.n = d->d_v;
-    m.k = d->kv_lora;
-    QCAU_CHECK_CUDA(launch_bf16_bmm(m, st));
-  }
-  // y = wo(act_quant(o_v))   (row-parallel partial; the caller all-reduces)
-  QCAU_CHECK_CUDA(launch_act_quant(ws + w.ov, ws + w.xo, ws + w.so, B, H * d->d_v, 128,
-                                   d->act_round_scale, a_e8, 0, st));
-  QCAU_CHECK_CUDA(launch_fp8_gemm(ws + w.xo, ws + w.so, wo, wo_scale, y, B, d->dim, H * d->d_v,
-                                  a_e8, w_e8, d->out_dtype == QCAU_OUT_F32, st));
+  return mla_out_stage(d, ws + w.olat, wkv_b_bf16, wo, wo_scale, y, ws, w, st);
+}
+
+int qcau_mla_decode_q(const qcau_mla_dims* d, const void* q_lora, const void* wq_b,
+                      const void* wq_b_scale, const void* wkv_b_bf16, const int32_t* positions,
+                      const float* freqs, void* q_abs, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  int rc = check_mla_dims(d, "mla_decode_q");
+  if (rc) return rc;
+  QCAU_CHECK_ARG(q_lora && wq_b && wq_b_scale && wkv_b_bf16 && positions && freqs && q_abs,
+                 "mla_decode_q: NULL pointer");
+  const MlaWs w = mla_ws(d);
+  if (workspace_bytes < w.total || !workspace)
+    return fail(QCAU_ERR_WORKSPACE, "mla_decode_q: workspace too small (need " +
+                                        std::to_string(w.total) + " bytes)");
+  if (d->batch == 0) return QCAU_OK;
+  return mla_q_stage(d, q_lora, wq_b, wq_b_scale, wkv_b_bf16, positions, freqs, q_abs,
+                     reinterpret_cast<uint8_t*>(workspace), w, to_stream(stream));
+}
+
+int qcau_mla_decode_out(const qcau_mla_dims* d, const void* o_lat, const void* wkv_b_bf16,
+                        const void* wo, const void* wo_scale, void* y, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  int rc = check_mla_dims(d, "mla_decode_out");
+  if (rc) return rc;
+  QCAU_CHECK_ARG(o_lat && wkv_b_bf16 && wo && wo_scale && y, "mla_decode_out: NULL pointer");
+  const MlaWs w = mla_ws(d);
+  if (workspace_bytes < w.total || !workspace)
+    return fail(QCAU_ERR_WORKSPACE, "mla_decode_out: workspace too small (need " +
+                                        std::to_string(w.total) + " bytes)");
+  if (d->batch == 0) return QCAU_OK;
+  return mla_out_stage(d, o_lat, wkv_b_bf16, wo, wo_scale, y,
+                       reinterpret_cast<uint8_t*>(workspace), w, to_stream(stream));
+}
+
+int qcau_decode_attn_paged_cp(const void* q_all, const void* cache, const int32_t* block_table,
+                              const int32_t* seqlens, float* part_o, float* part_ml, int64_t b,
+                              int64_t h, int64_t n_ranks, int64_t rank, int64_t d_qk, int64_t d_v,
+                              int64_t d_kv, int64_t page_size, int64_t max_pages,
+                              int64_t num_pages, int64_t max_seqlen, float softmax_scale,
+                              void* stream) {
+  QCAU_CHECK_ARG(q_all && cache && block_table && seqlens && part_o && part_ml,
+                 "decode_attn_paged_cp: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && h > 0 && page_size > 0 && max_pages > 0 && num_pages > 0,
+                 "decode_attn_paged_cp: bad shape");
+  QCAU_CHECK_ARG(n_ranks >= 1 && rank >= 0 && rank < n_ranks && h % n_ranks == 0,
+                 "decode_attn_paged_cp: rank out of range or heads not divisible by ranks");
+  QCAU_CHECK_ARG(max_seqlen >= 0 && max_seqlen <= max_pages * page_size,
+                 "decode_attn_paged_cp: max_seqlen exceeds the block table");
+  int rc = check_attn_widths(d_qk, d_v, d_kv, "decode_attn_paged_cp");
+  if (rc) return rc;
+  AttnArgs a{};
+  a.q = q_all;
+  a.q_row_stride = d_qk;
+  a.kv = cache;
+  a.block_table = block_table;
+  a.seqlens = seqlens;
+  a.b = b; a.s = 1; a.h = h; a.d_qk = d_qk; a.d_v = d_v; a.d_kv = d_kv;
+  a.page_size = page_size;
+  a.max_pages = max_pages;
+  a.num_pages = num_pages;
+  a.max_len = max_seqlen;
+  a.scale = softmax_scale;
+  a.splits = 1;
+  a.split_base = (int)rank;
+  a.splits_total = (int)n_ranks;
+  a.q_hblock = h / n_ranks;
+  a.part_hblock = h / n_ranks;
+  a.part_o = part_o;
+  a.part_ml = part_ml;
+  if (!decode_attn_sm100_supported(a))
+    return fail(QCAU_ERR_UNSUPPORTED,
+                "decode_attn_paged_cp: needs the sm_100a pair kernel (d_qk 576, d_v 512, page 64, "
+                "h a multiple of 128, h / n_ranks a multiple of 64 or 8, 16 or 32)");
+  if (b == 0) return QCAU_OK;
+  QCAU_CHECK_CUDA(launch_decode_attn_sm100(a, to_stream(stream)));
+  return QCAU_OK;
+}
+
+int qcau_attn_combine_ranks(const float* part_o, const float* part_ml, const float* attn_sink,
+                            void* o, int64_t b, int64_t h_local, int64_t n_ranks, int64_t d_v,
+                            void* stream) {
+  QCAU_CHECK_ARG(part_o && part_ml && o, "attn_combine_ranks: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && h_local > 0 && n_ranks >= 1 && d_v > 0 && d_v % 128 == 0,
+                 "attn_combine_ranks: bad shape");
+  AttnArgs a{};
+  a.part_o = const_cast<float*>(part_o);
+  a.part_ml = const_cast<float*>(part_ml);
+  a.sink = attn_sink;
+  a.o = o;
+  a.b = b; a.s = 1; a.h = h_local; a.d_v = d_v;
+  a.splits = (int)n_ranks;
+  a.part_split_major = 1;
+  QCAU_CHECK_CUDA(launch_attn_combine(a, to_stream(stream)));
   return QCAU_OK;
 }
 

@@ -87,6 +87,18 @@ struct AttnArgs {
   const uint8_t* kv_fp8;
   const float* kv_scale;
   const void* kv_rope;
+  // Context-parallel decode over ranks (tcgen05 pair kernel; 0 = off):
+  //   q is [h / q_hblock][rows][q_hblock][d_qk] (the ranks' all-gathered
+  //   head blocks) when q_hblock > 0;
+  //   this launch runs splits [split_base, split_base + splits) of
+  //   splits_total over each row's tiles when splits_total > 0;
+  //   partials go to [h / part_hblock][rows][splits][part_hblock] (one
+  //   block per destination rank) when part_hblock > 0.
+  int64_t q_hblock;
+  int split_base, splits_total;
+  int64_t part_hblock;
+  // combine: partials are [splits][rows][h] (1) instead of [rows][splits][h]
+  int part_split_major;
 };
 
 // General split-KV kernel, mma.sync 16-head tiles (attn_general.cu).

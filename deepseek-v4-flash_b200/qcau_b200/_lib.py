@@ -79,6 +79,13 @@ SIGNATURES = {
     "qcau_mla_decode_workspace_size": ([ctypes.POINTER(MlaDims)], _SZ),
     "qcau_mla_decode": ([ctypes.POINTER(MlaDims), _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                          _P, _P, _SZ, _P], ctypes.c_int),
+    "qcau_mla_decode_q": ([ctypes.POINTER(MlaDims), _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P],
+                          ctypes.c_int),
+    "qcau_decode_attn_paged_cp": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
+                                   _I64, _I64, _I64, _I64, _I64, _F, _P], ctypes.c_int),
+    "qcau_attn_combine_ranks": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P], ctypes.c_int),
+    "qcau_mla_decode_out": ([ctypes.POINTER(MlaDims), _P, _P, _P, _P, _P, _P, _SZ, _P],
+                            ctypes.c_int),
 }
 
 _lib = None

@@ -14,7 +14,17 @@ Heads are sharded like the reference's tensor parallelism: wq_b / wkv_b are
 column-parallel (this rank's heads, ColumnParallelLinear model.py:155-163),
 wo is row-parallel with an all-reduce of the partial outputs
 (RowParallelLinear model.py:166-180).  The latent cache is shared by all heads
-(MQA), so every rank reads all of it.
+(MQA).  Two ways to run the attention of N ranks:
+
+  attn_split="heads"    each rank attends with its own heads over the whole
+                        cache: every rank streams all of it, so the step time
+                        barely falls with N;
+  attn_split="context"  the ranks all-gather their absorbed queries, each
+                        attends with all heads over 1/N of every sequence's
+                        tiles, and an all-to-all brings each rank the
+                        partial softmax states of its heads, which it merges
+                        before the v-up.  Each rank streams 1/N of the cache
+                        and exchanges b*h/N*(N-1)*(512+2)*4 bytes.
 
 The reference's V4 attention has no wkv_b; this layer serves the absorbed-MLA
 decode configuration (kv_lora 512 + rope 64 cache rows, d_nope 128, d_v 128).
@@ -100,9 +110,13 @@ class MLADecodeLayer:
     """Holds this rank's weight shards and runs one decode step per call."""
 
     def __init__(self, cfg: MLAConfig, device, rank: int = 0, world_size: int = 1,
-                 process_group=None):
+                 process_group=None, attn_split: str = "context"):
         if cfg.n_heads % world_size:
             raise ValueError("n_heads must be divisible by the number of ranks")
+        if attn_split not in ("heads", "context"):
+            raise ValueError("attn_split must be 'heads' or 'context'")
+        self.attn_split = attn_split
+        self._cp = None
         self.cfg = cfg
         self.device = torch.device(device)
         self.rank, self.world_size = rank, world_size
@@ -212,10 +226,101 @@ class MLADecodeLayer:
     def forward(self, q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen,
                 y: Optional[torch.Tensor] = None) -> torch.Tensor:
         """y [batch, dim] bf16, summed over the head shards."""
+        if self.world_size > 1 and self.attn_split == "context":
+            return self.forward_context(q_lora, cache, block_table, seqlens, positions, freqs,
+                                        max_seqlen, y)
         y = self.forward_local(q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen, y)
         if self.world_size > 1:
             dist.all_reduce(y, group=self.group)
         return y
+
+    def _cp_buffers(self, B: int):
+        """Stage buffers of the context-parallel step, kept across steps."""
+        if self._cp is None or self._cp["B"] != B:
+            N, Hl, c, dev = self.world_size, self.n_local, self.cfg, self.device
+            w = c.kv_lora + c.d_rope
+            f32, bf16 = torch.float32, torch.bfloat16
+            self._cp = {
+                "B": B,
+                "q_local": torch.empty(B, Hl, w, device=dev, dtype=bf16),
+                "q_all": torch.empty(N, B, Hl, w, device=dev, dtype=bf16),
+                "part_o": torch.empty(N, B, Hl, c.kv_lora, device=dev, dtype=f32),
+                "part_ml": torch.empty(N, B, Hl, 2, device=dev, dtype=f32),
+                "recv_o": torch.empty(N, B, Hl, c.kv_lora, device=dev, dtype=f32),
+                "recv_ml": torch.empty(N, B, Hl, 2, device=dev, dtype=f32),
+                "o_lat": torch.empty(B, Hl, c.kv_lora, device=dev, dtype=bf16),
+            }
+        return self._cp
+
+    def forward_context(self, q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen,
+                        y: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y [batch, dim] bf16 summed over the ranks, the attention split by context.
+
+        With one rank the collectives are identities and the stages run as
+        one rank of one.
+        """
+        N = self.world_size
+        B = q_lora.size(0)
+        buf = self._cp_buffers(B)
+        if y is None:
+            y = torch.empty(B, self.cfg.dim, device=self.device, dtype=torch.bfloat16)
+        d = self.dims(B, block_table.size(1), cache.size(0), max_seqlen, freqs.size(0))
+        self._q_stage(d, q_lora, positions, freqs, buf["q_local"])
+        q_all = buf["q_local"]
+        if N > 1:   # [N, B, h/N, 576]: block j = the heads of rank j
+            dist.all_gather_into_tensor(buf["q_all"].view(-1, *buf["q_local"].shape[1:]),
+                                        buf["q_local"], group=self.group)
+            q_all = buf["q_all"]
+        self._attn_stage(q_all, cache, block_table, seqlens, max_seqlen, buf["part_o"],
+                         buf["part_ml"])
+        recv_o, recv_ml = buf["part_o"], buf["part_ml"]
+        if N > 1:   # block j of rank i goes to rank j, which stacks them by source
+            dist.all_to_all_single(buf["recv_o"], buf["part_o"], group=self.group)
+            dist.all_to_all_single(buf["recv_ml"], buf["part_ml"], group=self.group)
+            recv_o, recv_ml = buf["recv_o"], buf["recv_ml"]
+        self._combine_stage(recv_o, recv_ml, buf["o_lat"])
+        self._out_stage(d, buf["o_lat"], y)
+        if N > 1:
+            dist.all_reduce(y, group=self.group)
+        return y
+
+    # ------------------------------------------------------------ stages
+    def _q_stage(self, d, q_lora, positions, freqs, q_abs):
+        """q_abs [B, h/N, 576] of this rank's heads."""
+        ws = self.workspace(d)
+        check(lib().qcau_mla_decode_q(d, q_lora.data_ptr(), self.wq_b.data_ptr(),
+                                      self.wq_b_scale.data_ptr(), self.wkv_b_bf16.data_ptr(),
+                                      positions.data_ptr(), freqs.data_ptr(), q_abs.data_ptr(),
+                                      ws.data_ptr(), ws.numel(), stream_ptr(self.device)),
+              "mla_decode_q")
+
+    def _attn_stage(self, q_all, cache, block_table, seqlens, max_seqlen, part_o, part_ml):
+        """Partials [N, B, h/N, ...] of all heads over this rank's share of the tiles."""
+        c = self.cfg
+        w = c.kv_lora + c.d_rope
+        check(lib().qcau_decode_attn_paged_cp(q_all.data_ptr(), cache.data_ptr(),
+                                              block_table.data_ptr(), seqlens.data_ptr(),
+                                              part_o.data_ptr(), part_ml.data_ptr(),
+                                              q_all.size(-3), c.n_heads, self.world_size,
+                                              self.rank, w, c.kv_lora, w, c.page_size,
+                                              block_table.size(1), cache.size(0), max_seqlen,
+                                              c.softmax_scale, stream_ptr(self.device)),
+              "decode_attn_paged_cp")
+
+    def _combine_stage(self, recv_o, recv_ml, o_lat):
+        """o_lat [B, h/N, 512] bf16 from the N partials of this rank's heads."""
+        check(lib().qcau_attn_combine_ranks(recv_o.data_ptr(), recv_ml.data_ptr(), None,
+                                            o_lat.data_ptr(), o_lat.size(0), self.n_local,
+                                            self.world_size, self.cfg.kv_lora,
+                                            stream_ptr(self.device)), "attn_combine_ranks")
+
+    def _out_stage(self, d, o_lat, y):
+        """y [B, dim], this rank's row-parallel partial."""
+        ws = self.workspace(d)
+        check(lib().qcau_mla_decode_out(d, o_lat.data_ptr(), self.wkv_b_bf16.data_ptr(),
+                                        self.wo.data_ptr(), self.wo_scale.data_ptr(),
+                                        y.data_ptr(), ws.data_ptr(), ws.numel(),
+                                        stream_ptr(self.device)), "mla_decode_out")
 
 
 def make_paged_cache(batch: int, ctx: int, page_size: int, width: int, device, seed: int = 0,

@@ -302,6 +302,47 @@ int qcau_mla_decode(const qcau_mla_dims* dims, const void* q_lora,
                     const int32_t* positions, const float* freqs, void* y,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------
+ * The layer in stages, for head-sharded ranks that split the attention by
+ * context instead of each streaming the whole shared cache (no reference
+ * counterpart: its ranks run Attention.forward on their heads, model.py:
+ * 484-543, and meet only in RowParallelLinear's all-reduce, model.py:166-180).
+ * With N ranks, rank r owning heads [r*h/N, (r+1)*h/N):
+ *   mla_decode_q        q_abs [b, h/N, kv_lora+d_rope] of its heads
+ *   (caller)            all-gather -> q_all [N, b, h/N, 576]
+ *   decode_attn_paged_cp   all h heads over tiles [ntiles*r/N, ntiles*(r+1)/N)
+ *                       of every sequence (ntiles = ceil(seqlen/128)) ->
+ *                       partials [N, b, h/N, 512] and [N, b, h/N, 2] fp32,
+ *                       block j holding the heads of rank j
+ *   (caller)            all-to-all of the blocks -> [N, b, h/N, ...] by source
+ *   attn_combine_ranks  o_lat [b, h/N, 512] bf16 (sink optional)
+ *   mla_decode_out      y [b, dim] (row-parallel partial)
+ *   (caller)            all-reduce of y
+ * Every stage takes qcau_mla_dims with n_heads = h/N (the rank's heads) and
+ * the workspace of qcau_mla_decode_workspace_size.  The partials hold
+ * unnormalised sums with (max in log2 units, sum) as the split-KV path does;
+ * decode_attn_paged_cp needs the sm_100a pair kernel (d_qk 576, d_v 512,
+ * page 64, h a multiple of 128, h/N a multiple of 64 or one of 8, 16, 32)
+ * and returns QCAU_ERR_UNSUPPORTED otherwise.
+ * ---------------------------------------------------------------------- */
+int qcau_mla_decode_q(const qcau_mla_dims* dims, const void* q_lora, const void* wq_b,
+                      const void* wq_b_scale, const void* wkv_b_bf16,
+                      const int32_t* positions, const float* freqs, void* q_abs,
+                      void* workspace, size_t workspace_bytes, void* stream);
+int qcau_decode_attn_paged_cp(const void* q_all, const void* cache,
+                              const int32_t* block_table, const int32_t* seqlens,
+                              float* part_o, float* part_ml, int64_t b, int64_t h,
+                              int64_t n_ranks, int64_t rank, int64_t d_qk, int64_t d_v,
+                              int64_t d_kv, int64_t page_size, int64_t max_pages,
+                              int64_t num_pages, int64_t max_seqlen, float softmax_scale,
+                              void* stream);
+int qcau_attn_combine_ranks(const float* part_o, const float* part_ml, const float* attn_sink,
+                            void* o, int64_t b, int64_t h_local, int64_t n_ranks, int64_t d_v,
+                            void* stream);
+int qcau_mla_decode_out(const qcau_mla_dims* dims, const void* o_lat, const void* wkv_b_bf16,
+                        const void* wo, const void* wo_scale, void* y, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
