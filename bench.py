@@ -347,6 +347,9 @@ def main():
                     help="N > 1: split the attention of the head-sharded layer by context "
                          "(each rank streams 1/N of the cache) or by heads (each rank "
                          "streams all of it)")
+    ap.add_argument("--exchange", default="nccl", choices=["nccl", "p2p"],
+                    help="context split: partial states exchanged by an NCCL all-to-all, or "
+                         "stored by the attention kernel into the owning rank's memory")
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--ctx", type=int, default=4096)
     args = ap.parse_args()
@@ -378,7 +381,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=dev)
     cfg = MLAConfig(n_heads=HEADS, dc=DC, dim=DIM)
-    layer = MLADecodeLayer(cfg, dev, rank=rank, world_size=ws, attn_split=args.attn_split)
+    layer = MLADecodeLayer(cfg, dev, rank=rank, world_size=ws, attn_split=args.attn_split,
+                           exchange=args.exchange)
     cp = ws > 1 and args.attn_split == "context"
     layer.random_weights(seed=0)
     cache, table, seqlens = make_paged_cache(BATCH, CTX, PAGE, WIDTH, dev, seed=0)
@@ -539,8 +543,8 @@ def main():
                                    "[128,7168]",
                        "global_batch": BATCH, "seq_len": CTX, "heads_per_rank": H,
                        "parallelism": (f"head-shard tp{ws}, attention split by context "
-                                       "(q all-gather, partial all-to-all)" if cp else
-                                       f"head-shard tp{ws}"),
+                                       f"(q all-gather, partial exchange: {args.exchange})"
+                                       if cp else f"head-shard tp{ws}"),
                        "l2": "inputs (4.83 GB cache) larger than L2; no flush"},
             "roofline": roof,
             "e2e": {"value": e2e_val, "unit": "tok/s",
@@ -558,6 +562,7 @@ def main():
         print(json.dumps(line))
     if ws > 1:
         dist.barrier()
+        layer.close()   # peer receive buffers of the p2p exchange, if any (collective)
         dist.destroy_process_group()
 
 

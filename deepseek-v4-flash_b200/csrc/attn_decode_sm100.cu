@@ -93,11 +93,11 @@ constexpr size_t kSmemBytes = 1024 + kQBytes + kPBytes + (size_t)kKSlots * kKSlo
                               (size_t)kVSlots * kVSlot + sizeof(DecodeShared);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
+constexpr int kMaxBlocks = 16;  // destination head blocks of the partials
+
 struct DecodeParams {
   const int32_t* table;
   const int32_t* seqlens;
-  float* part_o;
-  float* part_ml;
   __nv_bfloat16* out;  // direct mode (one split): final output [rows, h, 512]
   const float* sink;   // direct mode: attention sink [h] or nullptr
   int* err;
@@ -108,13 +108,41 @@ struct DecodeParams {
   int qlen;    // query tokens per sequence (1 = decode; > 1 = causal prefill / chunk)
   int direct;  // 1: one split, the epilogue normalises and writes `out`
   // context-parallel decode over ranks: Q boxes of q_box heads from blocks of
-  // q_hblock heads; splits [split_base, +splits) of splits_total; partials
-  // in blocks of part_hblock heads, [block][rows][splits][part_hblock]
+  // q_hblock heads; splits [split_base, +splits) of splits_total; the
+  // partials of head block j (part_hblock heads) go to blk_o[j] / blk_ml[j],
+  // [rows][splits][part_hblock] each: local blocks, or the receive slots of
+  // the ranks that own the heads (peer memory over NVLink)
   int q_hblock, q_box;
   int split_base, splits_total;
   int part_hblock;
-  int64_t rows;
+  int nblk;
+  float* blk_o[kMaxBlocks];
+  float* blk_ml[kMaxBlocks];
+  // completion: when `counter` is set, the last CTA to finish raises
+  // flag[j] = epoch (release, system scope) for every block destination j
+  uint32_t* flag[kMaxBlocks];
+  unsigned int* counter;
+  uint32_t epoch;
 };
+
+// Called by thread 0 of each CTA once all the CTA's partial stores are
+// ordered before it (a CTA or cluster barrier): counts the CTA, and the last
+// one of the grid publishes `epoch` to every destination's flag.
+__device__ __forceinline__ void signal_done(const DecodeParams& p) {
+  if (p.counter == nullptr) return;
+  __threadfence_system();
+  unsigned int prev;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+               : "=r"(prev)
+               : "l"(p.counter)
+               : "memory");
+  if (prev == gridDim.x - 1) {
+    __threadfence_system();
+    for (int j = 0; j < p.nblk; j++)
+      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.flag[j]), "r"(p.epoch) : "memory");
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p.counter), "r"(0u) : "memory");
+  }
+}
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -162,10 +190,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int t_end = (int)((int64_t)ntiles * (gsplit + 1) / p.splits_total);
   const int T = t_end - t_begin;
   const int head0 = hg * 2 * p.cta_heads + (int)rank * p.cta_heads;
-  // partial row of (row b, this split, head): block head / part_hblock
-  auto part_row = [&](int head) -> int64_t {
-    const int blk = head / p.part_hblock;
-    return (((int64_t)blk * p.rows + b) * p.splits + split) * p.part_hblock + (head - blk * p.part_hblock);
+  // partial row of (row b, this split, head) in its head block's destination
+  auto part_row = [&](int head, int& blk) -> int64_t {
+    blk = head / p.part_hblock;
+    return ((int64_t)b * p.splits + split) * p.part_hblock + (head - blk * p.part_hblock);
   };
 
   if (T <= 0) {  // both CTAs of the pair take this branch together
@@ -176,10 +204,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       return;
     }
     for (int i = threadIdx.x; i < p.cta_heads; i += blockDim.x) {
-      const int64_t prow = part_row(head0 + i);
-      p.part_ml[prow * 2] = -INFINITY;
-      p.part_ml[prow * 2 + 1] = 0.f;
+      int blk;
+      const int64_t prow = part_row(head0 + i, blk);
+      p.blk_ml[blk][prow * 2] = -INFINITY;
+      p.blk_ml[blk][prow * 2 + 1] = 0.f;
     }
+    __syncthreads();
+    if (threadIdx.x == 0) signal_done(p);
     return;
   }
 
@@ -489,8 +520,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else if (ok) {
       tc_fence_after();
       const float l_tot = l_run + sh->xsum[row ^ 64];
-      const int64_t prow = part_row(head0 + hl);
-      float* po = p.part_o + prow * 512 + 256 * half;
+      int blk = 0;
+      const int64_t prow = hl < p.cta_heads ? part_row(head0 + hl, blk) : 0;
+      float* po = p.blk_o[blk] + prow * 512 + 256 * half;
 #pragma unroll 1
       for (int c = 0; c < 8; c++) {
         float v[32];
@@ -504,8 +536,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
       if (half == 0 && hl < p.cta_heads) {
-        p.part_ml[prow * 2] = m_run;
-        p.part_ml[prow * 2 + 1] = l_tot;
+        p.blk_ml[blk][prow * 2] = m_run;
+        p.blk_ml[blk][prow * 2 + 1] = l_tot;
       }
     }
   }
@@ -518,6 +550,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tmem_dealloc<2>(tmem, kTmemCols);
   }
   if (threadIdx.x == 0 && *abort) raise_dev_error(p.err, QCAU_DEVERR_TIMEOUT);
+  if (threadIdx.x == 0) signal_done(p);  // after the cluster barrier: both CTAs' stores
 }
 
 bool is_sm100_device() {
@@ -535,7 +568,9 @@ bool decode_attn_sm100_supported(const AttnArgs& a) {
   // multiples of 64 that divide h (the 1024-byte swizzle atom is 8 rows)
   const int64_t qhb = a.q_hblock > 0 ? a.q_hblock : a.h;
   const bool qblocks = qhb == a.h || (a.h % qhb == 0 && (qhb % 64 == 0 || (64 % qhb == 0 && qhb >= 8)));
-  const bool parts = a.part_hblock <= 0 || a.h % a.part_hblock == 0;
+  const bool parts = (a.part_hblock <= 0 || a.h % a.part_hblock == 0) &&
+                     a.h / (a.part_hblock > 0 ? a.part_hblock : a.h) <= kMaxBlocks &&
+                     (!a.peer || a.done_counter != nullptr);
   const bool ranges = a.splits_total <= 0 ||
                       (a.split_base >= 0 && a.split_base + a.splits <= a.splits_total);
   return qblocks && parts && ranges && a.block_table != nullptr && a.seqlens != nullptr &&
@@ -589,8 +624,6 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   DecodeParams p;
   p.table = a.block_table;
   p.seqlens = a.seqlens;
-  p.part_o = a.part_o;
-  p.part_ml = a.part_ml;
   p.out = reinterpret_cast<__nv_bfloat16*>(a.o);
   p.sink = a.sink;
   p.qlen = (int)a.s;
@@ -599,9 +632,27 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   p.split_base = a.splits_total > 0 ? a.split_base : 0;
   p.splits_total = a.splits_total > 0 ? a.splits_total : a.splits;
   p.part_hblock = a.part_hblock > 0 ? (int)a.part_hblock : (int)a.h;
-  p.rows = rows;
+  p.nblk = (int)(a.h / p.part_hblock);
+  for (int j = 0; j < kMaxBlocks; j++) {
+    p.blk_o[j] = nullptr;
+    p.blk_ml[j] = nullptr;
+    p.flag[j] = nullptr;
+  }
+  const int64_t blk_rows = rows * a.splits * p.part_hblock;
+  for (int j = 0; j < p.nblk; j++) {
+    if (a.peer) {  // receive slots of the ranks owning each block
+      p.blk_o[j] = a.peer_o[j];
+      p.blk_ml[j] = a.peer_ml[j];
+      p.flag[j] = a.peer_flag[j];
+    } else if (a.part_o) {
+      p.blk_o[j] = a.part_o + j * blk_rows * 512;
+      p.blk_ml[j] = a.part_ml + j * blk_rows * 2;
+    }
+  }
+  p.counter = a.peer ? a.done_counter : nullptr;
+  p.epoch = a.epoch;
   // one split and no partial buffers: the epilogue normalises and writes o
-  p.direct = (a.splits == 1 && a.part_o == nullptr) ? 1 : 0;
+  p.direct = (a.splits == 1 && a.part_o == nullptr && !a.peer) ? 1 : 0;
   p.err = device_error_word();
   p.max_pages = a.max_pages;
   p.num_pages = a.num_pages;

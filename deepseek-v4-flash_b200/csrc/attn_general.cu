@@ -484,6 +484,31 @@ cudaError_t launch_attn_general(const AttnArgs& p, cudaStream_t st) {
   return cudaErrorNotSupported;
 }
 
+// One thread per flag: spin (bounded) until flags[i] >= epoch, acquiring at
+// system scope what the peer that raised it wrote before its release.
+__global__ void wait_flags_kernel(const uint32_t* flags, int n, uint32_t epoch, int* err) {
+  const int i = threadIdx.x;
+  if (i >= n) return;
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + i) : "memory");
+    if ((int)(v - epoch) >= 0) break;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      raise_dev_error(err, QCAU_DEVERR_TIMEOUT);
+      break;
+    }
+    __nanosleep(64);
+  }
+}
+
+cudaError_t launch_wait_flags(const uint32_t* flags, int n, uint32_t epoch, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  if (n > 1024) return cudaErrorInvalidValue;
+  wait_flags_kernel<<<1, ((n + 31) / 32) * 32, 0, st>>>(flags, n, epoch, device_error_word());
+  return cudaGetLastError();
+}
+
 cudaError_t launch_attn_combine(const AttnArgs& p, cudaStream_t st) {
   const int64_t tasks = p.b * p.s * p.h;
   if (tasks == 0) return cudaSuccess;

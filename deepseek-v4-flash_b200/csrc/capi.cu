@@ -7,6 +7,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include <cstring>
 
 using namespace qcau;
 
@@ -810,6 +811,105 @@ int qcau_decode_attn_paged_cp(const void* q_all, const void* cache, const int32_
                 "h a multiple of 128, h / n_ranks a multiple of 64 or 8, 16 or 32)");
   if (b == 0) return QCAU_OK;
   QCAU_CHECK_CUDA(launch_decode_attn_sm100(a, to_stream(stream)));
+  return QCAU_OK;
+}
+
+int qcau_decode_attn_paged_cp_p2p(const void* q_all, const void* cache,
+                                  const int32_t* block_table, const int32_t* seqlens,
+                                  float* const* dst_o, float* const* dst_ml,
+                                  uint32_t* const* dst_flag, uint32_t epoch,
+                                  uint32_t* done_counter, int64_t b, int64_t h, int64_t n_ranks,
+                                  int64_t rank, int64_t d_qk, int64_t d_v, int64_t d_kv,
+                                  int64_t page_size, int64_t max_pages, int64_t num_pages,
+                                  int64_t max_seqlen, float softmax_scale, void* stream) {
+  QCAU_CHECK_ARG(q_all && cache && block_table && seqlens && dst_o && dst_ml && dst_flag &&
+                     done_counter,
+                 "decode_attn_paged_cp_p2p: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && h > 0 && page_size > 0 && max_pages > 0 && num_pages > 0,
+                 "decode_attn_paged_cp_p2p: bad shape");
+  QCAU_CHECK_ARG(n_ranks >= 1 && n_ranks <= 16 && rank >= 0 && rank < n_ranks && h % n_ranks == 0,
+                 "decode_attn_paged_cp_p2p: 1..16 ranks, rank in range, heads divisible by ranks");
+  for (int64_t j = 0; j < n_ranks; j++)
+    QCAU_CHECK_ARG(dst_o[j] && dst_ml[j] && dst_flag[j],
+                   "decode_attn_paged_cp_p2p: NULL destination pointer");
+  QCAU_CHECK_ARG(max_seqlen >= 0 && max_seqlen <= max_pages * page_size,
+                 "decode_attn_paged_cp_p2p: max_seqlen exceeds the block table");
+  int rc = check_attn_widths(d_qk, d_v, d_kv, "decode_attn_paged_cp_p2p");
+  if (rc) return rc;
+  AttnArgs a{};
+  a.q = q_all;
+  a.q_row_stride = d_qk;
+  a.kv = cache;
+  a.block_table = block_table;
+  a.seqlens = seqlens;
+  a.b = b; a.s = 1; a.h = h; a.d_qk = d_qk; a.d_v = d_v; a.d_kv = d_kv;
+  a.page_size = page_size;
+  a.max_pages = max_pages;
+  a.num_pages = num_pages;
+  a.max_len = max_seqlen;
+  a.scale = softmax_scale;
+  a.splits = 1;
+  a.split_base = (int)rank;
+  a.splits_total = (int)n_ranks;
+  a.q_hblock = h / n_ranks;
+  a.part_hblock = h / n_ranks;
+  a.peer = 1;
+  for (int64_t j = 0; j < n_ranks; j++) {
+    a.peer_o[j] = dst_o[j];
+    a.peer_ml[j] = dst_ml[j];
+    a.peer_flag[j] = dst_flag[j];
+  }
+  a.done_counter = done_counter;
+  a.epoch = epoch;
+  if (!decode_attn_sm100_supported(a))
+    return fail(QCAU_ERR_UNSUPPORTED,
+                "decode_attn_paged_cp_p2p: needs the sm_100a pair kernel (d_qk 576, d_v 512, "
+                "page 64, h a multiple of 128, h / n_ranks a multiple of 64 or 8, 16 or 32)");
+  if (b == 0) return QCAU_OK;
+  QCAU_CHECK_CUDA(launch_decode_attn_sm100(a, to_stream(stream)));
+  return QCAU_OK;
+}
+
+int qcau_wait_flags(const uint32_t* flags, int64_t n, uint32_t epoch, void* stream) {
+  QCAU_CHECK_ARG(flags != nullptr && n >= 0 && n <= 1024, "wait_flags: bad argument");
+  QCAU_CHECK_CUDA(launch_wait_flags(flags, (int)n, epoch, to_stream(stream)));
+  return QCAU_OK;
+}
+
+size_t qcau_ipc_handle_size(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int qcau_ipc_alloc(size_t bytes, void** ptr, void* handle_out) {
+  QCAU_CHECK_ARG(ptr != nullptr && handle_out != nullptr && bytes > 0, "ipc_alloc: bad argument");
+  void* p = nullptr;
+  QCAU_CHECK_CUDA(cudaMalloc(&p, bytes));
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle_out), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail_cuda(e, "ipc_alloc");
+  }
+  *ptr = p;
+  return QCAU_OK;
+}
+
+int qcau_ipc_open(const void* handle, void** ptr) {
+  QCAU_CHECK_ARG(handle != nullptr && ptr != nullptr, "ipc_open: bad argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  QCAU_CHECK_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return QCAU_OK;
+}
+
+int qcau_ipc_close(void* ptr) {
+  QCAU_CHECK_ARG(ptr != nullptr, "ipc_close: NULL pointer");
+  QCAU_CHECK_CUDA(cudaIpcCloseMemHandle(ptr));
+  return QCAU_OK;
+}
+
+int qcau_ipc_free(void* ptr) {
+  QCAU_CHECK_ARG(ptr != nullptr, "ipc_free: NULL pointer");
+  QCAU_CHECK_CUDA(cudaFree(ptr));
   return QCAU_OK;
 }
 

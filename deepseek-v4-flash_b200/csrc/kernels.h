@@ -99,7 +99,22 @@ struct AttnArgs {
   int64_t part_hblock;
   // combine: partials are [splits][rows][h] (1) instead of [rows][splits][h]
   int part_split_major;
+  // Partials of head block j written straight into the receive slot of the
+  // rank that owns it (peer memory), when peer != 0: peer_o[j] / peer_ml[j]
+  // are [rows][splits][part_hblock] x d_v / x 2; the last CTA of the grid to
+  // finish stores `epoch` to peer_flag[j] (release, system scope) and resets
+  // done_counter (a zeroed device word of this GPU).
+  int peer;
+  float* peer_o[16];
+  float* peer_ml[16];
+  uint32_t* peer_flag[16];
+  unsigned int* done_counter;
+  uint32_t epoch;
 };
+
+// Wait (bounded, ~1 s) until flags[i] >= epoch (wrapping compare) for i < n;
+// a timeout raises QCAU_DEVERR_TIMEOUT.  One block.
+cudaError_t launch_wait_flags(const uint32_t* flags, int n, uint32_t epoch, cudaStream_t st);
 
 // General split-KV kernel, mma.sync 16-head tiles (attn_general.cu).
 cudaError_t launch_attn_general(const AttnArgs& args, cudaStream_t st);

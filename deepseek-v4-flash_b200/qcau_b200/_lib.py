@@ -86,6 +86,15 @@ SIGNATURES = {
     "qcau_attn_combine_ranks": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P], ctypes.c_int),
     "qcau_mla_decode_out": ([ctypes.POINTER(MlaDims), _P, _P, _P, _P, _P, _P, _SZ, _P],
                             ctypes.c_int),
+    "qcau_ipc_handle_size": ([], _SZ),
+    "qcau_ipc_alloc": ([_SZ, ctypes.POINTER(ctypes.c_void_p), _P], ctypes.c_int),
+    "qcau_ipc_open": ([_P, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "qcau_ipc_close": ([_P], ctypes.c_int),
+    "qcau_ipc_free": ([_P], ctypes.c_int),
+    "qcau_decode_attn_paged_cp_p2p": ([_P, _P, _P, _P, _P, _P, _P, ctypes.c_uint32, _P, _I64,
+                                       _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                                       _I64, _F, _P], ctypes.c_int),
+    "qcau_wait_flags": ([_P, _I64, ctypes.c_uint32, _P], ctypes.c_int),
 }
 
 _lib = None

@@ -24,7 +24,13 @@ wo is row-parallel with an all-reduce of the partial outputs
                         tiles, and an all-to-all brings each rank the
                         partial softmax states of its heads, which it merges
                         before the v-up.  Each rank streams 1/N of the cache
-                        and exchanges b*h/N*(N-1)*(512+2)*4 bytes.
+                        and exchanges b*h/N*(N-1)*(512+2)*4 bytes:
+    exchange="nccl"     with an NCCL all-to-all (the faster one measured);
+    exchange="p2p"      stored by the attention kernel itself into the
+                        owning rank's receive area (CUDA IPC peer memory
+                        over NVLink), with a flag per source rank.  Its
+                        epilogue's 16-byte remote stores hold up each CTA
+                        pair, which costs more than the all-to-all at 8 GPUs.
 
 The reference's V4 attention has no wkv_b; this layer serves the absorbed-MLA
 decode configuration (kv_lora 512 + rope 64 cache rows, d_nope 128, d_v 128).
@@ -110,13 +116,17 @@ class MLADecodeLayer:
     """Holds this rank's weight shards and runs one decode step per call."""
 
     def __init__(self, cfg: MLAConfig, device, rank: int = 0, world_size: int = 1,
-                 process_group=None, attn_split: str = "context"):
+                 process_group=None, attn_split: str = "context", exchange: str = "nccl"):
         if cfg.n_heads % world_size:
             raise ValueError("n_heads must be divisible by the number of ranks")
         if attn_split not in ("heads", "context"):
             raise ValueError("attn_split must be 'heads' or 'context'")
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError("exchange must be 'p2p' or 'nccl'")
         self.attn_split = attn_split
+        self.exchange = exchange
         self._cp = None
+        self._peer = None
         self.cfg = cfg
         self.device = torch.device(device)
         self.rank, self.world_size = rank, world_size
@@ -271,6 +281,14 @@ class MLADecodeLayer:
             dist.all_gather_into_tensor(buf["q_all"].view(-1, *buf["q_local"].shape[1:]),
                                         buf["q_local"], group=self.group)
             q_all = buf["q_all"]
+        if N > 1 and self.exchange == "p2p":
+            # the attention kernel stores each rank's partials into that rank's
+            # receive area over NVLink and raises its flags; wait for all N
+            o_ptr, ml_ptr = self._peer_attn_stage(q_all, cache, block_table, seqlens, max_seqlen)
+            self._combine_ptrs(o_ptr, ml_ptr, buf["o_lat"])
+            self._out_stage(d, buf["o_lat"], y)
+            dist.all_reduce(y, group=self.group)
+            return y
         self._attn_stage(q_all, cache, block_table, seqlens, max_seqlen, buf["part_o"],
                          buf["part_ml"])
         recv_o, recv_ml = buf["part_o"], buf["part_ml"]
@@ -309,10 +327,43 @@ class MLADecodeLayer:
 
     def _combine_stage(self, recv_o, recv_ml, o_lat):
         """o_lat [B, h/N, 512] bf16 from the N partials of this rank's heads."""
-        check(lib().qcau_attn_combine_ranks(recv_o.data_ptr(), recv_ml.data_ptr(), None,
-                                            o_lat.data_ptr(), o_lat.size(0), self.n_local,
-                                            self.world_size, self.cfg.kv_lora,
+        self._combine_ptrs(recv_o.data_ptr(), recv_ml.data_ptr(), o_lat)
+
+    def _combine_ptrs(self, o_ptr: int, ml_ptr: int, o_lat):
+        check(lib().qcau_attn_combine_ranks(o_ptr, ml_ptr, None, o_lat.data_ptr(), o_lat.size(0),
+                                            self.n_local, self.world_size, self.cfg.kv_lora,
                                             stream_ptr(self.device)), "attn_combine_ranks")
+
+    def _peer_attn_stage(self, q_all, cache, block_table, seqlens, max_seqlen):
+        """Context-parallel attention with the exchange fused into the kernel;
+        returns the (o, ml) pointers of this rank's completed receive area."""
+        c, N, r = self.cfg, self.world_size, self.rank
+        B = q_all.size(-3)
+        if self._peer is None or self._peer.B != B:
+            if self._peer is not None:
+                self._peer.close()
+            self._peer = PeerExchange(self.device, self.group, r, N, B, self.n_local, c.kv_lora)
+        px = self._peer
+        px.epoch += 1
+        dst_o, dst_ml, dst_flag = px.destinations(px.epoch & 1)
+        w = c.kv_lora + c.d_rope
+        st = stream_ptr(self.device)
+        L = lib()
+        check(L.qcau_decode_attn_paged_cp_p2p(q_all.data_ptr(), cache.data_ptr(),
+                                              block_table.data_ptr(), seqlens.data_ptr(), dst_o,
+                                              dst_ml, dst_flag, px.epoch & 0xFFFFFFFF,
+                                              px.counter.data_ptr(), B, c.n_heads, N, r, w,
+                                              c.kv_lora, w, c.page_size, block_table.size(1),
+                                              cache.size(0), max_seqlen, c.softmax_scale, st),
+              "decode_attn_paged_cp_p2p")
+        check(L.qcau_wait_flags(px.flags_ptr(), N, px.epoch & 0xFFFFFFFF, st), "wait_flags")
+        return px.area(px.epoch & 1)
+
+    def close(self):
+        """Release the peer receive buffers (collective: every rank calls it)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     def _out_stage(self, d, o_lat, y):
         """y [B, dim], this rank's row-parallel partial."""
@@ -321,6 +372,87 @@ class MLADecodeLayer:
                                         self.wo.data_ptr(), self.wo_scale.data_ptr(),
                                         y.data_ptr(), ws.data_ptr(), ws.numel(),
                                         stream_ptr(self.device)), "mla_decode_out")
+
+
+class PeerExchange:
+    """Receive areas of the fused partial exchange, shared over CUDA IPC.
+
+    This rank's buffer (in its own GPU memory) holds two areas, used by
+    alternate steps, each [N_src, B, h/N, 512] fp32 (o) and [N_src, B, h/N, 2]
+    fp32 (max in log2 units, sum), then one flag word per source rank.  Every
+    rank opens every peer's buffer; `destinations(parity)` gives the pointers
+    where this rank's partials for rank j go (its slot in rank j's area) and
+    rank j's flag word for this rank.  Building it is collective.
+    """
+
+    def __init__(self, device, group, rank: int, world_size: int, batch: int, heads_local: int,
+                 d_v: int):
+        import ctypes
+        self.device, self.rank, self.N, self.B = device, rank, world_size, batch
+        align = lambda x: (x + 255) // 256 * 256   # noqa: E731
+        self.slot_o = batch * heads_local * d_v * 4       # one source's o partials
+        self.slot_ml = batch * heads_local * 2 * 4
+        self.area_o_bytes = align(world_size * self.slot_o)
+        self.area_ml_bytes = align(world_size * self.slot_ml)
+        self.area_bytes = self.area_o_bytes + self.area_ml_bytes
+        self.flags_off = 2 * self.area_bytes
+        total = self.flags_off + align(world_size * 4)
+        L = lib()
+        hsz = L.qcau_ipc_handle_size()
+        handle = (ctypes.c_ubyte * hsz)()
+        base = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            check(L.qcau_ipc_alloc(total, ctypes.byref(base), ctypes.cast(handle, ctypes.c_void_p)),
+                  "ipc_alloc")
+        self.base = base.value
+        handles = [None] * world_size
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.peers = []
+        for j, h in enumerate(handles):
+            if j == rank:
+                self.peers.append(self.base)
+                continue
+            p = ctypes.c_void_p()
+            hb = (ctypes.c_ubyte * hsz).from_buffer_copy(h)
+            with torch.cuda.device(device):
+                check(L.qcau_ipc_open(ctypes.cast(hb, ctypes.c_void_p), ctypes.byref(p)),
+                      "ipc_open")
+            self.peers.append(p.value)
+        self.counter = torch.zeros(1, device=device, dtype=torch.int32)
+        self.epoch = 0
+        self.group = group
+        self._ptrs = ctypes.c_void_p * world_size
+
+    def area(self, parity: int):
+        """(o, ml) device pointers of this rank's receive area `parity`."""
+        a = self.base + parity * self.area_bytes
+        return a, a + self.area_o_bytes
+
+    def flags_ptr(self) -> int:
+        return self.base + self.flags_off
+
+    def destinations(self, parity: int):
+        """Host arrays (as void pointers) of this rank's destinations in every rank."""
+        import ctypes
+        r = self.rank
+        off = parity * self.area_bytes
+        self._keep = (self._ptrs(*[p + off + r * self.slot_o for p in self.peers]),
+                      self._ptrs(*[p + off + self.area_o_bytes + r * self.slot_ml
+                                   for p in self.peers]),
+                      self._ptrs(*[p + self.flags_off + 4 * r for p in self.peers]))
+        return tuple(ctypes.cast(a, ctypes.c_void_p) for a in self._keep)
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (collective)."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        L = lib()
+        for j, p in enumerate(self.peers):
+            if j != self.rank:
+                check(L.qcau_ipc_close(p), "ipc_close")
+        dist.barrier(group=self.group)
+        check(L.qcau_ipc_free(self.base), "ipc_free")
+        self.peers = []
 
 
 def make_paged_cache(batch: int, ctx: int, page_size: int, width: int, device, seed: int = 0,

@@ -25,6 +25,8 @@
  *     qcau_device_error() after the stream has been synchronised.
  *   - The library never allocates device memory on its own: callers pass a
  *     workspace where one is needed, sized by the matching *_workspace_size().
+ *     The one allocating call is qcau_ipc_alloc, whose job it is (a buffer
+ *     shared with peer processes through CUDA IPC).
  *
  * Reference file:line citations are relative to the reference project root
  * (dinhthituyetmai05/Deepseek-V4-Flash).
@@ -342,6 +344,43 @@ int qcau_attn_combine_ranks(const float* part_o, const float* part_ml, const flo
 int qcau_mla_decode_out(const qcau_mla_dims* dims, const void* o_lat, const void* wkv_b_bf16,
                         const void* wo, const void* wo_scale, void* y, void* workspace,
                         size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * The exchange of decode_attn_paged_cp fused into the attention kernel (no
+ * reference counterpart).  Each rank owns a receive buffer in its own GPU
+ * memory, exported through CUDA IPC (ipc_alloc, zero-filled; handles of
+ * qcau_ipc_handle_size() bytes swapped between the processes by the
+ * caller; ipc_open maps a peer's buffer, with peer access over NVLink).
+ * decode_attn_paged_cp_p2p computes what decode_attn_paged_cp does, but
+ * writes the partials of head block j (the heads of rank j) straight into
+ * rank j's buffer: dst_o[j] -> [b, h/N, d_v] fp32 and dst_ml[j] ->
+ * [b, h/N, 2], this rank's slot of rank j's [N_src, b, h/N, ...] receive
+ * area.  The last CTA to finish then stores `epoch` to dst_flag[j] (this
+ * rank's flag word in rank j's buffer) with release semantics at system
+ * scope; done_counter is a zeroed uint32 of this GPU that the kernel
+ * resets.  wait_flags (one block, bounded at ~1 s, then
+ * QCAU_DEVERR_TIMEOUT) waits until the n flags of this rank's buffer reach
+ * `epoch` (wrapping compare); the receive area is then complete.
+ * All ranks call with the same b (b == 0 writes and signals nothing).  A
+ * receive area must not be rewritten before its owner has merged it: the
+ * caller alternates two areas by step and orders steps (the layer's
+ * all-reduce of y does).  Pointers in dst_* are device pointers; the arrays
+ * themselves are host memory of n_ranks entries (n_ranks <= 16).
+ * ---------------------------------------------------------------------- */
+size_t qcau_ipc_handle_size(void);
+int qcau_ipc_alloc(size_t bytes, void** ptr, void* handle_out);
+int qcau_ipc_open(const void* handle, void** ptr);
+int qcau_ipc_close(void* ptr);
+int qcau_ipc_free(void* ptr);
+int qcau_decode_attn_paged_cp_p2p(const void* q_all, const void* cache,
+                                  const int32_t* block_table, const int32_t* seqlens,
+                                  float* const* dst_o, float* const* dst_ml,
+                                  uint32_t* const* dst_flag, uint32_t epoch,
+                                  uint32_t* done_counter, int64_t b, int64_t h, int64_t n_ranks,
+                                  int64_t rank, int64_t d_qk, int64_t d_v, int64_t d_kv,
+                                  int64_t page_size, int64_t max_pages, int64_t num_pages,
+                                  int64_t max_seqlen, float softmax_scale, void* stream);
+int qcau_wait_flags(const uint32_t* flags, int64_t n, uint32_t epoch, void* stream);
 
 #ifdef __cplusplus
 }

@@ -194,7 +194,9 @@ def _cp_rank_main(rank, world_size, port, out_dir):
                             world_size=world_size)
     try:
         weights, q_lora, cache, table, seqlens, positions, freqs = _inputs()
-        layer = OracleStagesLayer(CFG, "cpu", rank, world_size, attn_split="context")
+        # the exchange through collectives (the fused peer-memory one needs GPUs)
+        layer = OracleStagesLayer(CFG, "cpu", rank, world_size, attn_split="context",
+                                  exchange="nccl")
         layer.load_weights(*weights)
         y = torch.empty(B, CFG.dim, dtype=torch.float32)
         layer.forward(q_lora, cache, table, seqlens, positions, freqs, CTX, y)
@@ -328,6 +330,81 @@ def test_cp_attention_emulated_ranks_match_decode(n):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("n", [2, 8])
+def test_cp_p2p_kernel_emulated_ranks(n):
+    """qcau_decode_attn_paged_cp_p2p of N ranks on one device: each launch
+    stores its partials into the (emulated) receive areas of the ranks that
+    own the heads and raises their flags; after qcau_wait_flags, merging each
+    area equals the single-rank decode attention.  The flags hold the epoch,
+    and the done counter is back at zero after every launch."""
+    import ctypes
+    L = _lib.lib()
+    dev = torch.device("cuda", 0)
+    H, ctx, bsz = 128, 2048, 5
+    cache, table, _ = make_paged_cache(bsz, ctx, PAGE, WIDTH, dev, seed=8)
+    seqlens = torch.tensor([2048, 1, 0, 1500, 700], device=dev, dtype=torch.int32)
+    g = torch.Generator(device=dev).manual_seed(9)
+    q = torch.randn(bsz, H, WIDTH, device=dev, generator=g).to(torch.bfloat16)
+    scale = 192 ** -0.5
+    st = _lib.stream_ptr(dev)
+    ref = torch.empty(bsz, H, 512, device=dev, dtype=torch.bfloat16)
+    need = L.qcau_decode_attn_workspace_size(bsz, H, 512, ctx)
+    ws = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+    _lib.check(L.qcau_decode_attn_paged(q.data_ptr(), cache.data_ptr(), table.data_ptr(),
+                                        seqlens.data_ptr(), None, ref.data_ptr(), bsz, H, WIDTH,
+                                        512, WIDTH, PAGE, table.size(1), cache.size(0), ctx, scale,
+                                        ws.data_ptr(), need, st), "decode")
+    hl = H // n
+    q_all = q.view(bsz, n, hl, WIDTH).transpose(0, 1).contiguous()
+    recv_o = torch.full((n, n, bsz, hl, 512), float("nan"), device=dev)   # [owner][src] ...
+    recv_ml = torch.full((n, n, bsz, hl, 2), float("nan"), device=dev)
+    flags = torch.zeros(n, n, device=dev, dtype=torch.int32)                # [owner][src]
+    counter = torch.zeros(1, device=dev, dtype=torch.int32)
+    epoch = 7
+    arr = ctypes.c_void_p * n
+    for r in range(n):
+        dst_o = arr(*[recv_o[j, r].data_ptr() for j in range(n)])
+        dst_ml = arr(*[recv_ml[j, r].data_ptr() for j in range(n)])
+        dst_f = arr(*[flags[j, r:].data_ptr() for j in range(n)])
+        _lib.check(L.qcau_decode_attn_paged_cp_p2p(
+            q_all.data_ptr(), cache.data_ptr(), table.data_ptr(), seqlens.data_ptr(),
+            ctypes.cast(dst_o, ctypes.c_void_p), ctypes.cast(dst_ml, ctypes.c_void_p),
+            ctypes.cast(dst_f, ctypes.c_void_p), epoch, counter.data_ptr(), bsz, H, n, r, WIDTH,
+            512, WIDTH, PAGE, table.size(1), cache.size(0), ctx, scale, st), "cp_p2p")
+    outs = []
+    for j in range(n):
+        _lib.check(L.qcau_wait_flags(flags[j].data_ptr(), n, epoch, st), "wait")
+        o = torch.empty(bsz, hl, 512, device=dev, dtype=torch.bfloat16)
+        _lib.check(L.qcau_attn_combine_ranks(recv_o[j].data_ptr(), recv_ml[j].data_ptr(), None,
+                                             o.data_ptr(), bsz, hl, n, 512, st), "combine")
+        outs.append(o)
+    got = torch.cat(outs, dim=1)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert torch.all(flags == epoch)
+    assert int(counter.item()) == 0
+    assert not torch.isnan(recv_ml).any(), "every slot was written"
+    a, b = got.float(), ref.float()
+    rms = b.pow(2).mean().sqrt().item()
+    assert (a - b).abs().max().item() <= 2e-2 * rms
+    assert torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item() >= 0.9999
+
+
+@pytest.mark.gpu
+def test_wait_flags_times_out_with_status():
+    """A flag that nothing raises: the wait gives up after its bound (~1 s)
+    and reports QCAU_DEVERR_TIMEOUT; the context stays usable."""
+    L = _lib.lib()
+    flags = torch.zeros(4, device="cuda", dtype=torch.int32)
+    flags[:3] = 5
+    _lib.check(L.qcau_wait_flags(flags.data_ptr(), 4, 5, _lib.stream_ptr()), "wait")
+    assert _lib.device_error() == _lib.DEVERR_TIMEOUT
+    flags[3] = 5
+    _lib.check(L.qcau_wait_flags(flags.data_ptr(), 4, 5, _lib.stream_ptr()), "wait")
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.gpu
 def test_cp_rejects_unsupported_head_blocks():
     L = _lib.lib()
     z = torch.zeros(16, device="cuda", dtype=torch.int32)
@@ -386,10 +463,14 @@ def _nccl_rank_main(rank, world_size, port, out_dir):
         freqs = precompute_freqs_cis(cfg.d_rope, ctx + 1, cfg.rope_theta, dev)
         positions = seqlens.clone()
         ys = {}
-        for mode in ("context", "heads"):
-            layer = MLADecodeLayer(cfg, dev, rank, world_size, attn_split=mode)
+        for name, mode, ex in (("p2p", "context", "p2p"), ("nccl", "context", "nccl"),
+                               ("heads", "heads", "nccl")):
+            layer = MLADecodeLayer(cfg, dev, rank, world_size, attn_split=mode, exchange=ex)
             layer.random_weights(seed=1)
-            ys[mode] = layer.forward(q_lora, cache, table, seqlens, positions, freqs, ctx).clone()
+            for _ in range(3):   # steps alternate the receive areas
+                y = layer.forward(q_lora, cache, table, seqlens, positions, freqs, ctx)
+            ys[name] = y.clone()
+            layer.close()
         if rank == 0:
             full = MLADecodeLayer(cfg, dev)
             full.random_weights(seed=1)
@@ -407,12 +488,13 @@ def _nccl_rank_main(rank, world_size, port, out_dir):
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs")
 def test_cp_layer_over_nccl_two_gpus(tmp_path):
-    """Two ranks over NCCL: the context-split layer and the head-split layer
-    both equal the one-GPU layer."""
+    """Two ranks: the context-split layer with the exchange fused into the
+    attention kernel (peer memory) and with an NCCL all-to-all, and the
+    head-split layer, all equal the one-GPU layer."""
     world_size = 2
     mp.start_processes(_nccl_rank_main, args=(world_size, _free_port(), str(tmp_path)),
                        nprocs=world_size, start_method="spawn", join=True)
     ref = np.load(tmp_path / "one0.npy")
-    for mode in ("context", "heads"):
+    for mode in ("p2p", "nccl", "heads"):
         for r in range(world_size):
             _assert_layer_close(np.load(tmp_path / f"{mode}{r}.npy"), ref, f"{mode} rank {r}")
