@@ -434,14 +434,14 @@ def main():
         # this rank's context-parallel attention: all heads over 1/N of every
         # sequence's tiles, partials for the exchange
         q_all = torch.randn(ws, BATCH, H, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
-        part_o = torch.empty(ws, BATCH, H, 512, device=dev)
+        part_o = torch.empty(ws, BATCH, H, 512, device=dev, dtype=torch.bfloat16)
         part_ml = torch.empty(ws, BATCH, H, 2, device=dev)
 
         def attn():
             _lib.check(L.qcau_decode_attn_paged_cp(
                 q_all.data_ptr(), cache.data_ptr(), table.data_ptr(), seqlens.data_ptr(),
                 part_o.data_ptr(), part_ml.data_ptr(), BATCH, HEADS, ws, rank, WIDTH, 512, WIDTH,
-                PAGE, table.size(1), cache.size(0), CTX, cfg.softmax_scale,
+                PAGE, table.size(1), cache.size(0), CTX, cfg.softmax_scale, 1,
                 _lib.stream_ptr(dev)), "attn_cp")
     else:
         q_abs = torch.randn(BATCH, H, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
@@ -472,9 +472,10 @@ def main():
     full_bytes = cache_bytes + BATCH * HEADS * (WIDTH + 512) * 2 + table.numel() * 4
     if cp:
         # 1/N of the cache and block table (the ranks' tile ranges are equal
-        # here: 256 tiles per sequence), q of all heads, fp32 partials out
+        # here: 256 tiles per sequence), q of all heads, partials out (bf16 O,
+        # fp32 max and sum)
         attn_bytes = (cache_bytes + table.numel() * 4) // ws + BATCH * HEADS * WIDTH * 2 + \
-            BATCH * HEADS * (512 + 2) * 4
+            BATCH * HEADS * (512 * 2 + 2 * 4)
         attn_flops = 2.0 * BATCH * (CTX // ws) * HEADS * (WIDTH + 512)
     else:
         attn_bytes = cache_bytes + BATCH * H * (WIDTH + 512) * 2 + table.numel() * 4

@@ -116,7 +116,8 @@ struct DecodeParams {
   int split_base, splits_total;
   int part_hblock;
   int nblk;
-  float* blk_o[kMaxBlocks];
+  void* blk_o[kMaxBlocks];     // fp32, or bf16 when part_bf16
+  int part_bf16;
   float* blk_ml[kMaxBlocks];
   // completion: when `counter` is set, the last CTA to finish raises
   // flag[j] = epoch (release, system scope) for every block destination j
@@ -522,17 +523,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const float l_tot = l_run + sh->xsum[row ^ 64];
       int blk = 0;
       const int64_t prow = hl < p.cta_heads ? part_row(head0 + hl, blk) : 0;
-      float* po = p.blk_o[blk] + prow * 512 + 256 * half;
+      const int64_t po = prow * 512 + 256 * half;  // element offset of this thread's half row
 #pragma unroll 1
       for (int c = 0; c < 8; c++) {
         float v[32];
         tmem_ld32(tmem + lane_base + kTmemO + c * 32, v);
         tmem_ld_wait();
-        float4* dst = reinterpret_cast<float4*>(po + (c >> 2) * 128 + (c & 3) * 32);
+        const int64_t e = po + (c >> 2) * 128 + (c & 3) * 32;
         if (hl < p.cta_heads) {
+          if (p.part_bf16) {  // unnormalised O rounded to bf16 (halves the exchange)
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.blk_o[blk]) + e);
 #pragma unroll
-          for (int i = 0; i < 8; i++)
-            dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            for (int i = 0; i < 4; i++)
+              dst[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
+                                  pack_bf16(v[8 * i + 4], v[8 * i + 5]),
+                                  pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+          } else {
+            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.blk_o[blk]) + e);
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+              dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+          }
         }
       }
       if (half == 0 && hl < p.cta_heads) {
@@ -645,11 +656,12 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
       p.blk_ml[j] = a.peer_ml[j];
       p.flag[j] = a.peer_flag[j];
     } else if (a.part_o) {
-      p.blk_o[j] = a.part_o + j * blk_rows * 512;
+      p.blk_o[j] = reinterpret_cast<uint8_t*>(a.part_o) + j * blk_rows * 512 * (a.part_bf16 ? 2 : 4);
       p.blk_ml[j] = a.part_ml + j * blk_rows * 2;
     }
   }
   p.counter = a.peer ? a.done_counter : nullptr;
+  p.part_bf16 = a.part_bf16;
   p.epoch = a.epoch;
   // one split and no partial buffers: the epilogue normalises and writes o
   p.direct = (a.splits == 1 && a.part_o == nullptr && !a.peer) ? 1 : 0;

@@ -434,7 +434,7 @@ __global__ void attn_combine_kernel(AttnArgs p) {
     L += (p.sink && isfinite(p.sink[hh])) ? 1.f : 0.f;
   const float inv = 1.f / fmaxf(L, 1.17549435e-38f);
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.o) + (qrow * p.h + hh) * p.d_v;
-  const float* po = p.part_o + prow0 * p.d_v;
+  const int64_t po0 = prow0 * p.d_v;
   const int64_t po_stride = pstride * p.d_v;
   for (int c = lane * 4; c < p.d_v; c += 128) {
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -442,7 +442,16 @@ __global__ void attn_combine_kernel(AttnArgs p) {
       const float mi = ml[i * ml_stride];
       if (mi == -INFINITY) continue;
       const float w = exp2f(mi - M);
-      const float4 v = *reinterpret_cast<const float4*>(po + i * po_stride + c);
+      const int64_t e = po0 + i * po_stride + c;
+      float4 v;
+      if (p.part_bf16) {
+        const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(p.part_o) + e);
+        const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        v = make_float4(lo.x, lo.y, hi.x, hi.y);
+      } else {
+        v = *reinterpret_cast<const float4*>(p.part_o + e);
+      }
       a.x = fmaf(v.x, w, a.x);
       a.y = fmaf(v.y, w, a.y);
       a.z = fmaf(v.z, w, a.z);

@@ -771,11 +771,11 @@ int qcau_mla_decode_out(const qcau_mla_dims* d, const void* o_lat, const void* w
 }
 
 int qcau_decode_attn_paged_cp(const void* q_all, const void* cache, const int32_t* block_table,
-                              const int32_t* seqlens, float* part_o, float* part_ml, int64_t b,
+                              const int32_t* seqlens, void* part_o, float* part_ml, int64_t b,
                               int64_t h, int64_t n_ranks, int64_t rank, int64_t d_qk, int64_t d_v,
                               int64_t d_kv, int64_t page_size, int64_t max_pages,
                               int64_t num_pages, int64_t max_seqlen, float softmax_scale,
-                              void* stream) {
+                              int32_t part_bf16, void* stream) {
   QCAU_CHECK_ARG(q_all && cache && block_table && seqlens && part_o && part_ml,
                  "decode_attn_paged_cp: NULL pointer");
   QCAU_CHECK_ARG(b >= 0 && h > 0 && page_size > 0 && max_pages > 0 && num_pages > 0,
@@ -803,8 +803,9 @@ int qcau_decode_attn_paged_cp(const void* q_all, const void* cache, const int32_
   a.splits_total = (int)n_ranks;
   a.q_hblock = h / n_ranks;
   a.part_hblock = h / n_ranks;
-  a.part_o = part_o;
+  a.part_o = reinterpret_cast<float*>(part_o);
   a.part_ml = part_ml;
+  a.part_bf16 = part_bf16 ? 1 : 0;
   if (!decode_attn_sm100_supported(a))
     return fail(QCAU_ERR_UNSUPPORTED,
                 "decode_attn_paged_cp: needs the sm_100a pair kernel (d_qk 576, d_v 512, page 64, "
@@ -816,12 +817,13 @@ int qcau_decode_attn_paged_cp(const void* q_all, const void* cache, const int32_
 
 int qcau_decode_attn_paged_cp_p2p(const void* q_all, const void* cache,
                                   const int32_t* block_table, const int32_t* seqlens,
-                                  float* const* dst_o, float* const* dst_ml,
+                                  void* const* dst_o, float* const* dst_ml,
                                   uint32_t* const* dst_flag, uint32_t epoch,
                                   uint32_t* done_counter, int64_t b, int64_t h, int64_t n_ranks,
                                   int64_t rank, int64_t d_qk, int64_t d_v, int64_t d_kv,
                                   int64_t page_size, int64_t max_pages, int64_t num_pages,
-                                  int64_t max_seqlen, float softmax_scale, void* stream) {
+                                  int64_t max_seqlen, float softmax_scale, int32_t part_bf16,
+                                  void* stream) {
   QCAU_CHECK_ARG(q_all && cache && block_table && seqlens && dst_o && dst_ml && dst_flag &&
                      done_counter,
                  "decode_attn_paged_cp_p2p: NULL pointer");
@@ -861,6 +863,7 @@ int qcau_decode_attn_paged_cp_p2p(const void* q_all, const void* cache,
   }
   a.done_counter = done_counter;
   a.epoch = epoch;
+  a.part_bf16 = part_bf16 ? 1 : 0;
   if (!decode_attn_sm100_supported(a))
     return fail(QCAU_ERR_UNSUPPORTED,
                 "decode_attn_paged_cp_p2p: needs the sm_100a pair kernel (d_qk 576, d_v 512, "
@@ -913,14 +916,15 @@ int qcau_ipc_free(void* ptr) {
   return QCAU_OK;
 }
 
-int qcau_attn_combine_ranks(const float* part_o, const float* part_ml, const float* attn_sink,
+int qcau_attn_combine_ranks(const void* part_o, const float* part_ml, const float* attn_sink,
                             void* o, int64_t b, int64_t h_local, int64_t n_ranks, int64_t d_v,
-                            void* stream) {
+                            int32_t part_bf16, void* stream) {
   QCAU_CHECK_ARG(part_o && part_ml && o, "attn_combine_ranks: NULL pointer");
   QCAU_CHECK_ARG(b >= 0 && h_local > 0 && n_ranks >= 1 && d_v > 0 && d_v % 128 == 0,
                  "attn_combine_ranks: bad shape");
   AttnArgs a{};
-  a.part_o = const_cast<float*>(part_o);
+  a.part_o = const_cast<float*>(reinterpret_cast<const float*>(part_o));
+  a.part_bf16 = part_bf16 ? 1 : 0;
   a.part_ml = const_cast<float*>(part_ml);
   a.sink = attn_sink;
   a.o = o;

@@ -82,8 +82,9 @@ SIGNATURES = {
     "qcau_mla_decode_q": ([ctypes.POINTER(MlaDims), _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _P],
                           ctypes.c_int),
     "qcau_decode_attn_paged_cp": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
-                                   _I64, _I64, _I64, _I64, _I64, _F, _P], ctypes.c_int),
-    "qcau_attn_combine_ranks": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P], ctypes.c_int),
+                                   _I64, _I64, _I64, _I64, _I64, _F, _I32, _P], ctypes.c_int),
+    "qcau_attn_combine_ranks": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
+                                ctypes.c_int),
     "qcau_mla_decode_out": ([ctypes.POINTER(MlaDims), _P, _P, _P, _P, _P, _P, _SZ, _P],
                             ctypes.c_int),
     "qcau_ipc_handle_size": ([], _SZ),
@@ -93,7 +94,7 @@ SIGNATURES = {
     "qcau_ipc_free": ([_P], ctypes.c_int),
     "qcau_decode_attn_paged_cp_p2p": ([_P, _P, _P, _P, _P, _P, _P, ctypes.c_uint32, _P, _I64,
                                        _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
-                                       _I64, _F, _P], ctypes.c_int),
+                                       _I64, _F, _I32, _P], ctypes.c_int),
     "qcau_wait_flags": ([_P, _I64, ctypes.c_uint32, _P], ctypes.c_int),
 }
 

@@ -254,9 +254,10 @@ class MLADecodeLayer:
                 "B": B,
                 "q_local": torch.empty(B, Hl, w, device=dev, dtype=bf16),
                 "q_all": torch.empty(N, B, Hl, w, device=dev, dtype=bf16),
-                "part_o": torch.empty(N, B, Hl, c.kv_lora, device=dev, dtype=f32),
+                # unnormalised O partials in bf16 (half the bytes to exchange)
+                "part_o": torch.empty(N, B, Hl, c.kv_lora, device=dev, dtype=bf16),
                 "part_ml": torch.empty(N, B, Hl, 2, device=dev, dtype=f32),
-                "recv_o": torch.empty(N, B, Hl, c.kv_lora, device=dev, dtype=f32),
+                "recv_o": torch.empty(N, B, Hl, c.kv_lora, device=dev, dtype=bf16),
                 "recv_ml": torch.empty(N, B, Hl, 2, device=dev, dtype=f32),
                 "o_lat": torch.empty(B, Hl, c.kv_lora, device=dev, dtype=bf16),
             }
@@ -322,7 +323,7 @@ class MLADecodeLayer:
                                               q_all.size(-3), c.n_heads, self.world_size,
                                               self.rank, w, c.kv_lora, w, c.page_size,
                                               block_table.size(1), cache.size(0), max_seqlen,
-                                              c.softmax_scale, stream_ptr(self.device)),
+                                              c.softmax_scale, 1, stream_ptr(self.device)),
               "decode_attn_paged_cp")
 
     def _combine_stage(self, recv_o, recv_ml, o_lat):
@@ -331,7 +332,7 @@ class MLADecodeLayer:
 
     def _combine_ptrs(self, o_ptr: int, ml_ptr: int, o_lat):
         check(lib().qcau_attn_combine_ranks(o_ptr, ml_ptr, None, o_lat.data_ptr(), o_lat.size(0),
-                                            self.n_local, self.world_size, self.cfg.kv_lora,
+                                            self.n_local, self.world_size, self.cfg.kv_lora, 1,
                                             stream_ptr(self.device)), "attn_combine_ranks")
 
     def _peer_attn_stage(self, q_all, cache, block_table, seqlens, max_seqlen):
@@ -354,7 +355,7 @@ class MLADecodeLayer:
                                               dst_ml, dst_flag, px.epoch & 0xFFFFFFFF,
                                               px.counter.data_ptr(), B, c.n_heads, N, r, w,
                                               c.kv_lora, w, c.page_size, block_table.size(1),
-                                              cache.size(0), max_seqlen, c.softmax_scale, st),
+                                              cache.size(0), max_seqlen, c.softmax_scale, 1, st),
               "decode_attn_paged_cp_p2p")
         check(L.qcau_wait_flags(px.flags_ptr(), N, px.epoch & 0xFFFFFFFF, st), "wait_flags")
         return px.area(px.epoch & 1)
@@ -378,7 +379,7 @@ class PeerExchange:
     """Receive areas of the fused partial exchange, shared over CUDA IPC.
 
     This rank's buffer (in its own GPU memory) holds two areas, used by
-    alternate steps, each [N_src, B, h/N, 512] fp32 (o) and [N_src, B, h/N, 2]
+    alternate steps, each [N_src, B, h/N, 512] bf16 (o) and [N_src, B, h/N, 2]
     fp32 (max in log2 units, sum), then one flag word per source rank.  Every
     rank opens every peer's buffer; `destinations(parity)` gives the pointers
     where this rank's partials for rank j go (its slot in rank j's area) and
@@ -390,7 +391,7 @@ class PeerExchange:
         import ctypes
         self.device, self.rank, self.N, self.B = device, rank, world_size, batch
         align = lambda x: (x + 255) // 256 * 256   # noqa: E731
-        self.slot_o = batch * heads_local * d_v * 4       # one source's o partials
+        self.slot_o = batch * heads_local * d_v * 2       # one source's o partials (bf16)
         self.slot_ml = batch * heads_local * 2 * 4
         self.area_o_bytes = align(world_size * self.slot_o)
         self.area_ml_bytes = align(world_size * self.slot_ml)

@@ -314,8 +314,10 @@ int qcau_mla_decode(const qcau_mla_dims* dims, const void* q_lora,
  *   (caller)            all-gather -> q_all [N, b, h/N, 576]
  *   decode_attn_paged_cp   all h heads over tiles [ntiles*r/N, ntiles*(r+1)/N)
  *                       of every sequence (ntiles = ceil(seqlen/128)) ->
- *                       partials [N, b, h/N, 512] and [N, b, h/N, 2] fp32,
- *                       block j holding the heads of rank j
+ *                       partials [N, b, h/N, 512] (fp32, or bf16 with
+ *                       part_bf16 = 1: half the bytes to exchange) and
+ *                       [N, b, h/N, 2] fp32, block j holding the heads of
+ *                       rank j
  *   (caller)            all-to-all of the blocks -> [N, b, h/N, ...] by source
  *   attn_combine_ranks  o_lat [b, h/N, 512] bf16 (sink optional)
  *   mla_decode_out      y [b, dim] (row-parallel partial)
@@ -333,14 +335,14 @@ int qcau_mla_decode_q(const qcau_mla_dims* dims, const void* q_lora, const void*
                       void* workspace, size_t workspace_bytes, void* stream);
 int qcau_decode_attn_paged_cp(const void* q_all, const void* cache,
                               const int32_t* block_table, const int32_t* seqlens,
-                              float* part_o, float* part_ml, int64_t b, int64_t h,
+                              void* part_o, float* part_ml, int64_t b, int64_t h,
                               int64_t n_ranks, int64_t rank, int64_t d_qk, int64_t d_v,
                               int64_t d_kv, int64_t page_size, int64_t max_pages,
                               int64_t num_pages, int64_t max_seqlen, float softmax_scale,
-                              void* stream);
-int qcau_attn_combine_ranks(const float* part_o, const float* part_ml, const float* attn_sink,
+                              int32_t part_bf16, void* stream);
+int qcau_attn_combine_ranks(const void* part_o, const float* part_ml, const float* attn_sink,
                             void* o, int64_t b, int64_t h_local, int64_t n_ranks, int64_t d_v,
-                            void* stream);
+                            int32_t part_bf16, void* stream);
 int qcau_mla_decode_out(const qcau_mla_dims* dims, const void* o_lat, const void* wkv_b_bf16,
                         const void* wo, const void* wo_scale, void* y, void* workspace,
                         size_t workspace_bytes, void* stream);
@@ -353,7 +355,8 @@ int qcau_mla_decode_out(const qcau_mla_dims* dims, const void* o_lat, const void
  * caller; ipc_open maps a peer's buffer, with peer access over NVLink).
  * decode_attn_paged_cp_p2p computes what decode_attn_paged_cp does, but
  * writes the partials of head block j (the heads of rank j) straight into
- * rank j's buffer: dst_o[j] -> [b, h/N, d_v] fp32 and dst_ml[j] ->
+ * rank j's buffer: dst_o[j] -> [b, h/N, d_v] (fp32, or bf16 with part_bf16)
+ * and dst_ml[j] ->
  * [b, h/N, 2], this rank's slot of rank j's [N_src, b, h/N, ...] receive
  * area.  The last CTA to finish then stores `epoch` to dst_flag[j] (this
  * rank's flag word in rank j's buffer) with release semantics at system
@@ -374,12 +377,13 @@ int qcau_ipc_close(void* ptr);
 int qcau_ipc_free(void* ptr);
 int qcau_decode_attn_paged_cp_p2p(const void* q_all, const void* cache,
                                   const int32_t* block_table, const int32_t* seqlens,
-                                  float* const* dst_o, float* const* dst_ml,
+                                  void* const* dst_o, float* const* dst_ml,
                                   uint32_t* const* dst_flag, uint32_t epoch,
                                   uint32_t* done_counter, int64_t b, int64_t h, int64_t n_ranks,
                                   int64_t rank, int64_t d_qk, int64_t d_v, int64_t d_kv,
                                   int64_t page_size, int64_t max_pages, int64_t num_pages,
-                                  int64_t max_seqlen, float softmax_scale, void* stream);
+                                  int64_t max_seqlen, float softmax_scale, int32_t part_bf16,
+                                  void* stream);
 int qcau_wait_flags(const uint32_t* flags, int64_t n, uint32_t epoch, void* stream);
 
 #ifdef __cplusplus

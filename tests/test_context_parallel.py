@@ -174,7 +174,7 @@ class OracleStagesLayer(MLADecodeLayer):
         part_ml.copy_(torch.from_numpy(pml))
 
     def _combine_stage(self, recv_o, recv_ml, o_lat):
-        o = merge_partials(recv_o.numpy(), recv_ml.numpy())
+        o = merge_partials(recv_o.float().numpy(), recv_ml.numpy())
         o_lat.copy_(torch.from_numpy(o.view(np.int16)).view(torch.bfloat16))
 
     def _out_stage(self, d, o_lat, y):
@@ -213,13 +213,11 @@ def test_context_parallel_layer_over_gloo_equals_unsharded(tmp_path):
     rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
     for r in range(world_size):
         y = np.load(tmp_path / f"y{r}.npy")
-        # P is rounded to bf16 against each rank's own maximum: bf16 noise in
-        # o_lat, which the FP8 act_quant of o_v (one e4m3 step is 1/8) can turn
-        # into a code flip of single elements; a wrong block or tile order
-        # would break the cosine
-        cos = float((y * ref).sum() / np.sqrt((y * y).sum() * (ref * ref).sum()))
-        assert cos >= 0.9999, f"rank {r}: cos {cos}"
-        assert np.max(np.abs(y - ref)) <= 5e-2 * rms, f"rank {r}"
+        # P is rounded to bf16 against each rank's own maximum and the O
+        # partials are exchanged in bf16: bf16 noise in o_lat, which the FP8
+        # act_quant of o_v (one e4m3 step is 1/8) can turn into a code flip of
+        # single elements; a wrong block or tile order would break the cosine
+        _assert_layer_close(y, ref, f"rank {r}")
 
 
 def test_rank_tile_ranges_partition_every_sequence():
@@ -271,14 +269,14 @@ def _assert_layer_close(y: np.ndarray, ref: np.ndarray, what: str):
     y, ref = y.astype(np.float64), ref.astype(np.float64)
     rms = float(np.sqrt(np.mean(ref ** 2)))
     cos = float((y * ref).sum() / np.sqrt((y * y).sum() * (ref * ref).sum()))
-    assert cos >= 0.9999, (what, cos)
+    assert cos >= 0.9995, (what, cos)
     assert float(np.mean(np.abs(y - ref))) <= 3e-2 * rms, what
     assert float(np.max(np.abs(y - ref))) <= 0.15 * rms, what
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("n", [1, 2, 4, 8])
-def test_cp_attention_emulated_ranks_match_decode(n):
+@pytest.mark.parametrize("n,bf16", [(1, 1), (2, 1), (4, 0), (4, 1), (8, 1)])
+def test_cp_attention_emulated_ranks_match_decode(n, bf16):
     """N ranks of qcau_decode_attn_paged_cp on one device, the block exchange
     done by indexing, merged by qcau_attn_combine_ranks, equal the
     single-rank qcau_decode_attn_paged (ragged lengths, an empty sequence,
@@ -302,21 +300,22 @@ def test_cp_attention_emulated_ranks_match_decode(n):
                                         ws.data_ptr(), need, st), "decode")
     hl = H // n
     q_all = q.view(bsz, n, hl, WIDTH).transpose(0, 1).contiguous()
-    part_o = torch.empty(n, n, bsz, hl, 512, device=dev)   # [rank][dest] ...
+    odt = torch.bfloat16 if bf16 else torch.float32
+    part_o = torch.empty(n, n, bsz, hl, 512, device=dev, dtype=odt)   # [rank][dest] ...
     part_ml = torch.empty(n, n, bsz, hl, 2, device=dev)
     for r in range(n):
         _lib.check(L.qcau_decode_attn_paged_cp(q_all.data_ptr(), cache.data_ptr(),
                                                table.data_ptr(), seqlens.data_ptr(),
                                                part_o[r].data_ptr(), part_ml[r].data_ptr(), bsz,
                                                H, n, r, WIDTH, 512, WIDTH, PAGE, table.size(1),
-                                               cache.size(0), ctx, scale, st), "cp")
+                                               cache.size(0), ctx, scale, bf16, st), "cp")
     outs = []
     for dst in range(n):
         recv_o = part_o[:, dst].contiguous()
         recv_ml = part_ml[:, dst].contiguous()
         o = torch.empty(bsz, hl, 512, device=dev, dtype=torch.bfloat16)
         _lib.check(L.qcau_attn_combine_ranks(recv_o.data_ptr(), recv_ml.data_ptr(), None,
-                                             o.data_ptr(), bsz, hl, n, 512, st), "combine")
+                                             o.data_ptr(), bsz, hl, n, 512, bf16, st), "combine")
         outs.append(o)
     got = torch.cat(outs, dim=1)
     torch.cuda.synchronize()
@@ -356,7 +355,8 @@ def test_cp_p2p_kernel_emulated_ranks(n):
                                         ws.data_ptr(), need, st), "decode")
     hl = H // n
     q_all = q.view(bsz, n, hl, WIDTH).transpose(0, 1).contiguous()
-    recv_o = torch.full((n, n, bsz, hl, 512), float("nan"), device=dev)   # [owner][src] ...
+    recv_o = torch.full((n, n, bsz, hl, 512), float("nan"), device=dev,
+                        dtype=torch.bfloat16)   # [owner][src] ...
     recv_ml = torch.full((n, n, bsz, hl, 2), float("nan"), device=dev)
     flags = torch.zeros(n, n, device=dev, dtype=torch.int32)                # [owner][src]
     counter = torch.zeros(1, device=dev, dtype=torch.int32)
@@ -370,13 +370,13 @@ def test_cp_p2p_kernel_emulated_ranks(n):
             q_all.data_ptr(), cache.data_ptr(), table.data_ptr(), seqlens.data_ptr(),
             ctypes.cast(dst_o, ctypes.c_void_p), ctypes.cast(dst_ml, ctypes.c_void_p),
             ctypes.cast(dst_f, ctypes.c_void_p), epoch, counter.data_ptr(), bsz, H, n, r, WIDTH,
-            512, WIDTH, PAGE, table.size(1), cache.size(0), ctx, scale, st), "cp_p2p")
+            512, WIDTH, PAGE, table.size(1), cache.size(0), ctx, scale, 1, st), "cp_p2p")
     outs = []
     for j in range(n):
         _lib.check(L.qcau_wait_flags(flags[j].data_ptr(), n, epoch, st), "wait")
         o = torch.empty(bsz, hl, 512, device=dev, dtype=torch.bfloat16)
         _lib.check(L.qcau_attn_combine_ranks(recv_o[j].data_ptr(), recv_ml[j].data_ptr(), None,
-                                             o.data_ptr(), bsz, hl, n, 512, st), "combine")
+                                             o.data_ptr(), bsz, hl, n, 512, 1, st), "combine")
         outs.append(o)
     got = torch.cat(outs, dim=1)
     torch.cuda.synchronize()
@@ -411,12 +411,12 @@ def test_cp_rejects_unsupported_head_blocks():
     # 128 heads over 3 ranks: not divisible
     rc = L.qcau_decode_attn_paged_cp(z.data_ptr(), z.data_ptr(), z.data_ptr(), z.data_ptr(),
                                      z.data_ptr(), z.data_ptr(), 1, 128, 3, 0, 576, 512, 576, 64,
-                                     1, 1, 64, 0.1, _lib.stream_ptr())
+                                     1, 1, 64, 0.1, 0, _lib.stream_ptr())
     assert rc == _lib.QCAU_ERR_INVALID
     # 128 heads over 16 ranks: blocks of 8 heads are allowed; 48 heads are not a multiple of 128
     rc = L.qcau_decode_attn_paged_cp(z.data_ptr(), z.data_ptr(), z.data_ptr(), z.data_ptr(),
                                      z.data_ptr(), z.data_ptr(), 1, 48, 2, 0, 576, 512, 576, 64,
-                                     1, 1, 64, 0.1, _lib.stream_ptr())
+                                     1, 1, 64, 0.1, 0, _lib.stream_ptr())
     assert rc == _lib.QCAU_ERR_UNSUPPORTED
 
 
