@@ -434,7 +434,7 @@ def main():
         # this rank's context-parallel attention: all heads over 1/N of every
         # sequence's tiles, partials for the exchange
         q_all = torch.randn(ws, BATCH, H, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
-        part_o = torch.empty(ws, BATCH, H, 512, device=dev, dtype=torch.bfloat16)
+        part_o = torch.empty(ws, BATCH, H, 512, device=dev, dtype=torch.float16)
         part_ml = torch.empty(ws, BATCH, H, 2, device=dev)
 
         def attn():
@@ -472,8 +472,8 @@ def main():
     full_bytes = cache_bytes + BATCH * HEADS * (WIDTH + 512) * 2 + table.numel() * 4
     if cp:
         # 1/N of the cache and block table (the ranks' tile ranges are equal
-        # here: 256 tiles per sequence), q of all heads, partials out (bf16 O,
-        # fp32 max and sum)
+        # here: 256 tiles per sequence), q of all heads, partials out (fp16
+        # O / sum, fp32 max and sum)
         attn_bytes = (cache_bytes + table.numel() * 4) // ws + BATCH * HEADS * WIDTH * 2 + \
             BATCH * HEADS * (512 * 2 + 2 * 4)
         attn_flops = 2.0 * BATCH * (CTX // ws) * HEADS * (WIDTH + 512)

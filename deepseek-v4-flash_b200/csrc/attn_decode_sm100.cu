@@ -116,8 +116,8 @@ struct DecodeParams {
   int split_base, splits_total;
   int part_hblock;
   int nblk;
-  void* blk_o[kMaxBlocks];     // fp32, or bf16 when part_bf16
-  int part_bf16;
+  void* blk_o[kMaxBlocks];     // fp32 O, or fp16 O / l when part_f16
+  int part_f16;
   float* blk_ml[kMaxBlocks];
   // completion: when `counter` is set, the last CTA to finish raises
   // flag[j] = epoch (release, system scope) for every block destination j
@@ -147,6 +147,11 @@ __device__ __forceinline__ void signal_done(const DecodeParams& p) {
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -524,6 +529,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int blk = 0;
       const int64_t prow = hl < p.cta_heads ? part_row(head0 + hl, blk) : 0;
       const int64_t po = prow * 512 + 256 * half;  // element offset of this thread's half row
+      const float inv_l = l_tot > 0.f ? 1.f / l_tot : 0.f;
 #pragma unroll 1
       for (int c = 0; c < 8; c++) {
         float v[32];
@@ -531,13 +537,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         const int64_t e = po + (c >> 2) * 128 + (c & 3) * 32;
         if (hl < p.cta_heads) {
-          if (p.part_bf16) {  // unnormalised O rounded to bf16 (halves the exchange)
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.blk_o[blk]) + e);
+          if (p.part_f16) {  // O / l in fp16: half the bytes, 2^-11 relative error
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.blk_o[blk]) + e);
 #pragma unroll
             for (int i = 0; i < 4; i++)
-              dst[i] = make_uint4(pack_bf16(v[8 * i], v[8 * i + 1]), pack_bf16(v[8 * i + 2], v[8 * i + 3]),
-                                  pack_bf16(v[8 * i + 4], v[8 * i + 5]),
-                                  pack_bf16(v[8 * i + 6], v[8 * i + 7]));
+              dst[i] = make_uint4(pack_f16(v[8 * i] * inv_l, v[8 * i + 1] * inv_l),
+                                  pack_f16(v[8 * i + 2] * inv_l, v[8 * i + 3] * inv_l),
+                                  pack_f16(v[8 * i + 4] * inv_l, v[8 * i + 5] * inv_l),
+                                  pack_f16(v[8 * i + 6] * inv_l, v[8 * i + 7] * inv_l));
           } else {
             float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.blk_o[blk]) + e);
 #pragma unroll
@@ -656,12 +663,12 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
       p.blk_ml[j] = a.peer_ml[j];
       p.flag[j] = a.peer_flag[j];
     } else if (a.part_o) {
-      p.blk_o[j] = reinterpret_cast<uint8_t*>(a.part_o) + j * blk_rows * 512 * (a.part_bf16 ? 2 : 4);
+      p.blk_o[j] = reinterpret_cast<uint8_t*>(a.part_o) + j * blk_rows * 512 * (a.part_f16 ? 2 : 4);
       p.blk_ml[j] = a.part_ml + j * blk_rows * 2;
     }
   }
   p.counter = a.peer ? a.done_counter : nullptr;
-  p.part_bf16 = a.part_bf16;
+  p.part_f16 = a.part_f16;
   p.epoch = a.epoch;
   // one split and no partial buffers: the epilogue normalises and writes o
   p.direct = (a.splits == 1 && a.part_o == nullptr && !a.peer) ? 1 : 0;

@@ -441,14 +441,15 @@ __global__ void attn_combine_kernel(AttnArgs p) {
     for (int i = 0; i < p.splits; i++) {
       const float mi = ml[i * ml_stride];
       if (mi == -INFINITY) continue;
-      const float w = exp2f(mi - M);
       const int64_t e = po0 + i * po_stride + c;
       float4 v;
-      if (p.part_bf16) {
-        const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(p.part_o) + e);
-        const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
-        const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+      float w = exp2f(mi - M);
+      if (p.part_f16) {  // O / l: weighted by l
+        const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(p.part_o) + e);
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
         v = make_float4(lo.x, lo.y, hi.x, hi.y);
+        w *= ml[i * ml_stride + 1];
       } else {
         v = *reinterpret_cast<const float4*>(p.part_o + e);
       }

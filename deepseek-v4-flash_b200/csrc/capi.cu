@@ -157,9 +157,14 @@ int run_decode_attn(AttnArgs a, void* ws, cudaStream_t st) {
   a.splits = sm100 ? sm100_splits(rows, a.h, a.max_len) : general_splits(rows, a.h, a.max_len);
   const bool partials = a.splits > 1;
   if (partials) {
+    // the pair kernel keeps its O partials as O / l in fp16 (half the bytes
+    // written and merged; the workspace is sized for fp32, the general
+    // kernel's format)
+    a.part_f16 = sm100 ? 1 : 0;
     a.part_o = reinterpret_cast<float*>(ws);
-    a.part_ml = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) +
-                                         align256((size_t)rows * a.splits * a.h * a.d_v * 4));
+    a.part_ml = reinterpret_cast<float*>(
+        reinterpret_cast<uint8_t*>(ws) +
+        align256((size_t)rows * a.splits * a.h * a.d_v * (a.part_f16 ? 2 : 4)));
   }
   if (sm100) {
     QCAU_CHECK_CUDA(launch_decode_attn_sm100(a, st));
@@ -775,7 +780,7 @@ int qcau_decode_attn_paged_cp(const void* q_all, const void* cache, const int32_
                               int64_t h, int64_t n_ranks, int64_t rank, int64_t d_qk, int64_t d_v,
                               int64_t d_kv, int64_t page_size, int64_t max_pages,
                               int64_t num_pages, int64_t max_seqlen, float softmax_scale,
-                              int32_t part_bf16, void* stream) {
+                              int32_t part_f16, void* stream) {
   QCAU_CHECK_ARG(q_all && cache && block_table && seqlens && part_o && part_ml,
                  "decode_attn_paged_cp: NULL pointer");
   QCAU_CHECK_ARG(b >= 0 && h > 0 && page_size > 0 && max_pages > 0 && num_pages > 0,
@@ -805,7 +810,7 @@ int qcau_decode_attn_paged_cp(const void* q_all, const void* cache, const int32_
   a.part_hblock = h / n_ranks;
   a.part_o = reinterpret_cast<float*>(part_o);
   a.part_ml = part_ml;
-  a.part_bf16 = part_bf16 ? 1 : 0;
+  a.part_f16 = part_f16 ? 1 : 0;
   if (!decode_attn_sm100_supported(a))
     return fail(QCAU_ERR_UNSUPPORTED,
                 "decode_attn_paged_cp: needs the sm_100a pair kernel (d_qk 576, d_v 512, page 64, "
@@ -822,7 +827,7 @@ int qcau_decode_attn_paged_cp_p2p(const void* q_all, const void* cache,
                                   uint32_t* done_counter, int64_t b, int64_t h, int64_t n_ranks,
                                   int64_t rank, int64_t d_qk, int64_t d_v, int64_t d_kv,
                                   int64_t page_size, int64_t max_pages, int64_t num_pages,
-                                  int64_t max_seqlen, float softmax_scale, int32_t part_bf16,
+                                  int64_t max_seqlen, float softmax_scale, int32_t part_f16,
                                   void* stream) {
   QCAU_CHECK_ARG(q_all && cache && block_table && seqlens && dst_o && dst_ml && dst_flag &&
                      done_counter,
@@ -863,7 +868,7 @@ int qcau_decode_attn_paged_cp_p2p(const void* q_all, const void* cache,
   }
   a.done_counter = done_counter;
   a.epoch = epoch;
-  a.part_bf16 = part_bf16 ? 1 : 0;
+  a.part_f16 = part_f16 ? 1 : 0;
   if (!decode_attn_sm100_supported(a))
     return fail(QCAU_ERR_UNSUPPORTED,
                 "decode_attn_paged_cp_p2p: needs the sm_100a pair kernel (d_qk 576, d_v 512, "
@@ -918,13 +923,13 @@ int qcau_ipc_free(void* ptr) {
 
 int qcau_attn_combine_ranks(const void* part_o, const float* part_ml, const float* attn_sink,
                             void* o, int64_t b, int64_t h_local, int64_t n_ranks, int64_t d_v,
-                            int32_t part_bf16, void* stream) {
+                            int32_t part_f16, void* stream) {
   QCAU_CHECK_ARG(part_o && part_ml && o, "attn_combine_ranks: NULL pointer");
   QCAU_CHECK_ARG(b >= 0 && h_local > 0 && n_ranks >= 1 && d_v > 0 && d_v % 128 == 0,
                  "attn_combine_ranks: bad shape");
   AttnArgs a{};
   a.part_o = const_cast<float*>(reinterpret_cast<const float*>(part_o));
-  a.part_bf16 = part_bf16 ? 1 : 0;
+  a.part_f16 = part_f16 ? 1 : 0;
   a.part_ml = const_cast<float*>(part_ml);
   a.sink = attn_sink;
   a.o = o;

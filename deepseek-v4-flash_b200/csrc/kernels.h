@@ -99,9 +99,10 @@ struct AttnArgs {
   int64_t part_hblock;
   // combine: partials are [splits][rows][h] (1) instead of [rows][splits][h]
   int part_split_major;
-  // the O partials (part_o / peer_o) are bf16 instead of fp32 (pair kernel
-  // writes, combine reads); the (max, sum) partials stay fp32
-  int part_bf16;
+  // the O partials (part_o / peer_o) are O / sum in fp16 instead of
+  // unnormalised O in fp32 (pair kernel writes, combine reads); the (max,
+  // sum) partials stay fp32
+  int part_f16;
   // Partials of head block j written straight into the receive slot of the
   // rank that owns it (peer memory), when peer != 0: peer_o[j] / peer_ml[j]
   // are [rows][splits][part_hblock] x d_v / x 2; the last CTA of the grid to

@@ -254,10 +254,11 @@ class MLADecodeLayer:
                 "B": B,
                 "q_local": torch.empty(B, Hl, w, device=dev, dtype=bf16),
                 "q_all": torch.empty(N, B, Hl, w, device=dev, dtype=bf16),
-                # unnormalised O partials in bf16 (half the bytes to exchange)
-                "part_o": torch.empty(N, B, Hl, c.kv_lora, device=dev, dtype=bf16),
+                # O partials normalised by their sum, in fp16 (half the bytes
+                # to exchange, 2^-11 relative error)
+                "part_o": torch.empty(N, B, Hl, c.kv_lora, device=dev, dtype=torch.float16),
                 "part_ml": torch.empty(N, B, Hl, 2, device=dev, dtype=f32),
-                "recv_o": torch.empty(N, B, Hl, c.kv_lora, device=dev, dtype=bf16),
+                "recv_o": torch.empty(N, B, Hl, c.kv_lora, device=dev, dtype=torch.float16),
                 "recv_ml": torch.empty(N, B, Hl, 2, device=dev, dtype=f32),
                 "o_lat": torch.empty(B, Hl, c.kv_lora, device=dev, dtype=bf16),
             }
@@ -379,7 +380,7 @@ class PeerExchange:
     """Receive areas of the fused partial exchange, shared over CUDA IPC.
 
     This rank's buffer (in its own GPU memory) holds two areas, used by
-    alternate steps, each [N_src, B, h/N, 512] bf16 (o) and [N_src, B, h/N, 2]
+    alternate steps, each [N_src, B, h/N, 512] fp16 (O / sum) and [N_src, B, h/N, 2]
     fp32 (max in log2 units, sum), then one flag word per source rank.  Every
     rank opens every peer's buffer; `destinations(parity)` gives the pointers
     where this rank's partials for rank j go (its slot in rank j's area) and
@@ -391,7 +392,7 @@ class PeerExchange:
         import ctypes
         self.device, self.rank, self.N, self.B = device, rank, world_size, batch
         align = lambda x: (x + 255) // 256 * 256   # noqa: E731
-        self.slot_o = batch * heads_local * d_v * 2       # one source's o partials (bf16)
+        self.slot_o = batch * heads_local * d_v * 2       # one source's o partials (fp16)
         self.slot_ml = batch * heads_local * 2 * 4
         self.area_o_bytes = align(world_size * self.slot_o)
         self.area_ml_bytes = align(world_size * self.slot_ml)

@@ -314,17 +314,18 @@ int qcau_mla_decode(const qcau_mla_dims* dims, const void* q_lora,
  *   (caller)            all-gather -> q_all [N, b, h/N, 576]
  *   decode_attn_paged_cp   all h heads over tiles [ntiles*r/N, ntiles*(r+1)/N)
  *                       of every sequence (ntiles = ceil(seqlen/128)) ->
- *                       partials [N, b, h/N, 512] (fp32, or bf16 with
- *                       part_bf16 = 1: half the bytes to exchange) and
- *                       [N, b, h/N, 2] fp32, block j holding the heads of
- *                       rank j
+ *                       partials [N, b, h/N, 512] (unnormalised O in
+ *                       fp32, or with part_f16 = 1 O / sum in fp16: half
+ *                       the bytes to exchange) and [N, b, h/N, 2] fp32
+ *                       (max in log2 units, sum), block j holding the heads
+ *                       of rank j
  *   (caller)            all-to-all of the blocks -> [N, b, h/N, ...] by source
  *   attn_combine_ranks  o_lat [b, h/N, 512] bf16 (sink optional)
  *   mla_decode_out      y [b, dim] (row-parallel partial)
  *   (caller)            all-reduce of y
  * Every stage takes qcau_mla_dims with n_heads = h/N (the rank's heads) and
  * the workspace of qcau_mla_decode_workspace_size.  The partials hold
- * unnormalised sums with (max in log2 units, sum) as the split-KV path does;
+ * (O, max in log2 units, sum) as the split-KV path does;
  * decode_attn_paged_cp needs the sm_100a pair kernel (d_qk 576, d_v 512,
  * page 64, h a multiple of 128, h/N a multiple of 64 or one of 8, 16, 32)
  * and returns QCAU_ERR_UNSUPPORTED otherwise.
@@ -339,10 +340,10 @@ int qcau_decode_attn_paged_cp(const void* q_all, const void* cache,
                               int64_t n_ranks, int64_t rank, int64_t d_qk, int64_t d_v,
                               int64_t d_kv, int64_t page_size, int64_t max_pages,
                               int64_t num_pages, int64_t max_seqlen, float softmax_scale,
-                              int32_t part_bf16, void* stream);
+                              int32_t part_f16, void* stream);
 int qcau_attn_combine_ranks(const void* part_o, const float* part_ml, const float* attn_sink,
                             void* o, int64_t b, int64_t h_local, int64_t n_ranks, int64_t d_v,
-                            int32_t part_bf16, void* stream);
+                            int32_t part_f16, void* stream);
 int qcau_mla_decode_out(const qcau_mla_dims* dims, const void* o_lat, const void* wkv_b_bf16,
                         const void* wo, const void* wo_scale, void* y, void* workspace,
                         size_t workspace_bytes, void* stream);
@@ -355,7 +356,7 @@ int qcau_mla_decode_out(const qcau_mla_dims* dims, const void* o_lat, const void
  * caller; ipc_open maps a peer's buffer, with peer access over NVLink).
  * decode_attn_paged_cp_p2p computes what decode_attn_paged_cp does, but
  * writes the partials of head block j (the heads of rank j) straight into
- * rank j's buffer: dst_o[j] -> [b, h/N, d_v] (fp32, or bf16 with part_bf16)
+ * rank j's buffer: dst_o[j] -> [b, h/N, d_v] (fp32, or fp16 with part_f16)
  * and dst_ml[j] ->
  * [b, h/N, 2], this rank's slot of rank j's [N_src, b, h/N, ...] receive
  * area.  The last CTA to finish then stores `epoch` to dst_flag[j] (this
@@ -382,7 +383,7 @@ int qcau_decode_attn_paged_cp_p2p(const void* q_all, const void* cache,
                                   uint32_t* done_counter, int64_t b, int64_t h, int64_t n_ranks,
                                   int64_t rank, int64_t d_qk, int64_t d_v, int64_t d_kv,
                                   int64_t page_size, int64_t max_pages, int64_t num_pages,
-                                  int64_t max_seqlen, float softmax_scale, int32_t part_bf16,
+                                  int64_t max_seqlen, float softmax_scale, int32_t part_f16,
                                   void* stream);
 int qcau_wait_flags(const uint32_t* flags, int64_t n, uint32_t epoch, void* stream);
 

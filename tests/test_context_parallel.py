@@ -29,6 +29,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle as O
+from helpers import assert_close_attn
 from qcau_b200 import _lib
 from qcau_b200.mla import (MLAConfig, MLADecodeLayer, make_paged_cache, precompute_freqs_cis,
                            quantize_weight_fp8, shard_weights)
@@ -103,9 +104,10 @@ def _oracle_layer(weights, q_lora, cache, table, seqlens, positions, freqs) -> n
 def rank_partials(q_all, cache, table, seqlens, rank, n, scale):
     """The context-parallel attention stage restated: all heads over rank
     `rank`'s tiles [ntiles*rank/n, ntiles*(rank+1)/n) of each sequence
-    (ntiles = ceil(seqlen/128)); partials [n, B, h/n, 512] and [n, B, h/n, 2]
-    with block j holding the heads of rank j, P rounded to bf16 for P.V and
-    the sum over the unrounded P (the kernel's numerics)."""
+    (ntiles = ceil(seqlen/128)); partials [n, B, h/n, 512] (O divided by its
+    sum) and [n, B, h/n, 2] (max in log2 units, sum) with block j holding the
+    heads of rank j, P rounded to bf16 for P.V and the sum over the unrounded
+    P (the kernel's numerics)."""
     qa = O.bf16_to_f32(q_all)                       # [n, B, hl, 576]
     nb, bsz, hl, w = qa.shape
     q = qa.transpose(1, 0, 2, 3).reshape(bsz, nb * hl, w)
@@ -123,7 +125,7 @@ def rank_partials(q_all, cache, table, seqlens, rank, n, scale):
             m = x.max(1)
             p = np.exp2(x - m[:, None]).astype(np.float32)
             l = p.sum(1)
-            o = O.bf16_to_f32(O.f32_to_bf16(p)) @ rows[:, :512]
+            o = (O.bf16_to_f32(O.f32_to_bf16(p)) @ rows[:, :512]) / l[:, None]
         else:
             m = np.full(nb * hl, -np.inf, np.float32)
             l = np.zeros(nb * hl, np.float32)
@@ -135,12 +137,12 @@ def rank_partials(q_all, cache, table, seqlens, rank, n, scale):
 
 
 def merge_partials(recv_o, recv_ml) -> np.ndarray:
-    """o [B, h/n, 512] bf16 (uint16) from [n, B, h/n, ...] partials."""
+    """o [B, h/n, 512] bf16 (uint16) from [n, B, h/n, ...] partials (O / sum)."""
     m = recv_ml[..., 0]
     M = m.max(0)
     wgt = np.where(np.isneginf(m), 0.0, np.exp2(m - np.where(np.isneginf(M), 0.0, M)))
     L = (recv_ml[..., 1] * wgt).sum(0)
-    o = (recv_o * wgt[..., None]).sum(0) / np.maximum(L, 1e-38)[..., None]
+    o = (recv_o * (wgt * recv_ml[..., 1])[..., None]).sum(0) / np.maximum(L, 1e-38)[..., None]
     return O.f32_to_bf16(o.astype(np.float32))
 
 
@@ -213,8 +215,8 @@ def test_context_parallel_layer_over_gloo_equals_unsharded(tmp_path):
     rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
     for r in range(world_size):
         y = np.load(tmp_path / f"y{r}.npy")
-        # P is rounded to bf16 against each rank's own maximum and the O
-        # partials are exchanged in bf16: bf16 noise in o_lat, which the FP8
+        # P is rounded to bf16 against each rank's own maximum (and the O
+        # partials are exchanged in fp16): bf16 noise in o_lat, which the FP8
         # act_quant of o_v (one e4m3 step is 1/8) can turn into a code flip of
         # single elements; a wrong block or tile order would break the cosine
         _assert_layer_close(y, ref, f"rank {r}")
@@ -275,8 +277,8 @@ def _assert_layer_close(y: np.ndarray, ref: np.ndarray, what: str):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("n,bf16", [(1, 1), (2, 1), (4, 0), (4, 1), (8, 1)])
-def test_cp_attention_emulated_ranks_match_decode(n, bf16):
+@pytest.mark.parametrize("n,f16", [(1, 1), (2, 1), (4, 0), (4, 1), (8, 1)])
+def test_cp_attention_emulated_ranks_match_decode(n, f16):
     """N ranks of qcau_decode_attn_paged_cp on one device, the block exchange
     done by indexing, merged by qcau_attn_combine_ranks, equal the
     single-rank qcau_decode_attn_paged (ragged lengths, an empty sequence,
@@ -300,7 +302,7 @@ def test_cp_attention_emulated_ranks_match_decode(n, bf16):
                                         ws.data_ptr(), need, st), "decode")
     hl = H // n
     q_all = q.view(bsz, n, hl, WIDTH).transpose(0, 1).contiguous()
-    odt = torch.bfloat16 if bf16 else torch.float32
+    odt = torch.float16 if f16 else torch.float32
     part_o = torch.empty(n, n, bsz, hl, 512, device=dev, dtype=odt)   # [rank][dest] ...
     part_ml = torch.empty(n, n, bsz, hl, 2, device=dev)
     for r in range(n):
@@ -308,22 +310,23 @@ def test_cp_attention_emulated_ranks_match_decode(n, bf16):
                                                table.data_ptr(), seqlens.data_ptr(),
                                                part_o[r].data_ptr(), part_ml[r].data_ptr(), bsz,
                                                H, n, r, WIDTH, 512, WIDTH, PAGE, table.size(1),
-                                               cache.size(0), ctx, scale, bf16, st), "cp")
+                                               cache.size(0), ctx, scale, f16, st), "cp")
     outs = []
     for dst in range(n):
         recv_o = part_o[:, dst].contiguous()
         recv_ml = part_ml[:, dst].contiguous()
         o = torch.empty(bsz, hl, 512, device=dev, dtype=torch.bfloat16)
         _lib.check(L.qcau_attn_combine_ranks(recv_o.data_ptr(), recv_ml.data_ptr(), None,
-                                             o.data_ptr(), bsz, hl, n, 512, bf16, st), "combine")
+                                             o.data_ptr(), bsz, hl, n, 512, f16, st), "combine")
         outs.append(o)
     got = torch.cat(outs, dim=1)
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
     a, b = got.float(), ref.float()
     assert torch.all(a[1] == 0), "an empty sequence gives zeros"
-    rms = b.pow(2).mean().sqrt().item()
-    assert (a - b).abs().max().item() <= 2e-2 * rms
+    # the path's bar (max(2e-2 * rms, 1 bf16 ulp)): the two merge orders round
+    # differently at large outputs
+    assert_close_attn(a.cpu().numpy(), b.cpu().numpy(), f"cp {n} ranks")
     cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
     assert cos >= 0.9999
 
@@ -356,7 +359,7 @@ def test_cp_p2p_kernel_emulated_ranks(n):
     hl = H // n
     q_all = q.view(bsz, n, hl, WIDTH).transpose(0, 1).contiguous()
     recv_o = torch.full((n, n, bsz, hl, 512), float("nan"), device=dev,
-                        dtype=torch.bfloat16)   # [owner][src] ...
+                        dtype=torch.float16)   # [owner][src] ...
     recv_ml = torch.full((n, n, bsz, hl, 2), float("nan"), device=dev)
     flags = torch.zeros(n, n, device=dev, dtype=torch.int32)                # [owner][src]
     counter = torch.zeros(1, device=dev, dtype=torch.int32)
@@ -385,8 +388,7 @@ def test_cp_p2p_kernel_emulated_ranks(n):
     assert int(counter.item()) == 0
     assert not torch.isnan(recv_ml).any(), "every slot was written"
     a, b = got.float(), ref.float()
-    rms = b.pow(2).mean().sqrt().item()
-    assert (a - b).abs().max().item() <= 2e-2 * rms
+    assert_close_attn(a.cpu().numpy(), b.cpu().numpy(), f"cp p2p {n} ranks")
     assert torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item() >= 0.9999
 
 
