@@ -1,7 +1,6 @@
 """GPU parity of the sm_100a kernels against the oracle and the reference's
 golden vectors.  Every call goes through the C ABI of libqcau_b200.so (via the
 qcau_b200 drop-ins).  Tolerances are those of tests/helpers.py."""
-import ctypes
 
 import numpy as np
 import pytest
