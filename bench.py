@@ -343,10 +343,10 @@ def main():
                     help="time the causal prefill attention, batch 4 x 4096 x 128 heads")
     ap.add_argument("--sparse-fp8-only", type=int, default=0, metavar="HEADS",
                     help="time the FP8-cache top-k sparse decode (batch 64, 131072 rows) at HEADS")
-    ap.add_argument("--attn-split", default="context", choices=["context", "heads"],
+    ap.add_argument("--attn-split", default="context", choices=["context", "rows", "heads"],
                     help="N > 1: split the attention of the head-sharded layer by context "
-                         "(each rank streams 1/N of the cache) or by heads (each rank "
-                         "streams all of it)")
+                         "(each rank 1/N of every sequence), by rows (each rank 1/N of the "
+                         "sequences) or by heads (each rank streams the whole cache)")
     ap.add_argument("--exchange", default="nccl", choices=["nccl", "p2p"],
                     help="context split: partial states exchanged by an NCCL all-to-all, or "
                          "stored by the attention kernel into the owning rank's memory")
@@ -384,6 +384,7 @@ def main():
     layer = MLADecodeLayer(cfg, dev, rank=rank, world_size=ws, attn_split=args.attn_split,
                            exchange=args.exchange)
     cp = ws > 1 and args.attn_split == "context"
+    rs = ws > 1 and args.attn_split == "rows"
     layer.random_weights(seed=0)
     cache, table, seqlens = make_paged_cache(BATCH, CTX, PAGE, WIDTH, dev, seed=0)
     positions = seqlens.clone()
@@ -443,6 +444,22 @@ def main():
                 part_o.data_ptr(), part_ml.data_ptr(), BATCH, HEADS, ws, rank, WIDTH, 512, WIDTH,
                 PAGE, table.size(1), cache.size(0), CTX, cfg.softmax_scale, 1,
                 _lib.stream_ptr(dev)), "attn_cp")
+    elif rs:
+        # this rank's sequences with all heads, q and o in the owners' head blocks
+        Br = BATCH // ws
+        q_rows = torch.randn(ws, Br, H, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
+        o_rows = torch.empty(ws, Br, H, 512, device=dev, dtype=torch.bfloat16)
+        need = L.qcau_decode_attn_workspace_size(Br, HEADS, 512, CTX)
+        wsb = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+        t_rows = table[rank * Br:(rank + 1) * Br]
+        s_rows = seqlens[rank * Br:(rank + 1) * Br]
+
+        def attn():
+            _lib.check(L.qcau_decode_attn_paged_blocked(
+                q_rows.data_ptr(), H, cache.data_ptr(), t_rows.data_ptr(), s_rows.data_ptr(),
+                None, o_rows.data_ptr(), H, Br, HEADS, WIDTH, 512, WIDTH, PAGE, table.size(1),
+                cache.size(0), CTX, cfg.softmax_scale, wsb.data_ptr(), need,
+                _lib.stream_ptr(dev)), "attn_rows")
     else:
         q_abs = torch.randn(BATCH, H, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
         o_lat = torch.empty(BATCH, H, 512, device=dev, dtype=torch.bfloat16)
@@ -477,6 +494,10 @@ def main():
         attn_bytes = (cache_bytes + table.numel() * 4) // ws + BATCH * HEADS * WIDTH * 2 + \
             BATCH * HEADS * (512 * 2 + 2 * 4)
         attn_flops = 2.0 * BATCH * (CTX // ws) * HEADS * (WIDTH + 512)
+    elif rs:
+        # the pages, q and o of 1/N of the sequences, all heads
+        attn_bytes = (cache_bytes + table.numel() * 4 + BATCH * HEADS * (WIDTH + 512) * 2) // ws
+        attn_flops = 2.0 * (BATCH // ws) * CTX * HEADS * (WIDTH + 512)
     else:
         attn_bytes = cache_bytes + BATCH * H * (WIDTH + 512) * 2 + table.numel() * 4
         attn_flops = 2.0 * BATCH * CTX * H * (WIDTH + 512)
@@ -491,7 +512,12 @@ def main():
                 "peak": tflops, "unit": "TFLOP/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
     traffic = traffic_from_profiles()
-    if cp:
+    if rs:
+        roof["traffic"] = traffic * attn_bytes / full_bytes if traffic else None
+        roof["traffic_note"] = "scaled from the 1-GPU full-launch capture by algorithmic bytes"
+        roof["kernel"] = ("decode attention of this rank's 1/N of the sequences, all heads "
+                          "(split-KV + combine); per launch")
+    elif cp:
         # the one-GPU capture's DRAM bytes per algorithmic byte, applied to this launch
         roof["traffic"] = traffic * attn_bytes / full_bytes if traffic else None
         roof["traffic_note"] = "scaled from the 1-GPU full-launch capture by algorithmic bytes"
@@ -569,7 +595,9 @@ def main():
                        "global_batch": BATCH, "seq_len": CTX, "heads_per_rank": H,
                        "parallelism": (f"head-shard tp{ws}, attention split by context "
                                        f"(q all-gather, partial exchange: {args.exchange})"
-                                       if cp else f"head-shard tp{ws}"),
+                                       if cp else
+                                       f"head-shard tp{ws}, attention split by sequences "
+                                       "(q and o all-to-all)" if rs else f"head-shard tp{ws}"),
                        "l2": "inputs (4.83 GB cache) larger than L2; no flush"},
             "roofline": roof,
             "e2e": {"value": e2e_val, "unit": "tok/s",

@@ -116,6 +116,8 @@ struct DecodeParams {
   int split_base, splits_total;
   int part_hblock;
   int nblk;
+  int o_hblock;   // direct mode: o as [h / o_hblock][rows][o_hblock][512]
+  int64_t rows;
   void* blk_o[kMaxBlocks];     // fp32 O, or fp16 O / l when part_f16
   int part_f16;
   float* blk_ml[kMaxBlocks];
@@ -202,11 +204,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     return ((int64_t)b * p.splits + split) * p.part_hblock + (head - blk * p.part_hblock);
   };
 
+  // direct-mode output row of (row b, head)
+  auto out_row = [&](int head) -> __nv_bfloat16* {
+    const int blk = head / p.o_hblock;
+    return p.out + (((int64_t)blk * p.rows + b) * p.o_hblock + (head - blk * p.o_hblock)) * 512;
+  };
+
   if (T <= 0) {  // both CTAs of the pair take this branch together
     if (p.direct) {  // no visible token: the output rows are zero
-      uint4* o4 = reinterpret_cast<uint4*>(p.out + (b * p.h + head0) * 512);
       for (int i = threadIdx.x; i < p.cta_heads * 64; i += blockDim.x)
-        o4[i] = make_uint4(0u, 0u, 0u, 0u);
+        reinterpret_cast<uint4*>(out_row(head0 + (i >> 6)))[i & 63] = make_uint4(0u, 0u, 0u, 0u);
       return;
     }
     for (int i = threadIdx.x; i < p.cta_heads; i += blockDim.x) {
@@ -507,7 +514,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       else
         den = l_tot + ((p.sink && hl < p.cta_heads && isfinite(p.sink[head0 + hl])) ? 1.f : 0.f);
       const float inv = 1.f / fmaxf(den, 1.17549435e-38f);
-      __nv_bfloat16* po = p.out + (b * p.h + head0 + hl) * 512 + 256 * half;
+      __nv_bfloat16* po = out_row(head0 + hl) + 256 * half;
 #pragma unroll 1
       for (int c = 0; c < 8; c++) {
         float v[32];
@@ -586,7 +593,8 @@ bool decode_attn_sm100_supported(const AttnArgs& a) {
   // multiples of 64 that divide h (the 1024-byte swizzle atom is 8 rows)
   const int64_t qhb = a.q_hblock > 0 ? a.q_hblock : a.h;
   const bool qblocks = qhb == a.h || (a.h % qhb == 0 && (qhb % 64 == 0 || (64 % qhb == 0 && qhb >= 8)));
-  const bool parts = (a.part_hblock <= 0 || a.h % a.part_hblock == 0) &&
+  const bool parts = (a.o_hblock <= 0 || a.h % a.o_hblock == 0) &&
+                     (a.part_hblock <= 0 || a.h % a.part_hblock == 0) &&
                      a.h / (a.part_hblock > 0 ? a.part_hblock : a.h) <= kMaxBlocks &&
                      (!a.peer || a.done_counter != nullptr);
   const bool ranges = a.splits_total <= 0 ||
@@ -669,6 +677,8 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   }
   p.counter = a.peer ? a.done_counter : nullptr;
   p.part_f16 = a.part_f16;
+  p.o_hblock = a.o_hblock > 0 ? (int)a.o_hblock : (int)a.h;
+  p.rows = rows;
   p.epoch = a.epoch;
   // one split and no partial buffers: the epilogue normalises and writes o
   p.direct = (a.splits == 1 && a.part_o == nullptr && !a.peer) ? 1 : 0;

@@ -433,7 +433,10 @@ __global__ void attn_combine_kernel(AttnArgs p) {
   else
     L += (p.sink && isfinite(p.sink[hh])) ? 1.f : 0.f;
   const float inv = 1.f / fmaxf(L, 1.17549435e-38f);
-  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.o) + (qrow * p.h + hh) * p.d_v;
+  const int64_t ob = p.o_hblock > 0 ? p.o_hblock : p.h;  // o in head blocks of ob
+  const int64_t oblk = hh / ob;
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.o) +
+                       ((oblk * rows + qrow) * ob + (hh - oblk * ob)) * p.d_v;
   const int64_t po0 = prow0 * p.d_v;
   const int64_t po_stride = pstride * p.d_v;
   for (int c = lane * 4; c < p.d_v; c += 128) {

@@ -414,6 +414,51 @@ int qcau_decode_attn_paged(const void* q, const void* cache, const int32_t* bloc
   return run_decode_attn(a, workspace, to_stream(stream));
 }
 
+int qcau_decode_attn_paged_blocked(const void* q, int64_t q_hblock, const void* cache,
+                                   const int32_t* block_table, const int32_t* seqlens,
+                                   const float* attn_sink, void* o, int64_t o_hblock, int64_t b,
+                                   int64_t h, int64_t d_qk, int64_t d_v, int64_t d_kv,
+                                   int64_t page_size, int64_t max_pages, int64_t num_pages,
+                                   int64_t max_seqlen, float softmax_scale, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  QCAU_CHECK_ARG(q && cache && block_table && seqlens && o,
+                 "decode_attn_paged_blocked: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && h > 0 && page_size > 0 && max_pages > 0 && num_pages > 0,
+                 "decode_attn_paged_blocked: bad shape");
+  QCAU_CHECK_ARG(q_hblock > 0 && o_hblock > 0 && h % q_hblock == 0 && h % o_hblock == 0,
+                 "decode_attn_paged_blocked: head blocks must divide h");
+  QCAU_CHECK_ARG(max_seqlen >= 0 && max_seqlen <= max_pages * page_size,
+                 "decode_attn_paged_blocked: max_seqlen exceeds the block table");
+  int rc = check_attn_widths(d_qk, d_v, d_kv, "decode_attn_paged_blocked");
+  if (rc) return rc;
+  const size_t need = qcau_decode_attn_workspace_size(b, h, d_v, max_seqlen);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(QCAU_ERR_WORKSPACE, "decode_attn_paged_blocked: workspace too small (need " +
+                                        std::to_string(need) + " bytes)");
+  AttnArgs a{};
+  a.q = q;
+  a.q_row_stride = d_qk;
+  a.q_hblock = q_hblock;
+  a.kv = cache;
+  a.block_table = block_table;
+  a.seqlens = seqlens;
+  a.sink = attn_sink;
+  a.o = o;
+  a.o_hblock = o_hblock;
+  a.b = b; a.s = 1; a.h = h; a.d_qk = d_qk; a.d_v = d_v; a.d_kv = d_kv;
+  a.page_size = page_size;
+  a.max_pages = max_pages;
+  a.num_pages = num_pages;
+  a.max_len = max_seqlen;
+  a.scale = softmax_scale;
+  if (!decode_attn_sm100_supported(a))
+    return fail(QCAU_ERR_UNSUPPORTED,
+                "decode_attn_paged_blocked: needs the sm_100a pair kernel (d_qk 576, d_v 512, "
+                "page 64, h a multiple of 128, head blocks a multiple of 64 or 8, 16 or 32)");
+  if (b == 0) return QCAU_OK;
+  return run_decode_attn(a, workspace, to_stream(stream));
+}
+
 size_t qcau_sparse_attn_fp8_workspace_size(int64_t b, int64_t s, int64_t h, int64_t topk) {
   return attn_ws_bytes(b * s, h, 512, general_splits(b * s, h, topk));
 }

@@ -99,6 +99,9 @@ struct AttnArgs {
   int64_t part_hblock;
   // combine: partials are [splits][rows][h] (1) instead of [rows][splits][h]
   int part_split_major;
+  // o as [h / o_hblock][rows][o_hblock][d_v] (the head owners' blocks) when
+  // o_hblock > 0 (pair kernel's direct epilogue and the combine)
+  int64_t o_hblock;
   // the O partials (part_o / peer_o) are O / sum in fp16 instead of
   // unnormalised O in fp32 (pair kernel writes, combine reads); the (max,
   // sum) partials stay fp32

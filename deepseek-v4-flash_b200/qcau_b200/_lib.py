@@ -73,6 +73,9 @@ SIGNATURES = {
     "qcau_prefill_attn_workspace_size": ([_I64, _I64, _I64, _I64, _I64], _SZ),
     "qcau_prefill_attn_paged": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
                                  _I64, _I64, _I64, _I64, _F, _P, _SZ, _P], ctypes.c_int),
+    "qcau_decode_attn_paged_blocked": ([_P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
+                                        _I64, _I64, _I64, _I64, _I64, _I64, _F, _P, _SZ, _P],
+                                       ctypes.c_int),
     "qcau_decode_attn_paged_noalloc": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
                                         _I64, _I64, _I64, _I64, _F, _P], ctypes.c_int),
     "qcau_dequant_fp8_weight": ([_P, _P, _I32, _P, _I64, _I64, _P], ctypes.c_int),

@@ -19,6 +19,12 @@ wo is row-parallel with an all-reduce of the partial outputs
   attn_split="heads"    each rank attends with its own heads over the whole
                         cache: every rank streams all of it, so the step time
                         barely falls with N;
+  attn_split="rows"     each rank attends with all heads over 1/N of the
+                        sequences: an all-to-all of the absorbed queries
+                        (B/N rows x h/N heads per pair of ranks) in, one of
+                        the bf16 outputs back; each rank streams the pages
+                        of its own sequences and nothing is merged across
+                        ranks;
   attn_split="context"  the ranks all-gather their absorbed queries, each
                         attends with all heads over 1/N of every sequence's
                         tiles, and an all-to-all brings each rank the
@@ -119,13 +125,14 @@ class MLADecodeLayer:
                  process_group=None, attn_split: str = "context", exchange: str = "nccl"):
         if cfg.n_heads % world_size:
             raise ValueError("n_heads must be divisible by the number of ranks")
-        if attn_split not in ("heads", "context"):
-            raise ValueError("attn_split must be 'heads' or 'context'")
+        if attn_split not in ("heads", "context", "rows"):
+            raise ValueError("attn_split must be 'heads', 'context' or 'rows'")
         if exchange not in ("p2p", "nccl"):
             raise ValueError("exchange must be 'p2p' or 'nccl'")
         self.attn_split = attn_split
         self.exchange = exchange
         self._cp = None
+        self._rows = None
         self._peer = None
         self.cfg = cfg
         self.device = torch.device(device)
@@ -239,10 +246,79 @@ class MLADecodeLayer:
         if self.world_size > 1 and self.attn_split == "context":
             return self.forward_context(q_lora, cache, block_table, seqlens, positions, freqs,
                                         max_seqlen, y)
+        if self.world_size > 1 and self.attn_split == "rows":
+            return self.forward_rows(q_lora, cache, block_table, seqlens, positions, freqs,
+                                     max_seqlen, y)
         y = self.forward_local(q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen, y)
         if self.world_size > 1:
             dist.all_reduce(y, group=self.group)
         return y
+
+    def _rows_buffers(self, B: int, max_seqlen: int):
+        """Stage buffers of the row-split step, kept across steps."""
+        N, Hl, c, dev = self.world_size, self.n_local, self.cfg, self.device
+        Br = B // N
+        need = lib().qcau_decode_attn_workspace_size(Br, c.n_heads, c.kv_lora, max_seqlen)
+        if self._rows is None or self._rows["B"] != B or self._rows["ws"].numel() < need:
+            w = c.kv_lora + c.d_rope
+            bf16 = torch.bfloat16
+            self._rows = {
+                "B": B,
+                "q_local": torch.empty(B, Hl, w, device=dev, dtype=bf16),
+                "q_rows": torch.empty(N, Br, Hl, w, device=dev, dtype=bf16),
+                "o_rows": torch.empty(N, Br, Hl, c.kv_lora, device=dev, dtype=bf16),
+                "o_lat": torch.empty(B, Hl, c.kv_lora, device=dev, dtype=bf16),
+                "ws": torch.empty(max(need, 1), device=dev, dtype=torch.uint8),
+            }
+        return self._rows
+
+    def forward_rows(self, q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen,
+                     y: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y [batch, dim] bf16 summed over the ranks, the attention split by sequences.
+
+        Rank r attends, with all heads, over sequences [r*B/N, (r+1)*B/N):
+        an all-to-all hands it their queries from every head owner, and a
+        second all-to-all hands each owner its heads' outputs for every
+        sequence.  With one rank the collectives are identities.
+        """
+        N, r = self.world_size, self.rank
+        B = q_lora.size(0)
+        if B % N:
+            raise ValueError("attn_split='rows' needs the batch divisible by the number of ranks")
+        Br = B // N
+        buf = self._rows_buffers(B, max_seqlen)
+        if y is None:
+            y = torch.empty(B, self.cfg.dim, device=self.device, dtype=torch.bfloat16)
+        d = self.dims(B, block_table.size(1), cache.size(0), max_seqlen, freqs.size(0))
+        self._q_stage(d, q_lora, positions, freqs, buf["q_local"])
+        q_rows = buf["q_local"].view(N, Br, *buf["q_local"].shape[1:])
+        if N > 1:   # block j of rank i: rows of rank j, heads of rank i
+            dist.all_to_all_single(buf["q_rows"], q_rows, group=self.group)
+            q_rows = buf["q_rows"]
+        rows = slice(r * Br, (r + 1) * Br)
+        self._rows_attn_stage(q_rows, cache, block_table[rows], seqlens[rows], max_seqlen,
+                              buf["o_rows"], buf["ws"])
+        o_lat = buf["o_rows"].view(B, *buf["o_lat"].shape[1:])
+        if N > 1:   # block j of rank i: heads of rank j, rows of rank i
+            dist.all_to_all_single(buf["o_lat"], buf["o_rows"], group=self.group)
+            o_lat = buf["o_lat"]
+        self._out_stage(d, o_lat, y)
+        if N > 1:
+            dist.all_reduce(y, group=self.group)
+        return y
+
+    def _rows_attn_stage(self, q_rows, cache, table_rows, seqlens_rows, max_seqlen, o_rows, ws):
+        """o_rows [N, B/N, h/N, 512]: all heads over this rank's sequences,
+        from q_rows [N, B/N, h/N, 576] (both in blocks of the heads' owners)."""
+        c = self.cfg
+        w = c.kv_lora + c.d_rope
+        Br = q_rows.size(1)
+        check(lib().qcau_decode_attn_paged_blocked(
+            q_rows.data_ptr(), self.n_local, cache.data_ptr(), table_rows.data_ptr(),
+            seqlens_rows.data_ptr(), None, o_rows.data_ptr(), self.n_local, Br, c.n_heads, w,
+            c.kv_lora, w, c.page_size, table_rows.size(1), cache.size(0), max_seqlen,
+            c.softmax_scale, ws.data_ptr(), ws.numel(), stream_ptr(self.device)),
+              "decode_attn_paged_blocked")
 
     def _cp_buffers(self, B: int):
         """Stage buffers of the context-parallel step, kept across steps."""

@@ -184,6 +184,25 @@ int qcau_decode_attn_paged(const void* q, const void* cache,
                            size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * decode_attn_paged_blocked -- decode_attn_paged with q and o in head blocks
+ * (no reference counterpart): q [h / q_hblock, b, q_hblock, d_qk] and o
+ * [h / o_hblock, b, o_hblock, d_v], the layouts in which head-sharded ranks
+ * hand each other the query and output rows of the sequences one rank
+ * attends (see the layer stages below).  Same workspace, kernels, split
+ * counts and results as decode_attn_paged; needs the sm_100a pair kernel
+ * (d_qk 576, d_v 512, page 64, h a multiple of 128, each head block a
+ * multiple of 64 or one of 8, 16, 32) and returns QCAU_ERR_UNSUPPORTED
+ * otherwise.
+ * ---------------------------------------------------------------------- */
+int qcau_decode_attn_paged_blocked(const void* q, int64_t q_hblock, const void* cache,
+                                   const int32_t* block_table, const int32_t* seqlens,
+                                   const float* attn_sink, void* o, int64_t o_hblock, int64_t b,
+                                   int64_t h, int64_t d_qk, int64_t d_v, int64_t d_kv,
+                                   int64_t page_size, int64_t max_pages, int64_t num_pages,
+                                   int64_t max_seqlen, float softmax_scale, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * sparse_attn_fp8 -- sparse_attn (kernel.py:355-368) over an FP8 latent
  * cache: top-k gather decode at long context with the latent part stored as
  * e4m3 codes and one fp32 scale per row, the rope part in bf16.  The

@@ -175,6 +175,15 @@ class OracleStagesLayer(MLADecodeLayer):
         part_o.copy_(torch.from_numpy(po))
         part_ml.copy_(torch.from_numpy(pml))
 
+    def _rows_attn_stage(self, q_rows, cache, table_rows, seqlens_rows, max_seqlen, o_rows, ws):
+        qa = _bf16(q_rows)                                   # [N, B/N, h/N, 576]
+        nb, br, hl, w = qa.shape
+        q = np.ascontiguousarray(qa.transpose(1, 0, 2, 3).reshape(br, nb * hl, w))
+        o = O.paged_decode_attn(q, _bf16(cache), table_rows.numpy(), seqlens_rows.numpy(), None,
+                                self.cfg.softmax_scale, 512)   # [B/N, h, 512]
+        ob = np.ascontiguousarray(o.reshape(br, nb, hl, 512).transpose(1, 0, 2, 3))
+        o_rows.copy_(torch.from_numpy(O.f32_to_bf16(ob).view(np.int16)).view(torch.bfloat16))
+
     def _combine_stage(self, recv_o, recv_ml, o_lat):
         o = merge_partials(recv_o.float().numpy(), recv_ml.numpy())
         o_lat.copy_(torch.from_numpy(o.view(np.int16)).view(torch.bfloat16))
@@ -190,14 +199,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _cp_rank_main(rank, world_size, port, out_dir):
+def _cp_rank_main(rank, world_size, port, out_dir, split="context"):
     os.environ["OMP_NUM_THREADS"] = "2"
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=world_size)
     try:
         weights, q_lora, cache, table, seqlens, positions, freqs = _inputs()
         # the exchange through collectives (the fused peer-memory one needs GPUs)
-        layer = OracleStagesLayer(CFG, "cpu", rank, world_size, attn_split="context",
+        layer = OracleStagesLayer(CFG, "cpu", rank, world_size, attn_split=split,
                                   exchange="nccl")
         layer.load_weights(*weights)
         y = torch.empty(B, CFG.dim, dtype=torch.float32)
@@ -207,9 +216,12 @@ def _cp_rank_main(rank, world_size, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_context_parallel_layer_over_gloo_equals_unsharded(tmp_path):
+@pytest.mark.parametrize("split", ["context", "rows"])
+def test_split_attention_layer_over_gloo_equals_unsharded(tmp_path, split):
+    """The context split (partial states exchanged) and the row split
+    (queries and outputs exchanged, whole sequences per rank)."""
     world_size = 2
-    mp.start_processes(_cp_rank_main, args=(world_size, _free_port(), str(tmp_path)),
+    mp.start_processes(_cp_rank_main, args=(world_size, _free_port(), str(tmp_path), split),
                        nprocs=world_size, start_method="spawn", join=True)
     ref = _oracle_layer(*_inputs())
     rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
@@ -423,6 +435,62 @@ def test_cp_rejects_unsupported_head_blocks():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("hb", [16, 32, 64, 128])
+def test_blocked_decode_equals_plain_decode(hb):
+    """qcau_decode_attn_paged_blocked with q and o in head blocks gives the
+    same bits as qcau_decode_attn_paged (same kernel and splits)."""
+    L = _lib.lib()
+    dev = torch.device("cuda", 0)
+    H, ctx, bsz = 128, 2048, 6
+    cache, table, _ = make_paged_cache(bsz, ctx, PAGE, WIDTH, dev, seed=11)
+    seqlens = torch.tensor([2048, 0, 1, 129, 1500, 640], device=dev, dtype=torch.int32)
+    g = torch.Generator(device=dev).manual_seed(12)
+    q = torch.randn(bsz, H, WIDTH, device=dev, generator=g).to(torch.bfloat16)
+    st = _lib.stream_ptr(dev)
+    need = L.qcau_decode_attn_workspace_size(bsz, H, 512, ctx)
+    ws = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+    ref = torch.empty(bsz, H, 512, device=dev, dtype=torch.bfloat16)
+    _lib.check(L.qcau_decode_attn_paged(q.data_ptr(), cache.data_ptr(), table.data_ptr(),
+                                        seqlens.data_ptr(), None, ref.data_ptr(), bsz, H, WIDTH,
+                                        512, WIDTH, PAGE, table.size(1), cache.size(0), ctx,
+                                        0.07, ws.data_ptr(), need, st), "decode")
+    qb = q.view(bsz, H // hb, hb, WIDTH).transpose(0, 1).contiguous()
+    ob = torch.empty(H // hb, bsz, hb, 512, device=dev, dtype=torch.bfloat16)
+    _lib.check(L.qcau_decode_attn_paged_blocked(qb.data_ptr(), hb, cache.data_ptr(),
+                                                table.data_ptr(), seqlens.data_ptr(), None,
+                                                ob.data_ptr(), hb, bsz, H, WIDTH, 512, WIDTH, PAGE,
+                                                table.size(1), cache.size(0), ctx, 0.07,
+                                                ws.data_ptr(), need, st), "blocked")
+    got = ob.transpose(0, 1).reshape(bsz, H, 512)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert torch.equal(got, ref)
+
+
+@pytest.mark.gpu
+def test_row_split_stages_one_rank_match_fused_layer():
+    """forward_rows at one rank (q stage, blocked attention, out stage)
+    gives the bits of the fused qcau_mla_decode."""
+    dev = torch.device("cuda", 0)
+    cfg = MLAConfig(n_heads=128)
+    layer = MLADecodeLayer(cfg, dev, attn_split="rows")
+    layer.random_weights(seed=1)
+    bsz, ctx = 8, 2048
+    cache, table, seqlens = make_paged_cache(bsz, ctx, PAGE, WIDTH, dev, seed=2)
+    seqlens[3] = 1000
+    g = torch.Generator(device=dev).manual_seed(3)
+    q_lora = torch.randn(bsz, cfg.dc, device=dev, generator=g)
+    q_lora = (q_lora * torch.rsqrt(q_lora.square().mean(-1, keepdim=True))).to(torch.bfloat16)
+    freqs = precompute_freqs_cis(cfg.d_rope, ctx + 1, cfg.rope_theta, dev)
+    positions = seqlens.clone()
+    y_fused = layer.forward_local(q_lora, cache, table, seqlens, positions, freqs, ctx).clone()
+    y_rows = layer.forward_rows(q_lora, cache, table, seqlens, positions, freqs, ctx)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    assert torch.equal(y_rows, y_fused)
+
+
+@pytest.mark.gpu
 def test_staged_layer_one_rank_matches_fused_layer():
     """forward_context at one rank (q stage, cp attention, combine, out stage)
     equals the fused qcau_mla_decode."""
@@ -466,7 +534,7 @@ def _nccl_rank_main(rank, world_size, port, out_dir):
         positions = seqlens.clone()
         ys = {}
         for name, mode, ex in (("p2p", "context", "p2p"), ("nccl", "context", "nccl"),
-                               ("heads", "heads", "nccl")):
+                               ("rows", "rows", "nccl"), ("heads", "heads", "nccl")):
             layer = MLADecodeLayer(cfg, dev, rank, world_size, attn_split=mode, exchange=ex)
             layer.random_weights(seed=1)
             for _ in range(3):   # steps alternate the receive areas
@@ -491,12 +559,12 @@ def _nccl_rank_main(rank, world_size, port, out_dir):
                     reason="needs two GPUs")
 def test_cp_layer_over_nccl_two_gpus(tmp_path):
     """Two ranks: the context-split layer with the exchange fused into the
-    attention kernel (peer memory) and with an NCCL all-to-all, and the
-    head-split layer, all equal the one-GPU layer."""
+    attention kernel (peer memory) and with an NCCL all-to-all, the
+    row-split layer and the head-split layer, all equal the one-GPU layer."""
     world_size = 2
     mp.start_processes(_nccl_rank_main, args=(world_size, _free_port(), str(tmp_path)),
                        nprocs=world_size, start_method="spawn", join=True)
     ref = np.load(tmp_path / "one0.npy")
-    for mode in ("p2p", "nccl", "heads"):
+    for mode in ("p2p", "nccl", "rows", "heads"):
         for r in range(world_size):
             _assert_layer_close(np.load(tmp_path / f"{mode}{r}.npy"), ref, f"{mode} rank {r}")
