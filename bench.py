@@ -343,7 +343,7 @@ def main():
                     help="time the causal prefill attention, batch 4 x 4096 x 128 heads")
     ap.add_argument("--sparse-fp8-only", type=int, default=0, metavar="HEADS",
                     help="time the FP8-cache top-k sparse decode (batch 64, 131072 rows) at HEADS")
-    ap.add_argument("--attn-split", default="context", choices=["context", "rows", "heads"],
+    ap.add_argument("--attn-split", default="rows", choices=["context", "rows", "heads"],
                     help="N > 1: split the attention of the head-sharded layer by context "
                          "(each rank 1/N of every sequence), by rows (each rank 1/N of the "
                          "sequences) or by heads (each rank streams the whole cache)")

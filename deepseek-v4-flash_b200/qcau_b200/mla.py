@@ -19,12 +19,13 @@ wo is row-parallel with an all-reduce of the partial outputs
   attn_split="heads"    each rank attends with its own heads over the whole
                         cache: every rank streams all of it, so the step time
                         barely falls with N;
-  attn_split="rows"     each rank attends with all heads over 1/N of the
+  attn_split="rows"     (the default) each rank attends with all heads over 1/N of the
                         sequences: an all-to-all of the absorbed queries
                         (B/N rows x h/N heads per pair of ranks) in, one of
                         the bf16 outputs back; each rank streams the pages
                         of its own sequences and nothing is merged across
-                        ranks;
+                        ranks (a batch that does not divide by the ranks
+                        runs the context split);
   attn_split="context"  the ranks all-gather their absorbed queries, each
                         attends with all heads over 1/N of every sequence's
                         tiles, and an all-to-all brings each rank the
@@ -122,7 +123,7 @@ class MLADecodeLayer:
     """Holds this rank's weight shards and runs one decode step per call."""
 
     def __init__(self, cfg: MLAConfig, device, rank: int = 0, world_size: int = 1,
-                 process_group=None, attn_split: str = "context", exchange: str = "nccl"):
+                 process_group=None, attn_split: str = "rows", exchange: str = "nccl"):
         if cfg.n_heads % world_size:
             raise ValueError("n_heads must be divisible by the number of ranks")
         if attn_split not in ("heads", "context", "rows"):
@@ -243,12 +244,14 @@ class MLADecodeLayer:
     def forward(self, q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen,
                 y: Optional[torch.Tensor] = None) -> torch.Tensor:
         """y [batch, dim] bf16, summed over the head shards."""
-        if self.world_size > 1 and self.attn_split == "context":
-            return self.forward_context(q_lora, cache, block_table, seqlens, positions, freqs,
-                                        max_seqlen, y)
-        if self.world_size > 1 and self.attn_split == "rows":
+        rows = self.attn_split == "rows" and q_lora.size(0) % self.world_size == 0
+        if self.world_size > 1 and rows:
             return self.forward_rows(q_lora, cache, block_table, seqlens, positions, freqs,
                                      max_seqlen, y)
+        if self.world_size > 1 and self.attn_split in ("context", "rows"):
+            # the row split needs the batch to divide by the ranks; else by context
+            return self.forward_context(q_lora, cache, block_table, seqlens, positions, freqs,
+                                        max_seqlen, y)
         y = self.forward_local(q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen, y)
         if self.world_size > 1:
             dist.all_reduce(y, group=self.group)
