@@ -568,3 +568,22 @@ def test_cp_layer_over_nccl_two_gpus(tmp_path):
     for mode in ("p2p", "nccl", "rows", "heads"):
         for r in range(world_size):
             _assert_layer_close(np.load(tmp_path / f"{mode}{r}.npy"), ref, f"{mode} rank {r}")
+
+
+def test_row_split_falls_back_to_context_split_for_uneven_batch():
+    """attn_split="rows" (the default) runs the row split when the batch
+    divides by the ranks and the context split when it does not."""
+    called = []
+
+    class Probe(MLADecodeLayer):
+        def forward_rows(self, *a, **k):
+            called.append("rows")
+
+        def forward_context(self, *a, **k):
+            called.append("context")
+
+    layer = Probe(CFG, "cpu", rank=0, world_size=2)
+    assert layer.attn_split == "rows"
+    for bsz in (2, 3):
+        layer.forward(torch.zeros(bsz, CFG.dc), None, None, None, None, None, 0)
+    assert called == ["rows", "context"]
