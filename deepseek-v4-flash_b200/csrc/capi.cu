@@ -122,21 +122,40 @@ int general_splits(int64_t b, int64_t h, int64_t max_len) {
 }
 
 // Splits of the tcgen05 two-CTA decode kernel: one CTA pair per (sequence,
-// 128-head group, split), one pair per two SMs.  Pick the split count whose
-// last wave is fullest (at least 4 tiles of 128 tokens per split).
+// 128-head group, split), one pair per two SMs, at least 4 tiles of 128
+// tokens per split.  The count minimises an estimate of the launch time
+// fitted to B200 timings of 16..128 sequences x 128 heads at 32K tokens
+// (within 3 % of 23 measured split counts): per wave of pairs, 12.4 us of
+// setup (TMEM, barriers, the Q load, the first K tile, the partial stores)
+// plus 2.39 us per tile of the longest split, each busy pair above 64
+// adding 0.3 % per tile (the pairs share HBM and L2); the combine adds
+// 0.015 us per partial row.  A part-filled single wave therefore beats
+// more, shorter splits: 64 sequences run fastest unsplit.
+double sm100_launch_us(int64_t pairs, int64_t tiles, int64_t s) {
+  constexpr int64_t kSlots = kNumSms / 2;
+  constexpr int64_t kQuietPairs = 64;
+  const double n = (double)((tiles + s - 1) / s);
+  auto wave = [&](int64_t busy) {
+    const double contention = busy > kQuietPairs ? 0.0081 * (double)(busy - kQuietPairs) : 0.0;
+    return 12.39 + n * (2.392 + contention);
+  };
+  const int64_t units = pairs * s;
+  double us = (double)(units / kSlots) * wave(kSlots);
+  if (units % kSlots) us += wave(units % kSlots);
+  if (s > 1) us += 0.015 * (double)units;
+  return us;
+}
+
 int sm100_splits(int64_t b, int64_t h, int64_t max_len) {
   const int64_t pairs = b * (h / 128 > 0 ? h / 128 : 1);
-  const int64_t slots = kNumSms / 2;
+  const int64_t tiles = (max_len + 127) / 128 > 0 ? (max_len + 127) / 128 : 1;
   const int64_t cap = (max_len + 511) / 512 > 0 ? (max_len + 511) / 512 : 1;
   int best = 1;
-  double best_score = -1.0;
-  for (int s = 1; s <= 32 && s <= cap; s++) {
-    const double units = (double)(pairs * s);
-    const double waves = units / (double)slots;
-    const double eff = waves / (double)((int64_t)((units + slots - 1) / slots));
-    const double score = eff - 0.004 * s;  // partials cost a little per split
-    if (score > best_score + 1e-9) {
-      best_score = score;
+  double best_us = sm100_launch_us(pairs, tiles, 1);
+  for (int s = 2; s <= 32 && s <= cap; s++) {
+    const double us = sm100_launch_us(pairs, tiles, s);
+    if (us < best_us - 1e-9) {
+      best_us = us;
       best = s;
     }
   }
