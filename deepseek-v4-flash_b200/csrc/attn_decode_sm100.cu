@@ -10,8 +10,12 @@
 // units); P and the denominator then share that stale max, so O / l is the
 // same quotient and P stays <= 2^8 (bf16 rounding is scale-free).
 //
-// Work unit = one CTA pair (cluster of 2) x one sequence x one KV split x 128
-// heads; tiles of 128 tokens (2 pages).  CTA r of the pair owns heads
+// Work unit = one sequence x one KV split x 128 heads, run by one CTA pair
+// (cluster of 2); tiles of 128 tokens (2 pages).  When the units outnumber the
+// pairs that fit on the device, the grid is one pair per slot and each pair
+// runs units pair, pair + npairs, ...: TMEM, the barriers and the launch are
+// paid once, the next unit's Q loads as soon as the last QK of the current
+// one has completed, and its QK tiles run under the current epilogue.  CTA r of the pair owns heads
 // [64r, 64r+64) of the group.  With h = 64, 32 or 16 heads (a head shard of
 // 128) the pair owns all h heads, h/2 per CTA, and the remaining MMA rows of
 // each CTA are padding (Q rows of other heads, or zeros past h) whose outputs
@@ -47,6 +51,8 @@
 // 7 PV issuer (pair leader).
 // Every wait is bounded; a timeout raises QCAU_DEVERR_TIMEOUT, drains the
 // copies in flight, frees TMEM and returns.
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -80,7 +86,9 @@ struct DecodeShared {
   uint64_t s_free[2];        // leader: the 8 softmax warps have read S(t)
   uint64_t p_full;           // leader: the 8 softmax warps wrote P(t) / corrected O
   uint64_t p_free;           // both: PV(t) done with P and O
-  uint64_t o_full;           // both: last PV done
+  uint64_t o_full;           // both: last PV of the unit done
+  uint64_t q_empty;          // both: last QK of the unit done (Q may be reloaded)
+  uint64_t o_free;           // leader: the 8 epilogue warps have read O
   uint64_t xbar[2];          // local: the 4 softmax warps exchanged tile maxima
   uint64_t lbar;             // local: denominator exchange
   float xmax[2][128];
@@ -118,6 +126,7 @@ struct DecodeParams {
   int nblk;
   int o_hblock;   // direct mode: o as [h / o_hblock][rows][o_hblock][512]
   int64_t rows;
+  int64_t units;  // work units; pair i of the grid runs units i, i + pairs, ...
   void* blk_o[kMaxBlocks];     // fp32 O, or fp16 O / l when part_f16
   int part_f16;
   float* blk_ml[kMaxBlocks];
@@ -161,6 +170,33 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// One work unit: query row b (sequence bs), KV split, and the first head of
+// this CTA's half of the 128-head group.
+struct DecodeUnit {
+  int64_t b, bs;
+  int split, seqlen, t_begin, T, head0;
+};
+
+__device__ __forceinline__ DecodeUnit decode_unit(const DecodeParams& p, int64_t unit,
+                                                  uint32_t rank) {
+  DecodeUnit U;
+  const int hg = (int)(unit % p.hgroups);
+  const int64_t rest = unit / p.hgroups;
+  U.split = (int)(rest % p.splits);
+  // query row r = (sequence bs, token t of qlen): token t sees the cached
+  // prefix up to its own position, seqlens[bs] - (qlen - 1 - t) tokens
+  U.b = rest / p.splits;
+  U.bs = U.b / p.qlen;
+  U.seqlen = p.seqlens[U.bs] - (p.qlen - 1 - (int)(U.b % p.qlen));
+  const int ntiles = (U.seqlen + kTile - 1) / kTile;
+  const int gsplit = p.split_base + U.split;  // this split among splits_total
+  U.t_begin = (int)((int64_t)ntiles * gsplit / p.splits_total);
+  const int t_end = (int)((int64_t)ntiles * (gsplit + 1) / p.splits_total);
+  U.T = t_end - U.t_begin;
+  U.head0 = hg * 2 * p.cta_heads + (int)rank * p.cta_heads;
+  return U;
+}
+
 // All lanes wait; the warp agrees on the outcome (timeouts are per lane).
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const bool ok = mbar_wait<true>(bar, parity, abort);
@@ -183,49 +219,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
-  const int64_t unit = blockIdx.x >> 1;
-  const int hg = (int)(unit % p.hgroups);
-  const int64_t rest = unit / p.hgroups;
-  const int split = (int)(rest % p.splits);
-  // query row r = (sequence bs, token t of qlen): token t sees the cached
-  // prefix up to its own position, seqlens[bs] - (qlen - 1 - t) tokens
-  const int64_t b = rest / p.splits;
-  const int64_t bs = b / p.qlen;
-  const int seqlen = p.seqlens[bs] - (p.qlen - 1 - (int)(b % p.qlen));
-  const int ntiles = (seqlen + kTile - 1) / kTile;
-  const int gsplit = p.split_base + split;  // this split among splits_total
-  const int t_begin = (int)((int64_t)ntiles * gsplit / p.splits_total);
-  const int t_end = (int)((int64_t)ntiles * (gsplit + 1) / p.splits_total);
-  const int T = t_end - t_begin;
-  const int head0 = hg * 2 * p.cta_heads + (int)rank * p.cta_heads;
-  // partial row of (row b, this split, head) in its head block's destination
-  auto part_row = [&](int head, int& blk) -> int64_t {
+  const int64_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  // partial row of (row U.b, split U.split, head) in its head block's destination
+  auto part_row = [&](const DecodeUnit& U, int head, int& blk) -> int64_t {
     blk = head / p.part_hblock;
-    return ((int64_t)b * p.splits + split) * p.part_hblock + (head - blk * p.part_hblock);
+    return ((int64_t)U.b * p.splits + U.split) * p.part_hblock + (head - blk * p.part_hblock);
   };
 
-  // direct-mode output row of (row b, head)
-  auto out_row = [&](int head) -> __nv_bfloat16* {
+  // direct-mode output row of (row U.b, head)
+  auto out_row = [&](const DecodeUnit& U, int head) -> __nv_bfloat16* {
     const int blk = head / p.o_hblock;
-    return p.out + (((int64_t)blk * p.rows + b) * p.o_hblock + (head - blk * p.o_hblock)) * 512;
+    return p.out + (((int64_t)blk * p.rows + U.b) * p.o_hblock + (head - blk * p.o_hblock)) * 512;
   };
-
-  if (T <= 0) {  // both CTAs of the pair take this branch together
-    if (p.direct) {  // no visible token: the output rows are zero
-      for (int i = threadIdx.x; i < p.cta_heads * 64; i += blockDim.x)
-        reinterpret_cast<uint4*>(out_row(head0 + (i >> 6)))[i & 63] = make_uint4(0u, 0u, 0u, 0u);
-      return;
-    }
-    for (int i = threadIdx.x; i < p.cta_heads; i += blockDim.x) {
-      int blk;
-      const int64_t prow = part_row(head0 + i, blk);
-      p.blk_ml[blk][prow * 2] = -INFINITY;
-      p.blk_ml[blk][prow * 2 + 1] = 0.f;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) signal_done(p);
-    return;
-  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kKSlots; i++) {
@@ -245,6 +250,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(&sh->p_full, 8);
     mbar_init(&sh->p_free, 1);
     mbar_init(&sh->o_full, 1);
+    mbar_init(&sh->q_empty, 1);
+    mbar_init(&sh->o_free, 8);
     mbar_init(&sh->lbar, 4);
     sh->abort = 0;
     fence_barrier_init();
@@ -255,10 +262,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
 
-  const int pages_used = (seqlen + 63) / 64;
-  auto page_of = [&](int pidx) -> int {
+  // physical page of the unit's page pidx (units with T > 0 have seqlen >= 1)
+  auto page_of = [&](const DecodeUnit& U, int pidx) -> int {
+    const int pages_used = (U.seqlen + 63) / 64;
     if (pidx >= pages_used) pidx = pages_used - 1;  // masked tokens: any valid page
-    const int64_t e = p.table[bs * p.max_pages + pidx];
+    const int64_t e = p.table[U.bs * p.max_pages + pidx];
     if (e < 0 || e >= p.num_pages) {
       raise_dev_error(p.err, QCAU_DEVERR_INDEX);
       return 0;
@@ -268,7 +276,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   if (warp == 0 || warp == 6) {
     // ------------------------------------------------ TMA producers (both CTAs)
-    // warp 0: Q, then the K boxes of tiles 0, 1, ...; warp 6: the V pages.
+    // warp 0: per unit Q, then the K boxes of its tiles; warp 6: the V pages.
     if (lane == 0) {
       const bool is_k = warp == 0;
       uint64_t* fullb = is_k ? sh->kfull : sh->vfull;
@@ -278,50 +286,58 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       constexpr int kMaxSlots = kKSlots > kVSlots ? kKSlots : kVSlots;
       int last_use[kMaxSlots];  // per slot: last ring pass whose copy was issued
       for (int i = 0; i < kMaxSlots; i++) last_use[i] = -1;
-      if (is_k) {
-        if (leader) mbar_arrive_expect_tx(&sh->q_full, 2 * kQBytes);
-        const uint32_t q_full_l = mapa_shared(smem_u32(&sh->q_full), 0);
-        // 64 head rows per chunk, in boxes of q_box heads of one block
-        // (rows past the last head are zero-filled padding)
-        for (int k = 0; k < 9; k++)
-          for (int m = 0; m < 64; m += p.q_box) {
-            const int hd = head0 + m;
-            tma_load_4d_pair(sQ + k * 8192 + m * 128, &tm_q, q_full_l, 64 * k, hd % p.q_hblock,
-                             (int)b, hd / p.q_hblock);
-          }
-      }
-      int n = 0;
+      const uint32_t q_full_l = mapa_shared(smem_u32(&sh->q_full), 0);
+      int n = 0, nq = 0;  // ring copies issued; units whose Q was issued
       bool ok = true;
-      for (int it = 0; it < T && ok; it++) {
-        const int t = t_begin + it;
-        for (int i = 0; i < per_tile; i++, n++) {
-          const int slot = n % nslots, u = n / nslots;
-          if (!(ok = mbar_wait(&emptyb[slot], (u & 1) ^ 1, abort))) break;
-          if (leader) mbar_arrive_expect_tx(&fullb[slot], is_k ? 2 * kKSlot : 2 * kVSlot);
-          last_use[slot] = u;
-          const uint32_t fb = mapa_shared(smem_u32(&fullb[slot]), 0);
-          if (is_k) {
-            // chunks 3i..3i+2 (dims 192i..192i+191) of this CTA's page of the tile
-            tma_load_4d_pair(sK + slot * kKSlot, &tm_k, fb, 0, 0, 3 * i,
-                             page_of(2 * t + (int)rank));
-          } else {
-            // page i of the tile: this CTA's dims [256r, 256r+256), 4 chunks in one box
-            tma_load_4d_pair(sV + slot * kVSlot, &tm_v, fb, 0, 0, 4 * (int)rank,
-                             page_of(2 * t + i));
+      for (int64_t unit = pair; unit < p.units && ok; unit += npairs) {
+        const DecodeUnit U = decode_unit(p, unit, rank);
+        if (U.T <= 0) continue;
+        if (is_k) {
+          // Q of the previous unit is free once its last QK has completed
+          if (nq > 0 && !(ok = mbar_wait(&sh->q_empty, (nq - 1) & 1, abort))) break;
+          if (leader) mbar_arrive_expect_tx(&sh->q_full, 2 * kQBytes);
+          // 64 head rows per chunk, in boxes of q_box heads of one block
+          // (rows past the last head are zero-filled padding)
+          for (int k = 0; k < 9; k++)
+            for (int m = 0; m < 64; m += p.q_box) {
+              const int hd = U.head0 + m;
+              tma_load_4d_pair(sQ + k * 8192 + m * 128, &tm_q, q_full_l, 64 * k,
+                               hd % p.q_hblock, (int)U.b, hd / p.q_hblock);
+            }
+          nq++;
+        }
+        for (int it = 0; it < U.T && ok; it++) {
+          const int t = U.t_begin + it;
+          for (int i = 0; i < per_tile; i++, n++) {
+            const int slot = n % nslots, u = n / nslots;
+            if (!(ok = mbar_wait(&emptyb[slot], (u & 1) ^ 1, abort))) break;
+            if (leader) mbar_arrive_expect_tx(&fullb[slot], is_k ? 2 * kKSlot : 2 * kVSlot);
+            last_use[slot] = u;
+            const uint32_t fb = mapa_shared(smem_u32(&fullb[slot]), 0);
+            if (is_k) {
+              // chunks 3i..3i+2 (dims 192i..192i+191) of this CTA's page of the tile
+              tma_load_4d_pair(sK + slot * kKSlot, &tm_k, fb, 0, 0, 3 * i,
+                               page_of(U, 2 * t + (int)rank));
+            } else {
+              // page i of the tile: this CTA's dims [256r, 256r+256), 4 chunks in one box
+              tma_load_4d_pair(sV + slot * kVSlot, &tm_v, fb, 0, 0, 4 * (int)rank,
+                               page_of(U, 2 * t + i));
+            }
           }
         }
       }
       if (*abort && leader) {
         // the leader's full barriers count both CTAs' copies: drain them all
         volatile int never = 0;
-        if (is_k) mbar_wait<true>(&sh->q_full, 0, &never);
+        if (is_k && nq > 0) mbar_wait<true>(&sh->q_full, (nq - 1) & 1, &never);
         for (int slot = 0; slot < nslots; slot++)
           if (last_use[slot] >= 0) mbar_wait<true>(&fullb[slot], last_use[slot] & 1, &never);
       }
     }
   } else if (warp == 1 || warp == 7) {
     // ------------------------------------------------ MMA issuers (pair leader)
-    // warp 1 issues QK(0), QK(1), ...; warp 7 issues PV(0), PV(1), ...
+    // warp 1 issues QK(0), QK(1), ...; warp 7 issues PV(0), PV(1), ... over
+    // the pair's tiles in unit order (gt counts them across units)
     if (leader && lane == 0) {
       const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
@@ -330,60 +346,74 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool ok = true;
       if (warp == 1) {
         const uint32_t idesc_qk = make_idesc(128, 128, kFmtBF16, kFmtBF16, false, false);
-        int nk = 0;
-        ok = mbar_wait(&sh->q_full, 0, abort);
-        for (int it = 0; it < T && ok; it++) {
-          const int sb = it & 1;
-          if (it >= 2 && !(ok = mbar_wait<true>(&sh->s_free[sb], ((it >> 1) - 1) & 1, abort)))
-            break;
-          tc_fence_after();
-          for (int g = 0; g < kKPerTile; g++, nk++) {
-            const int slot = nk % kKSlots, u = nk / kKSlots;
-            if (!(ok = mbar_wait(&sh->kfull[slot], u & 1, abort))) break;
-            // chunk k = 3g + c: 4 MMAs of 16 dims, B = this CTA's 64 tokens (N = 128)
+        int nk = 0, gt = 0, nu = 0;  // K boxes consumed, tiles, units
+        for (int64_t unit = pair; unit < p.units && ok; unit += npairs) {
+          const DecodeUnit U = decode_unit(p, unit, rank);
+          if (U.T <= 0) continue;
+          if (!(ok = mbar_wait(&sh->q_full, nu & 1, abort))) break;
+          for (int it = 0; it < U.T && ok; it++, gt++) {
+            const int sb = gt & 1;
+            if (gt >= 2 && !(ok = mbar_wait<true>(&sh->s_free[sb], ((gt >> 1) - 1) & 1, abort)))
+              break;
+            tc_fence_after();
+            for (int g = 0; g < kKPerTile; g++, nk++) {
+              const int slot = nk % kKSlots, u = nk / kKSlots;
+              if (!(ok = mbar_wait(&sh->kfull[slot], u & 1, abort))) break;
+              // chunk k = 3g + c: 4 MMAs of 16 dims, B = this CTA's 64 tokens (N = 128)
 #pragma unroll
-            for (int c = 0; c < 3; c++)
+              for (int c = 0; c < 3; c++)
 #pragma unroll
-              for (int kk = 0; kk < 4; kk++)
-                mma_bf16_pair(tmem + kTmemS + sb * 64,
-                              make_sdesc(q_addr + (3 * g + c) * 8192 + kk * 32, 16, 1024),
-                              make_sdesc(k_addr + slot * kKSlot + c * 8192 + kk * 32, 16, 1024),
-                              idesc_qk, (g | c | kk) != 0 ? 1u : 0u);
-            tc_commit_pair(&sh->kempty[slot], 3);
-            last_bar = &sh->kempty[slot];
-            last_phase = u & 1;
+                for (int kk = 0; kk < 4; kk++)
+                  mma_bf16_pair(tmem + kTmemS + sb * 64,
+                                make_sdesc(q_addr + (3 * g + c) * 8192 + kk * 32, 16, 1024),
+                                make_sdesc(k_addr + slot * kKSlot + c * 8192 + kk * 32, 16, 1024),
+                                idesc_qk, (g | c | kk) != 0 ? 1u : 0u);
+              tc_commit_pair(&sh->kempty[slot], 3);
+              last_bar = &sh->kempty[slot];
+              last_phase = u & 1;
+            }
+            if (ok) tc_commit_pair(&sh->s_full[sb], 3);
           }
-          if (ok) tc_commit_pair(&sh->s_full[sb], 3);
+          // both CTAs' Q may be reloaded once the unit's QK MMAs have completed
+          if (ok) tc_commit_pair(&sh->q_empty, 3);
+          nu++;
         }
       } else {
         const uint32_t idesc_pv = make_idesc(128, 256, kFmtBF16, kFmtBF16, false, true);
-        int nv = 0;
-        for (int it = 0; it < T && ok; it++) {
-          if (!(ok = mbar_wait<true>(&sh->p_full, it & 1, abort))) break;
-          tc_fence_after();
-          for (int pg = 0; pg < kVPerTile; pg++, nv++) {
-            const int slot = nv % kVSlots, u = nv / kVSlots;
-            if (!(ok = mbar_wait(&sh->vfull[slot], u & 1, abort))) break;
-            // PV MMA j takes chunks 2j, 2j+1 of each CTA's slot: its output
-            // columns are dims 256r + 128j + [0, 128) of CTA r's half
+        int nv = 0, gt = 0, nu = 0;  // V pages consumed, tiles, units
+        for (int64_t unit = pair; unit < p.units && ok; unit += npairs) {
+          const DecodeUnit U = decode_unit(p, unit, rank);
+          if (U.T <= 0) continue;
+          // the first PV of a unit overwrites O: the previous epilogue has read it
+          if (nu > 0 && !(ok = mbar_wait<true>(&sh->o_free, (nu - 1) & 1, abort))) break;
+          for (int it = 0; it < U.T && ok; it++, gt++) {
+            if (!(ok = mbar_wait<true>(&sh->p_full, gt & 1, abort))) break;
+            tc_fence_after();
+            for (int pg = 0; pg < kVPerTile; pg++, nv++) {
+              const int slot = nv % kVSlots, u = nv / kVSlots;
+              if (!(ok = mbar_wait(&sh->vfull[slot], u & 1, abort))) break;
+              // PV MMA j takes chunks 2j, 2j+1 of each CTA's slot: its output
+              // columns are dims 256r + 128j + [0, 128) of CTA r's half
 #pragma unroll
-            for (int j = 0; j < 2; j++)
+              for (int j = 0; j < 2; j++)
 #pragma unroll
-              for (int kk = 0; kk < 4; kk++) {
-                // 16 tokens of page pg: P chunk pg, V slot rows 16kk..16kk+15
-                const uint64_t ad = make_sdesc(p_addr + pg * 8192 + kk * 32, 16, 1024);
-                const uint64_t bd =
-                    make_sdesc(v_addr + slot * kVSlot + j * 16384 + kk * 2048, 8192, 1024);
-                mma_bf16_pair(tmem + kTmemO + j * 128, ad, bd, idesc_pv,
-                              (it > 0 || pg > 0 || kk > 0) ? 1u : 0u);
-              }
-            tc_commit_pair(&sh->vempty[slot], 3);
-            last_bar = &sh->vempty[slot];
-            last_phase = u & 1;
+                for (int kk = 0; kk < 4; kk++) {
+                  // 16 tokens of page pg: P chunk pg, V slot rows 16kk..16kk+15
+                  const uint64_t ad = make_sdesc(p_addr + pg * 8192 + kk * 32, 16, 1024);
+                  const uint64_t bd =
+                      make_sdesc(v_addr + slot * kVSlot + j * 16384 + kk * 2048, 8192, 1024);
+                  mma_bf16_pair(tmem + kTmemO + j * 128, ad, bd, idesc_pv,
+                                (it > 0 || pg > 0 || kk > 0) ? 1u : 0u);
+                }
+              tc_commit_pair(&sh->vempty[slot], 3);
+              last_bar = &sh->vempty[slot];
+              last_phase = u & 1;
+            }
+            if (ok) tc_commit_pair(&sh->p_free, 3);
           }
-          if (ok) tc_commit_pair(&sh->p_free, 3);
+          if (ok) tc_commit_pair(&sh->o_full, 3);
+          nu++;
         }
-        if (ok) tc_commit_pair(&sh->o_full, 3);
       }
       if (*abort && last_bar != nullptr) {
         // the MMAs issued so far finish before TMEM and the slots go away
@@ -396,174 +426,201 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // TMEM lane
     const int hl = row & 63, half = row >> 6;
+    const int et = threadIdx.x - 64;      // 0..127 over warps 2-5
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const float sl2 = p.scale * kLog2e;
     const uint32_t s_free_l[2] = {mapa_shared(smem_u32(&sh->s_free[0]), 0),
                                   mapa_shared(smem_u32(&sh->s_free[1]), 0)};
     const uint32_t p_full_l = mapa_shared(smem_u32(&sh->p_full), 0);
-    float m_run = -INFINITY, l_run = 0.f;
+    const uint32_t o_free_l = mapa_shared(smem_u32(&sh->o_free), 0);
+    int gt = 0, nu = 0;  // tiles, units with tiles
     bool ok = true;
-    for (int it = 0; it < T && ok; it++) {
-      const int sb = it & 1;
-      const uint32_t s_addr = tmem + lane_base + kTmemS + sb * 64;
-      const int tok0 = (t_begin + it) * kTile + half * 64;
-      const int nvalid = seqlen - tok0;  // tokens of this half that exist (may be <= 0 or > 64)
-      if (!(ok = warp_wait(&sh->s_full[sb], (it >> 1) & 1, abort))) break;
-      tc_fence_after();
-      // this thread's 64 scores into registers; the S buffer is then free
-      float v[64];
-#pragma unroll
-      for (int c = 0; c < 2; c++)
-        tmem_ld32(s_addr + c * 32, *reinterpret_cast<float(*)[32]>(v + 32 * c));
-#pragma unroll
-      for (int c = 0; c < 2; c++) tmem_ld_wait_regs(v + 32 * c);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_remote(s_free_l[sb]);
-      const bool full = nvalid >= 64;
-      // pass 1: tile max
-      float mx = -INFINITY;
-      if (full) {
-#pragma unroll
-        for (int i = 0; i < 64; i++) mx = fmaxf(mx, v[i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; i++)
-          if (i < nvalid) mx = fmaxf(mx, v[i]);
-      }
-      mx = (mx == -INFINITY) ? -INFINITY : mx * sl2;
-      sh->xmax[sb][row] = mx;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sh->xbar[sb]);
-      if (!(ok = warp_wait(&sh->xbar[sb], (it >> 1) & 1, abort))) break;
-      const float tmax = fmaxf(mx, sh->xmax[sb][row ^ 64]);
-      float alpha = 1.f;
-      bool resc = false;
-      if (m_run == -INFINITY) {
-        m_run = tmax;  // first tile: PV starts a fresh accumulator
-      } else if (tmax > m_run + kRescale) {
-        alpha = exp2f(m_run - tmax);
-        m_run = tmax;
-        resc = true;
-      }
-      // pass 2 into registers: P = 2^(s*scale*log2e - m) as bf16 pairs; the
-      // row sum is over the unrounded values
-      const uint64_t sc2 = f2_pack(sl2, sl2), nm2 = f2_pack(-m_run, -m_run);
-      uint64_t sum2 = f2_pack(0.f, 0.f);
-      uint32_t pk[32];
-#pragma unroll
-      for (int i = 0; i < 32; i++) {
-        const int e = 2 * i;
-        float x0, x1;
-        f2_unpack(f2_fma(f2_pack(v[e], v[e + 1]), sc2, nm2), x0, x1);
-        float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
-        if (!full) {
-          p0 = (e < nvalid) ? p0 : 0.f;
-          p1 = (e + 1 < nvalid) ? p1 : 0.f;
+    for (int64_t unit = pair; unit < p.units && ok; unit += npairs) {
+      const DecodeUnit U = decode_unit(p, unit, rank);
+      if (U.T <= 0) {
+        if (p.direct) {  // no visible token: the output rows are zero
+          for (int i = et; i < p.cta_heads * 64; i += 128)
+            reinterpret_cast<uint4*>(out_row(U, U.head0 + (i >> 6)))[i & 63] =
+                make_uint4(0u, 0u, 0u, 0u);
+        } else {  // an empty partial: weight zero in the combine
+          for (int i = et; i < p.cta_heads; i += 128) {
+            int blk;
+            const int64_t prow = part_row(U, U.head0 + i, blk);
+            p.blk_ml[blk][prow * 2] = -INFINITY;
+            p.blk_ml[blk][prow * 2 + 1] = 0.f;
+          }
         }
-        sum2 = f2_add(sum2, f2_pack(p0, p1));
-        pk[i] = pack_bf16(p0, p1);
+        continue;
       }
-      float ps0, ps1;
-      f2_unpack(sum2, ps0, ps1);
-      const float ps = ps0 + ps1;
-      // P(t) reuses the buffer of P(t-1), and O holds tiles < t, once PV(t-1) is done
-      if (it >= 1 && !(ok = warp_wait(&sh->p_free, (it - 1) & 1, abort))) break;
-      // 64 tokens = one 128-byte row (chunk `half`, the page of CTA `half`)
-      // of eight sixteen-byte units, swizzled
-      uint8_t* pbase = sP + half * 8192 + hl * 128;
-#pragma unroll
-      for (int u = 0; u < 8; u++)
-        *reinterpret_cast<uint4*>(pbase + ((u ^ (hl & 7)) << 4)) =
-            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-      l_run = l_run * alpha + ps;
-      if (__any_sync(0xffffffffu, resc)) {
-        // rescale this warp's rows of O (PV(t-1) is complete)
+      const int seqlen = U.seqlen, head0 = U.head0;
+      float m_run = -INFINITY, l_run = 0.f;
+      for (int it = 0; it < U.T && ok; it++, gt++) {
+        const int sb = gt & 1;
+        const uint32_t s_addr = tmem + lane_base + kTmemS + sb * 64;
+        const int tok0 = (U.t_begin + it) * kTile + half * 64;
+        const int nvalid = seqlen - tok0;  // tokens of this half that exist (may be <= 0 or > 64)
+        if (!(ok = warp_wait(&sh->s_full[sb], (gt >> 1) & 1, abort))) break;
         tc_fence_after();
+        // this thread's 64 scores into registers; the S buffer is then free
+        float v[64];
+#pragma unroll
+        for (int c = 0; c < 2; c++)
+          tmem_ld32(s_addr + c * 32, *reinterpret_cast<float(*)[32]>(v + 32 * c));
+#pragma unroll
+        for (int c = 0; c < 2; c++) tmem_ld_wait_regs(v + 32 * c);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(s_free_l[sb]);
+        const bool full = nvalid >= 64;
+        // pass 1: tile max
+        float mx = -INFINITY;
+        if (full) {
+#pragma unroll
+          for (int i = 0; i < 64; i++) mx = fmaxf(mx, v[i]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; i++)
+            if (i < nvalid) mx = fmaxf(mx, v[i]);
+        }
+        mx = (mx == -INFINITY) ? -INFINITY : mx * sl2;
+        sh->xmax[sb][row] = mx;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh->xbar[sb]);
+        if (!(ok = warp_wait(&sh->xbar[sb], (gt >> 1) & 1, abort))) break;
+        const float tmax = fmaxf(mx, sh->xmax[sb][row ^ 64]);
+        float alpha = 1.f;
+        bool resc = false;
+        if (m_run == -INFINITY) {
+          m_run = tmax;  // first tile: PV starts a fresh accumulator
+        } else if (tmax > m_run + kRescale) {
+          alpha = exp2f(m_run - tmax);
+          m_run = tmax;
+          resc = true;
+        }
+        // pass 2 into registers: P = 2^(s*scale*log2e - m) as bf16 pairs; the
+        // row sum is over the unrounded values
+        const uint64_t sc2 = f2_pack(sl2, sl2), nm2 = f2_pack(-m_run, -m_run);
+        uint64_t sum2 = f2_pack(0.f, 0.f);
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          const int e = 2 * i;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(v[e], v[e + 1]), sc2, nm2), x0, x1);
+          float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+          if (!full) {
+            p0 = (e < nvalid) ? p0 : 0.f;
+            p1 = (e + 1 < nvalid) ? p1 : 0.f;
+          }
+          sum2 = f2_add(sum2, f2_pack(p0, p1));
+          pk[i] = pack_bf16(p0, p1);
+        }
+        float ps0, ps1;
+        f2_unpack(sum2, ps0, ps1);
+        const float ps = ps0 + ps1;
+        // P(t) reuses the buffer of P(t-1), and O holds tiles < t, once PV(t-1) is done
+        if (gt >= 1 && !(ok = warp_wait(&sh->p_free, (gt - 1) & 1, abort))) break;
+        // 64 tokens = one 128-byte row (chunk `half`, the page of CTA `half`)
+        // of eight sixteen-byte units, swizzled
+        uint8_t* pbase = sP + half * 8192 + hl * 128;
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          *reinterpret_cast<uint4*>(pbase + ((u ^ (hl & 7)) << 4)) =
+              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        l_run = l_run * alpha + ps;
+        if (__any_sync(0xffffffffu, resc)) {
+          // rescale this warp's rows of O (PV(t-1) is complete)
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < 8; c++) {
+            float v[32];
+            const uint32_t ta = tmem + lane_base + kTmemO + c * 32;
+            tmem_ld32(ta, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] *= alpha;
+            tmem_st32(ta, v);
+          }
+          tmem_st_wait();
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(p_full_l);
+      }
+      if (ok) ok = warp_wait(&sh->o_full, nu & 1, abort);
+      sh->xsum[row] = l_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->lbar);
+      if (ok) ok = warp_wait(&sh->lbar, nu & 1, abort);
+      if (ok && p.direct) {
+        // one split: sink and normalisation as attn_combine does for one part,
+        // O / (l + 2^(sink*log2e - m)), rounded to bf16
+        tc_fence_after();
+        const float l_tot = l_run + sh->xsum[row ^ 64];
+        float den;
+        const float sk = (p.sink && hl < p.cta_heads) ? p.sink[head0 + hl] * kLog2e : -INFINITY;
+        if (m_run != -INFINITY)
+          den = l_tot + exp2f(sk - m_run);
+        else
+          den = l_tot + ((p.sink && hl < p.cta_heads && isfinite(p.sink[head0 + hl])) ? 1.f : 0.f);
+        const float inv = 1.f / fmaxf(den, 1.17549435e-38f);
+        __nv_bfloat16* po = out_row(U, head0 + hl) + 256 * half;
 #pragma unroll 1
         for (int c = 0; c < 8; c++) {
           float v[32];
-          const uint32_t ta = tmem + lane_base + kTmemO + c * 32;
-          tmem_ld32(ta, v);
+          tmem_ld32(tmem + lane_base + kTmemO + c * 32, v);
           tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; i++) v[i] *= alpha;
-          tmem_st32(ta, v);
-        }
-        tmem_st_wait();
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_remote(p_full_l);
-    }
-    if (ok) ok = warp_wait(&sh->o_full, 0, abort);
-    sh->xsum[row] = l_run;
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sh->lbar);
-    if (ok) ok = warp_wait(&sh->lbar, 0, abort);
-    if (ok && p.direct) {
-      // one split: sink and normalisation as attn_combine does for one part,
-      // O / (l + 2^(sink*log2e - m)), rounded to bf16
-      tc_fence_after();
-      const float l_tot = l_run + sh->xsum[row ^ 64];
-      float den;
-      const float sk = (p.sink && hl < p.cta_heads) ? p.sink[head0 + hl] * kLog2e : -INFINITY;
-      if (m_run != -INFINITY)
-        den = l_tot + exp2f(sk - m_run);
-      else
-        den = l_tot + ((p.sink && hl < p.cta_heads && isfinite(p.sink[head0 + hl])) ? 1.f : 0.f);
-      const float inv = 1.f / fmaxf(den, 1.17549435e-38f);
-      __nv_bfloat16* po = out_row(head0 + hl) + 256 * half;
-#pragma unroll 1
-      for (int c = 0; c < 8; c++) {
-        float v[32];
-        tmem_ld32(tmem + lane_base + kTmemO + c * 32, v);
-        tmem_ld_wait();
-        uint4* dst = reinterpret_cast<uint4*>(po + (c >> 2) * 128 + (c & 3) * 32);
-        if (hl < p.cta_heads) {
-#pragma unroll
-          for (int i = 0; i < 4; i++)
-            dst[i] = make_uint4(pack_bf16(v[8 * i] * inv, v[8 * i + 1] * inv),
-                                pack_bf16(v[8 * i + 2] * inv, v[8 * i + 3] * inv),
-                                pack_bf16(v[8 * i + 4] * inv, v[8 * i + 5] * inv),
-                                pack_bf16(v[8 * i + 6] * inv, v[8 * i + 7] * inv));
-        }
-      }
-    } else if (ok) {
-      tc_fence_after();
-      const float l_tot = l_run + sh->xsum[row ^ 64];
-      int blk = 0;
-      const int64_t prow = hl < p.cta_heads ? part_row(head0 + hl, blk) : 0;
-      const int64_t po = prow * 512 + 256 * half;  // element offset of this thread's half row
-      const float inv_l = l_tot > 0.f ? 1.f / l_tot : 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 8; c++) {
-        float v[32];
-        tmem_ld32(tmem + lane_base + kTmemO + c * 32, v);
-        tmem_ld_wait();
-        const int64_t e = po + (c >> 2) * 128 + (c & 3) * 32;
-        if (hl < p.cta_heads) {
-          if (p.part_f16) {  // O / l in fp16: half the bytes, 2^-11 relative error
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.blk_o[blk]) + e);
+          uint4* dst = reinterpret_cast<uint4*>(po + (c >> 2) * 128 + (c & 3) * 32);
+          if (hl < p.cta_heads) {
 #pragma unroll
             for (int i = 0; i < 4; i++)
-              dst[i] = make_uint4(pack_f16(v[8 * i] * inv_l, v[8 * i + 1] * inv_l),
-                                  pack_f16(v[8 * i + 2] * inv_l, v[8 * i + 3] * inv_l),
-                                  pack_f16(v[8 * i + 4] * inv_l, v[8 * i + 5] * inv_l),
-                                  pack_f16(v[8 * i + 6] * inv_l, v[8 * i + 7] * inv_l));
-          } else {
-            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.blk_o[blk]) + e);
-#pragma unroll
-            for (int i = 0; i < 8; i++)
-              dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+              dst[i] = make_uint4(pack_bf16(v[8 * i] * inv, v[8 * i + 1] * inv),
+                                  pack_bf16(v[8 * i + 2] * inv, v[8 * i + 3] * inv),
+                                  pack_bf16(v[8 * i + 4] * inv, v[8 * i + 5] * inv),
+                                  pack_bf16(v[8 * i + 6] * inv, v[8 * i + 7] * inv));
           }
         }
+      } else if (ok) {
+        tc_fence_after();
+        const float l_tot = l_run + sh->xsum[row ^ 64];
+        int blk = 0;
+        const int64_t prow = hl < p.cta_heads ? part_row(U, head0 + hl, blk) : 0;
+        const int64_t po = prow * 512 + 256 * half;  // element offset of this thread's half row
+        const float inv_l = l_tot > 0.f ? 1.f / l_tot : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 8; c++) {
+          float v[32];
+          tmem_ld32(tmem + lane_base + kTmemO + c * 32, v);
+          tmem_ld_wait();
+          const int64_t e = po + (c >> 2) * 128 + (c & 3) * 32;
+          if (hl < p.cta_heads) {
+            if (p.part_f16) {  // O / l in fp16: half the bytes, 2^-11 relative error
+              uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.blk_o[blk]) + e);
+#pragma unroll
+              for (int i = 0; i < 4; i++)
+                dst[i] = make_uint4(pack_f16(v[8 * i] * inv_l, v[8 * i + 1] * inv_l),
+                                    pack_f16(v[8 * i + 2] * inv_l, v[8 * i + 3] * inv_l),
+                                    pack_f16(v[8 * i + 4] * inv_l, v[8 * i + 5] * inv_l),
+                                    pack_f16(v[8 * i + 6] * inv_l, v[8 * i + 7] * inv_l));
+            } else {
+              float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.blk_o[blk]) + e);
+#pragma unroll
+              for (int i = 0; i < 8; i++)
+                dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            }
+          }
+        }
+        if (half == 0 && hl < p.cta_heads) {
+          p.blk_ml[blk][prow * 2] = m_run;
+          p.blk_ml[blk][prow * 2 + 1] = l_tot;
+        }
       }
-      if (half == 0 && hl < p.cta_heads) {
-        p.blk_ml[blk][prow * 2] = m_run;
-        p.blk_ml[blk][prow * 2 + 1] = l_tot;
-      }
+      // O is read: the next unit's first PV may overwrite it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(o_free_l);
+      nu++;
     }
   }
 
@@ -584,6 +641,35 @@ bool is_sm100_device() {
   cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
   return major == 10 && minor == 0;
+}
+
+// CTA pairs of the kernel that can be resident at once on the current device
+// (one CTA per SM, clusters of two), or 0 when the query fails.  Queried once
+// per device, after the kernel's shared memory limit is set.
+int resident_pairs() {
+  static std::mutex mu;
+  static int cached[64];
+  static bool init = false;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!init) {
+    for (int& c : cached) c = -1;
+    init = true;
+  }
+  if (cached[dev] < 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, decode_attn_sm100_kernel, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    cached[dev] = n;
+  }
+  return cached[dev];
 }
 
 }  // namespace
@@ -695,7 +781,12 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
                                        (int)kSmemBytes);
   if (e != cudaSuccess) return e;
   const int64_t units = a.b * a.s * a.splits * p.hgroups;
-  decode_attn_sm100_kernel<<<(unsigned)(2 * units), kThreads, kSmemBytes, st>>>(tq, tk, tv, p);
+  p.units = units;
+  // one pair per unit; when the units outnumber the pairs that fit at once,
+  // one pair per slot, each looping over units (no pair waits for another)
+  const int64_t slots = resident_pairs();
+  const int64_t pairs = (slots > 0 && units > slots) ? slots : units;
+  decode_attn_sm100_kernel<<<(unsigned)(2 * pairs), kThreads, kSmemBytes, st>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }
 

@@ -130,7 +130,11 @@ int general_splits(int64_t b, int64_t h, int64_t max_len) {
 // plus 2.39 us per tile of the longest split, each busy pair above 64
 // adding 0.3 % per tile (the pairs share HBM and L2); the combine adds
 // 0.015 us per partial row.  A part-filled single wave therefore beats
-// more, shorter splits: 64 sequences run fastest unsplit.
+// more, shorter splits: 64 sequences run fastest unsplit.  With more units
+// than pairs the kernel runs one pair per slot looping over units, which
+// halves the setup of the later units (128 sequences x 4 splits: 1.30 ms
+// against 1.34 ms); the estimate keeps the per-wave form, whose choices
+// were measured best for 16, 32, 64 and 128 sequences on either grid.
 double sm100_launch_us(int64_t pairs, int64_t tiles, int64_t s) {
   constexpr int64_t kSlots = kNumSms / 2;
   constexpr int64_t kQuietPairs = 64;
