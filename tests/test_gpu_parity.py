@@ -419,8 +419,11 @@ def _ragged_decode_case(h, B, max_len, seed):
     gen = torch.Generator(device="cuda").manual_seed(seed)
     page, width = 64, 576
     special = [0, 1, 63, 64, 127, 128, 129, max_len]
-    sl_l = special + torch.randint(0, max_len + 1, (B - len(special),), generator=gen,
-                                   device="cuda").tolist()
+    if B <= len(special):  # the longest ones
+        sl_l = special[len(special) - B:]
+    else:
+        sl_l = special + torch.randint(0, max_len + 1, (B - len(special),), generator=gen,
+                                       device="cuda").tolist()
     max_pages = (max_len + page - 1) // page
     pages = B * max_pages + 3
     cache = torch.randn(pages, page, width, device="cuda", generator=gen)
@@ -433,37 +436,40 @@ def _ragged_decode_case(h, B, max_len, seed):
     return q, cache, table, sl, sink
 
 
-# 100 x 128 heads to 8192 tokens: 2 splits, partials and the combine; 80
-# short sequences: one split, the kernel normalises and writes o itself
-@pytest.mark.parametrize("h,B,max_len", [(128, 100, 8192), (128, 80, 600)])
+# Decode rows run on the balanced schedule: each CTA pair takes an equal
+# range of all (row, head group) tiles, so rows are cut into pieces whose
+# partials the combine merges.  100 x 128 heads to 8192 tokens, 80 short
+# sequences, 16 sequences in up to 6 pieces, one sequence over 64 pairs, and
+# 256 heads (two head groups a row).
+@pytest.mark.parametrize("h,B,max_len", [(128, 100, 8192), (128, 80, 600), (128, 16, 8192),
+                                         (128, 1, 8192), (256, 24, 4096)])
 def test_decode_paged_two_cta_more_units_than_pairs(h, B, max_len):
-    """More work units (sequence x split) than CTA pairs fit on the device, so
-    each pair runs several units in turn, against the oracle."""
+    """Ragged sequences (empty, one token, page and tile edges, full length)
+    on the balanced schedule, against the oracle."""
     q, cache, table, sl, sink = _ragged_decode_case(h, B, max_len, 1000 + h + B)
     scale = 192 ** -0.5
     o = _decode_abi(q, cache, table, sl, sink, scale, 512, max_len)
     assert _lib.device_error() == 0
     ref = O.paged_decode_attn(n_bf16(q), n_bf16(cache), table.cpu().numpy(), sl.cpu().numpy(),
                               sink.cpu().numpy(), scale, 512)
-    assert_close_attn(f32(n_bf16(o)), f32(O.f32_to_bf16(ref)), f"units > pairs h{h} B{B}")
+    assert_close_attn(f32(n_bf16(o)), f32(O.f32_to_bf16(ref)), f"balanced h{h} B{B}")
 
 
-# (batch, sub-batch, max_len): 100 rows in 2 splits (200 units) against 4 x 25
-# rows (50 units each); 150 rows in one split against 3 x 50 rows.  The split
-# count of the full batch and of its sub-batches is the same.
-@pytest.mark.parametrize("h", [128, 16])
-@pytest.mark.parametrize("B,sub,max_len", [(100, 25, 2048), (150, 50, 600)])
-def test_decode_paged_units_loop_bit_exact(h, B, sub, max_len):
-    """A pair that runs several units in turn gives the same bits as one pair
-    per unit: the batch in one launch (more units than resident pairs) against
-    its sub-batches in separate launches (fewer units than pairs)."""
+# (heads, batch, sub-batch): 148 rows run 2 whole rows a pair, 74 rows one;
+# 74 rows of 256 heads are 148 (row, head group) pieces, 37 rows 74.  No row
+# is cut in either, so every row's arithmetic is the same.
+@pytest.mark.parametrize("h,B,sub", [(128, 148, 74), (16, 148, 74), (256, 74, 37)])
+def test_decode_paged_units_loop_bit_exact(h, B, sub):
+    """A pair that runs several rows in turn gives the same bits as a pair
+    that runs one: the batch in one launch against its halves."""
+    max_len = 2048
     q, cache, table, sl, sink = _ragged_decode_case(h, B, max_len, 2000 + h + B)
     scale = 192 ** -0.5
     whole = _decode_abi(q, cache, table, sl, sink, scale, 512, max_len)
     parts = torch.cat([_decode_abi(q[i:i + sub], cache, table[i:i + sub], sl[i:i + sub], sink,
                                    scale, 512, max_len) for i in range(0, B, sub)])
     assert _lib.device_error() == 0
-    assert torch.equal(whole, parts), "the unit loop changed the result"
+    assert torch.equal(whole, parts), "the pair's walk over rows changed the result"
     assert bool(torch.isfinite(whole.float()).all())
 
 
