@@ -480,8 +480,9 @@ __global__ void attn_combine_kernel(AttnArgs p) {
 // a split issued together: lane l holds dims 4l + 128k (k < 4), each
 // split's weight is computed once, and all four loads of a split precede its
 // arithmetic (two splits in flight).  An empty split (max -inf, its O never
-// written) is loaded and then discarded by a select, so its stale values
-// never enter the sums.  The arithmetic and its order are attn_combine_kernel's.
+// written) is not loaded (the predicate is the same for the whole warp) and
+// adds zeros, so stale values never enter the sums.  The arithmetic and its
+// order are attn_combine_kernel's.
 template <bool kF16>
 __global__ void __launch_bounds__(256) attn_combine512_kernel(AttnArgs p) {
   const int lane = threadIdx.x & 31;
@@ -524,7 +525,8 @@ __global__ void __launch_bounds__(256) attn_combine512_kernel(AttnArgs p) {
       const __half* src = reinterpret_cast<const __half*>(p.part_o) + e;
       uint2 u[4];
 #pragma unroll
-      for (int k = 0; k < 4; k++) u[k] = *reinterpret_cast<const uint2*>(src + 128 * k);
+      for (int k = 0; k < 4; k++)
+        u[k] = live ? *reinterpret_cast<const uint2*>(src + 128 * k) : make_uint2(0u, 0u);
       w = live ? exp2f(mi - M) * ml[i * ml_stride + 1] : 0.f;
 #pragma unroll
       for (int k = 0; k < 4; k++) {
@@ -539,7 +541,8 @@ __global__ void __launch_bounds__(256) attn_combine512_kernel(AttnArgs p) {
       const float* src = p.part_o + e;
       float4 f[4];
 #pragma unroll
-      for (int k = 0; k < 4; k++) f[k] = *reinterpret_cast<const float4*>(src + 128 * k);
+      for (int k = 0; k < 4; k++)
+        f[k] = live ? *reinterpret_cast<const float4*>(src + 128 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
       w = live ? exp2f(mi - M) : 0.f;
 #pragma unroll
       for (int k = 0; k < 4; k++) {

@@ -166,41 +166,6 @@ int sm100_splits(int64_t b, int64_t h, int64_t max_len) {
   return best;
 }
 
-// Balanced decode schedule of the pair kernel (one query token per
-// sequence): the tiles of every (row, 128-head group) at max_len, row after
-// row, are cut into one equal range per CTA pair (74, fewer when a range
-// would hold under 4 tiles).  A pair runs its range as pieces cut at row
-// ends, so no pair idles and none runs more than a few pieces; a row cut
-// into several pieces gets one partial slot per piece.  `splits` is the most
-// pieces of any row (the owner of tile x is the largest q with
-// floor(q G / P) <= x, as in the kernel).
-struct StreamPlan {
-  int64_t nt = 0, pairs = 0;
-  int splits = 0;  // 0: not applicable
-};
-
-StreamPlan sm100_stream_plan(int64_t rows, int64_t h, int64_t max_len) {
-  StreamPlan sp;
-  const int64_t hgroups = h >= 128 ? h / 128 : 1;
-  const int64_t nt = (max_len + 127) / 128;
-  const int64_t v = rows * hgroups;
-  if (v <= 0 || nt <= 0) return sp;
-  const int64_t g = v * nt;
-  int64_t pairs = kNumSms / 2;
-  if (pairs > g / 4) pairs = g / 4;
-  if (pairs < 1) pairs = 1;
-  int64_t most = 1;
-  for (int64_t i = 0; i < v; i++) {
-    const int64_t first = ((i * nt + 1) * pairs - 1) / g;
-    const int64_t last = ((i + 1) * nt * pairs - 1) / g;
-    if (last - first + 1 > most) most = last - first + 1;
-  }
-  sp.nt = nt;
-  sp.pairs = pairs;
-  sp.splits = (int)most;
-  return sp;
-}
-
 size_t attn_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int splits) {
   if (splits <= 1) return 0;
   return align256((size_t)rows * splits * h * d_v * 4) + align256((size_t)rows * splits * h * 2 * 4);
@@ -212,19 +177,7 @@ size_t attn_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int splits) {
 int run_decode_attn(AttnArgs a, void* ws, cudaStream_t st) {
   const bool sm100 = decode_attn_sm100_supported(a);
   const int64_t rows = a.b * a.s;
-  // decode rows of the pair kernel take the balanced schedule; prefill rows
-  // and fixed split ranges take the split count
-  StreamPlan sp;
-  if (sm100 && a.s == 1 && a.splits_total <= 0 && !a.peer)
-    sp = sm100_stream_plan(rows, a.h, a.max_len);
-  if (sp.splits > 0) {
-    a.stream = 1;
-    a.stream_nt = sp.nt;
-    a.stream_pairs = sp.pairs;
-    a.splits = sp.splits;
-  } else {
-    a.splits = sm100 ? sm100_splits(rows, a.h, a.max_len) : general_splits(rows, a.h, a.max_len);
-  }
+  a.splits = sm100 ? sm100_splits(rows, a.h, a.max_len) : general_splits(rows, a.h, a.max_len);
   const bool partials = a.splits > 1;
   if (partials) {
     // the pair kernel keeps its O partials as O / l in fp16 (half the bytes
@@ -246,13 +199,9 @@ int run_decode_attn(AttnArgs a, void* ws, cudaStream_t st) {
 }
 
 // Workspace of run_decode_attn for `rows` query tokens, whichever kernel runs.
-// (qlen = 1: decode rows, which the pair kernel runs on the balanced
-// schedule; qlen > 1: prefill rows, on the split count)
-size_t decode_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int64_t max_len, int64_t qlen) {
+size_t decode_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int64_t max_len) {
   const size_t w1 = attn_ws_bytes(rows, h, d_v, general_splits(rows, h, max_len));
-  const StreamPlan sp = qlen == 1 ? sm100_stream_plan(rows, h, max_len) : StreamPlan{};
-  const int pair_splits = sp.splits > 0 ? sp.splits : sm100_splits(rows, h, max_len);
-  const size_t w2 = attn_ws_bytes(rows, h, d_v, pair_splits);
+  const size_t w2 = attn_ws_bytes(rows, h, d_v, sm100_splits(rows, h, max_len));
   return w1 > w2 ? w1 : w2;
 }
 
@@ -450,7 +399,7 @@ int qcau_forward(const void* c_q, const void* wq_b, const void* wq_b_scale, int3
 }
 
 size_t qcau_decode_attn_workspace_size(int64_t b, int64_t h, int64_t d_v, int64_t max_seqlen) {
-  return decode_ws_bytes(b, h, d_v, max_seqlen, 1);
+  return decode_ws_bytes(b, h, d_v, max_seqlen);
 }
 
 int qcau_decode_attn_paged(const void* q, const void* cache, const int32_t* block_table,
@@ -583,7 +532,7 @@ int qcau_sparse_attn_fp8(const void* q, const void* kv_latent, const float* kv_s
 
 size_t qcau_prefill_attn_workspace_size(int64_t b, int64_t s, int64_t h, int64_t d_v,
                                         int64_t max_seqlen) {
-  return decode_ws_bytes(b * s, h, d_v, max_seqlen, s);
+  return decode_ws_bytes(b * s, h, d_v, max_seqlen);
 }
 
 int qcau_prefill_attn_paged(const void* q, const void* cache, const int32_t* block_table,
@@ -721,7 +670,7 @@ static MlaWs mla_ws(const qcau_mla_dims* d) {
   w.ov = off; off += align256(B * H * d->d_v * 2);
   w.xo = off; off += align256(B * H * d->d_v);
   w.so = off; off += align256(B * ((H * d->d_v) / 128) * 4);
-  w.attn = off; off += decode_ws_bytes(d->batch, d->n_heads, d->kv_lora, d->max_seqlen, 1);
+  w.attn = off; off += decode_ws_bytes(d->batch, d->n_heads, d->kv_lora, d->max_seqlen);
   w.total = off;
   return w;
 }
