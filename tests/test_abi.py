@@ -68,6 +68,23 @@ def test_sparse_attn_rejects_empty_kv():
     assert b"at least one latent row" in L.qcau_last_error()
 
 
+def test_decode_split_counts_measured_best():
+    """The two-CTA kernel's split counts at the shapes they were measured on
+    (128 heads, 512-wide values, B200), read back from the workspace the
+    decode entry asks for (fp32 O and (max, sum) partials per split): 128
+    sequences x 32K in 4 splits, 64 x 32K and 128 x 4K unsplit (the faster
+    choices over 8 and 4 splits), 16 x 32K in 4."""
+    L = _lib.lib()
+
+    def ws(b, splits):
+        return b * splits * 128 * (512 + 2) * 4 if splits > 1 else 0
+
+    assert L.qcau_decode_attn_workspace_size(128, 128, 512, 32768) == ws(128, 4)
+    assert L.qcau_decode_attn_workspace_size(64, 128, 512, 32768) == 0
+    assert L.qcau_decode_attn_workspace_size(128, 128, 512, 4096) == 0
+    assert L.qcau_decode_attn_workspace_size(16, 128, 512, 32768) == ws(16, 4)
+
+
 def test_workspace_errors_before_launch():
     L = _lib.lib()
     need = L.qcau_decode_attn_workspace_size(128, 128, 512, 32768)
