@@ -120,25 +120,25 @@ def cpu_reference(steps: int, warmup: int, threads: int):
     thread runs a head-shard sample of one decode token of the same workload:
     SAMPLE_HEADS of the 128 heads (q-up rows, attention heads and o-proj input
     columns of that shard), i.e. SAMPLE_HEADS/128 of the token's work, so a
-    step takes seconds instead of half a minute.  Returns (tok/s, sample)."""
+    step takes seconds instead of half a minute.  The inputs are generated
+    before the clock starts; only quant_gemm and sparse_attention are timed.
+    Returns (tok/s, sample)."""
     sys.path.insert(0, str(REPO / "oracle"))
     import oracle as O  # CPU checker / baseline only
 
     if not O.ref_available():
         return None, "oracle/_ref/qcau_ref not built"
     hs = SAMPLE_HEADS
-    args = (threads, threads, hs, WIDTH, CTX, DC, hs * 192, DIM)
-    for _ in range(warmup):
-        O.ref_bench_decode(*args)
-    secs = 0.0
-    for _ in range(steps):
-        secs += O.ref_bench_decode(*args)["seconds"]
+    r = O.ref_bench_decode(threads, threads, hs, WIDTH, CTX, DC, hs * 192, DIM,
+                           steps=steps, warmup=warmup)
+    secs = r["seconds"]
     frac = hs / HEADS
     sample = (f"per step each of {threads} threads runs {hs} of the {HEADS} heads of one decode "
               f"token ({frac:g} of its work): qcau_c quant_gemm q-up [1,{DC}]x[{hs * 192},{DC}], "
               f"sparse_attention over {CTX} rows x {hs} heads x {WIDTH} (the C++ port has one "
               f"width for K and V), quant_gemm o-proj [1,{hs * 128}]x[{DIM},{hs * 128}]; "
-              f"{steps} steps; tok/s = threads x {frac:g} / step time")
+              f"inputs generated before the clock; {warmup} untimed and {steps} timed steps; "
+              f"tok/s = threads x {frac:g} / step time")
     return threads * frac * steps / secs, sample
 
 

@@ -5,10 +5,14 @@
 // (Deepseek_origin/inference/kernel.py:276-352): fp32 scores, online softmax,
 // P rounded to bf16 before P.V, denominator summed from fp32 P; the sink and
 // the final normalisation are applied by attn_combine (kernel.py:345-348).
-// One deliberate difference in the schedule, not in the result: the running
-// max is only raised when a tile's max exceeds it by more than 2^8 (log2
-// units); P and the denominator then share that stale max, so O / l is the
-// same quotient and P stays <= 2^8 (bf16 rounding is scale-free).
+// The running max is the reference's: every tile that raises it rescales O
+// (in TMEM) and the denominator, so P is rounded to bf16 at the exact running
+// max and the tile's largest score gets P = 1 exactly, as kernel.py:331-343
+// computes.  (A stale max, raised only beyond a threshold, saves the O
+// rescales but rounds the dominant tokens' P at another scale; at 2^8 that
+// moved outputs of near-full-length rows up to 1 % from the reference.)  The
+// tile is 128 tokens where the reference's is 64: the max of the whole tile
+// scales both pages' P.
 //
 // Work unit = one sequence x one KV split x 128 heads, run by one CTA pair
 // (cluster of 2); tiles of 128 tokens (2 pages).  When the units outnumber the
@@ -70,7 +74,12 @@ constexpr int kVPerTile = 2;          // the tile's 2 pages
 constexpr int kQBytes = 9 * 8192;     // 64 heads x 576 bf16 (9 chunks of 64 rows)
 constexpr int kPBytes = 2 * 8192;     // 64 heads x 128 tokens bf16 (2 chunks of 64 tokens)
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kRescale = 8.0f;      // raise the running max only beyond 2^8
+// The running max (log2 units) is raised when a tile's max exceeds it by more
+// than kRescale; 0 is the reference's exact running max per tile.
+#ifndef QCAU_DECODE_RESCALE_LOG2
+#define QCAU_DECODE_RESCALE_LOG2 0.0f
+#endif
+constexpr float kRescale = QCAU_DECODE_RESCALE_LOG2;
 
 constexpr uint32_t kTmemO = 0;        // 2 accumulators x 128 columns
 constexpr uint32_t kTmemS = 256;      // 2 buffers x 64 columns
@@ -529,17 +538,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         l_run = l_run * alpha + ps;
         if (__any_sync(0xffffffffu, resc)) {
-          // rescale this warp's rows of O (PV(t-1) is complete)
+          // rescale this warp's rows of O (PV(t-1) is complete): 256 columns
+          // in two rounds of four loads in flight
           tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < 8; c++) {
-            float v[32];
-            const uint32_t ta = tmem + lane_base + kTmemO + c * 32;
-            tmem_ld32(ta, v);
-            tmem_ld_wait();
+          for (int c0 = 0; c0 < 8; c0 += 4) {
+            float o[4][32];
+            const uint32_t ta = tmem + lane_base + kTmemO + c0 * 32;
 #pragma unroll
-            for (int i = 0; i < 32; i++) v[i] *= alpha;
-            tmem_st32(ta, v);
+            for (int c = 0; c < 4; c++) tmem_ld32(ta + c * 32, o[c]);
+#pragma unroll
+            for (int c = 0; c < 4; c++) tmem_ld_wait_regs(o[c]);
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+#pragma unroll
+              for (int i = 0; i < 32; i++) o[c][i] *= alpha;
+              tmem_st32(ta + c * 32, o[c]);
+            }
           }
           tmem_st_wait();
         }
@@ -570,7 +585,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 8; c++) {
           float v[32];
           tmem_ld32(tmem + lane_base + kTmemO + c * 32, v);
-          tmem_ld_wait();
+          tmem_ld_wait_regs(v);
           uint4* dst = reinterpret_cast<uint4*>(po + (c >> 2) * 128 + (c & 3) * 32);
           if (hl < p.cta_heads) {
 #pragma unroll
@@ -592,7 +607,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 8; c++) {
           float v[32];
           tmem_ld32(tmem + lane_base + kTmemO + c * 32, v);
-          tmem_ld_wait();
+          tmem_ld_wait_regs(v);
           const int64_t e = po + (c >> 2) * 128 + (c & 3) * 32;
           if (hl < p.cta_heads) {
             if (p.part_f16) {  // O / l in fp16: half the bytes, 2^-11 relative error

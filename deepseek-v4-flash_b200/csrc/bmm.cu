@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c4 = 0; c4 < BN / 32; c4++) {
         float v[32];
         tmem_ld32(taddr + c4 * 32, v);
-        tmem_ld_wait();
+        tmem_ld_wait_regs(v);
         if (row < m) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c4 * 32);
 #pragma unroll

@@ -2,6 +2,7 @@
 // reporting, workspace layout and the orchestration of the multi-kernel
 // entry points.  No entry point synchronises the host or allocates device
 // memory; qcau_device_error() is the only call that synchronises.
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -43,18 +44,25 @@ __device__ int g_qcau_device_error;
 
 namespace qcau {
 
+// The address is resolved once per device and kept for the life of the
+// process (a reset of the device's primary context is not supported).
 int* device_error_word() {
   static std::mutex mu;
-  static int* addr[64] = {nullptr};
+  static std::atomic<int*> addr[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (addr[dev]) return addr[dev];
+  int* a = addr[dev].load(std::memory_order_acquire);
+  if (a) return a;
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
+  a = addr[dev].load(std::memory_order_relaxed);
+  if (!a) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_qcau_device_error) == cudaSuccess) addr[dev] = (int*)p;
+    if (cudaGetSymbolAddress(&p, g_qcau_device_error) == cudaSuccess) {
+      a = (int*)p;
+      addr[dev].store(a, std::memory_order_release);
+    }
   }
-  return addr[dev];
+  return a;
 }
 
 // ---------------------------------------------------------------- TMA descriptors
@@ -580,7 +588,8 @@ int qcau_prefill_attn_paged(const void* q, const void* cache, const int32_t* blo
 static __device__ __align__(256) uint8_t g_decode_scratch[QCAU_DECODE_STATIC_SCRATCH_BYTES];
 
 // Address of g_decode_scratch on the current device, resolved once per device
-// with that device current.
+// with that device current and kept for the life of the process (a reset of
+// the device's primary context is not supported).
 static int decode_scratch_address(void** out) {
   static std::mutex mu;
   static void* addr[64] = {nullptr};

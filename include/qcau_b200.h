@@ -262,8 +262,11 @@ int qcau_prefill_attn_paged(const void* q, const void* cache,
  *   > QCAU_DECODE_STATIC_SCRATCH_BYTES, e.g. batch 128 x 128 heads at 32K
  *   context) are rejected with QCAU_ERR_WORKSPACE before any device work.
  *   The scratch address is resolved once per device (cudaGetSymbolAddress
- *   with that device current); make the first call on each device outside
- *   any stream capture.  Nothing in the scratch must start at zero: every
+ *   with that device current) and kept until the process exits; make the
+ *   first call on each device outside any stream capture.  A reset of the
+ *   device's primary context (cudaDeviceReset) while the library is loaded
+ *   is not supported: the kept address would be stale.  Nothing in the
+ *   scratch must start at zero: every
  *   partial row the combine reads is written earlier in the same call.
  *   There is ONE scratch per device: calls whose executions overlap on the
  *   same device (two streams, or two host threads) race on it and give

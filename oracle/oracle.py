@@ -264,9 +264,11 @@ def ref_quant_gemm(a_f32, sa, w_f32, sw) -> np.ndarray:
 
 
 def ref_bench_decode(threads: int, seqs: int, heads: int, width: int, ctx: int,
-                     dc: int, nq: int, no: int) -> dict:
-    """Time qcau_c on `seqs` decode tokens (one per sequence) on `threads` cores."""
+                     dc: int, nq: int, no: int, steps: int = 1, warmup: int = 0) -> dict:
+    """Time qcau_c on `seqs` decode tokens (one per sequence) on `threads` cores:
+    inputs generated first, then `warmup` untimed and `steps` timed steps."""
     out = subprocess.run([str(REF_BIN), "bench_decode", str(threads), str(seqs), str(heads),
-                          str(width), str(ctx), str(dc), str(nq), str(no)],
+                          str(width), str(ctx), str(dc), str(nq), str(no), str(steps),
+                          str(warmup)],
                          check=True, capture_output=True, text=True)
     return json.loads(out.stdout.strip().splitlines()[-1])

@@ -15,11 +15,13 @@
 //       main.cpp:9-24), dir/sa.bin [S,Dc/128] f32, dir/w.bin [N,Dc] bf16-held
 //       fp8 values, dir/sw.bin [N/128,Dc/128] f32 -> dir/out.bin [S,N] bf16
 //       calls quant_gemm (qcau.cpp:30-90).
-//   qcau_ref bench_decode THREADS SEQS H C CTX DC NQ NO
+//   qcau_ref bench_decode THREADS SEQS H C CTX DC NQ NO [STEPS [WARMUP]]
 //       times one decode token per sequence: quant_gemm q-up [1,DC]x[NQ,DC],
 //       sparse_attention over CTX rows with H heads of width C, quant_gemm
 //       o-proj [1,H*128]x[NO,H*128]; SEQS sequences spread over THREADS
-//       std::threads.  Prints one JSON line with the seconds.
+//       std::threads.  The inputs are generated before the clock starts;
+//       WARMUP untimed steps, then STEPS timed ones.  Prints one JSON line
+//       with the total seconds and each step's.
 #include "Core.h"
 #include "qcau.cpp"
 
@@ -87,60 +89,107 @@ static int mode_qgemm(int argc, char** argv) {
     return 0;
 }
 
-// One decode token of one sequence through the reference's C++ kernels.
-static void one_token(int H, int C, int ctx, int Dc, int NQ, int NO, unsigned seed) {
-    std::mt19937 g(seed);
-    std::normal_distribution<float> nd(0.f, 1.f);
-    int no_in = H * 128;
-    Tensor<__bf16> a(Shape(1, 1, Dc));
-    Tensor<float> sa(Shape(1, 1, Dc / 128));
-    Tensor<__bf16> wq(Shape(1, NQ, Dc));
-    Tensor<float> swq(Shape(1, NQ / 128, Dc / 128));
-    for (int i = 0; i < Dc; i++) a.raw()[i] = (__bf16)nd(g);
-    for (int i = 0; i < Dc / 128; i++) sa.raw()[i] = 1.0f / 64;
-    for (long i = 0; i < (long)NQ * Dc; i++) wq.raw()[i] = (__bf16)(nd(g) * 8.0f);
-    for (int i = 0; i < (NQ / 128) * (Dc / 128); i++) swq.raw()[i] = 1.0f / 512;
-    Tensor<__bf16> qp(Shape(1, 1, NQ));
-    quant_gemm(a, wq, sa, swq, true, false, qp);
+// The inputs of one decode token of one sequence, generated before any
+// timing (seeded normal values, the reference's bf16-held fp8 convention for
+// the GEMM operands), and the buffers its outputs go to.
+struct TokenData {
+    int H, C, ctx, Dc, NQ, NO;
+    std::vector<__bf16> a, wq, qp, q, kv, o, ao, wo, y;
+    std::vector<float> sa, swq, sink, sao, swo;
+    std::vector<int> idx;
 
-    Tensor<__bf16> q(Shape(1, H, C));
-    for (int i = 0; i < H * C; i++) q.raw()[i] = (__bf16)nd(g);
-    Tensor<__bf16> kv(Shape(1, ctx, C));
-    for (long i = 0; i < (long)ctx * C; i++) kv.raw()[i] = (__bf16)nd(g);
-    Tensor<int> idx(Shape(1, 1, ctx));
-    for (int i = 0; i < ctx; i++) idx.raw()[i] = i;
-    Tensor<float> sink(Shape(1, H, 1));
-    for (int i = 0; i < H; i++) sink.raw()[i] = -1e30f;
-    Tensor<__bf16> o(Shape(1, H, C));
-    sparse_attention(q, kv, sink, idx, o);
+    TokenData(int H_, int C_, int ctx_, int Dc_, int NQ_, int NO_, unsigned seed)
+        : H(H_), C(C_), ctx(ctx_), Dc(Dc_), NQ(NQ_), NO(NO_) {
+        std::mt19937 g(seed);
+        std::normal_distribution<float> nd(0.f, 1.f);
+        const int no_in = H * 128;
+        auto fill = [&](std::vector<__bf16>& v, size_t n, float k) {
+            v.resize(n);
+            for (auto& x : v) x = (__bf16)(nd(g) * k);
+        };
+        fill(a, (size_t)Dc, 1.f);
+        sa.assign(Dc / 128, 1.0f / 64);
+        fill(wq, (size_t)NQ * Dc, 8.f);
+        swq.assign((size_t)(NQ / 128) * (Dc / 128), 1.0f / 512);
+        qp.assign(NQ, (__bf16)0.f);
+        fill(q, (size_t)H * C, 1.f);
+        fill(kv, (size_t)ctx * C, 1.f);
+        idx.resize(ctx);
+        for (int i = 0; i < ctx; i++) idx[i] = i;
+        sink.assign(H, -1e30f);
+        o.assign((size_t)H * C, (__bf16)0.f);
+        fill(ao, (size_t)no_in, 1.f);
+        sao.assign(no_in / 128, 1.0f / 64);
+        fill(wo, (size_t)NO * no_in, 8.f);
+        swo.assign((size_t)(NO / 128) * (no_in / 128), 1.0f / 512);
+        y.assign(NO, (__bf16)0.f);
+    }
 
-    Tensor<__bf16> ao(Shape(1, 1, no_in));
-    for (int i = 0; i < no_in; i++) ao.raw()[i] = (__bf16)nd(g);
-    Tensor<float> sao(Shape(1, 1, no_in / 128));
-    for (int i = 0; i < no_in / 128; i++) sao.raw()[i] = 1.0f / 64;
-    Tensor<__bf16> wo(Shape(1, NO, no_in));
-    for (long i = 0; i < (long)NO * no_in; i++) wo.raw()[i] = (__bf16)(nd(g) * 8.0f);
-    Tensor<float> swo(Shape(1, NO / 128, no_in / 128));
-    for (int i = 0; i < (NO / 128) * (no_in / 128); i++) swo.raw()[i] = 1.0f / 512;
-    Tensor<__bf16> y(Shape(1, 1, NO));
-    quant_gemm(ao, wo, sao, swo, true, false, y);
-}
+    // The reference's work for the token: quant_gemm q-up (qcau.cpp:30-90),
+    // sparse_attention over all ctx rows (qcau.cpp:169-284), quant_gemm o-proj.
+    void run() {
+        const int no_in = H * 128;
+        Tensor<__bf16> ta(a.data(), Shape(1, 1, Dc), false);
+        Tensor<float> tsa(sa.data(), Shape(1, 1, Dc / 128), false);
+        Tensor<__bf16> twq(wq.data(), Shape(1, NQ, Dc), false);
+        Tensor<float> tswq(swq.data(), Shape(1, NQ / 128, Dc / 128), false);
+        Tensor<__bf16> tqp(qp.data(), Shape(1, 1, NQ), false);
+        quant_gemm(ta, twq, tsa, tswq, true, false, tqp);
+        Tensor<__bf16> tq(q.data(), Shape(1, H, C), false);
+        Tensor<__bf16> tkv(kv.data(), Shape(1, ctx, C), false);
+        Tensor<int> tidx(idx.data(), Shape(1, 1, ctx), false);
+        Tensor<float> tsink(sink.data(), Shape(1, H, 1), false);
+        Tensor<__bf16> to(o.data(), Shape(1, H, C), false);
+        sparse_attention(tq, tkv, tsink, tidx, to);
+        Tensor<__bf16> tao(ao.data(), Shape(1, 1, no_in), false);
+        Tensor<float> tsao(sao.data(), Shape(1, 1, no_in / 128), false);
+        Tensor<__bf16> two(wo.data(), Shape(1, NO, no_in), false);
+        Tensor<float> tswo(swo.data(), Shape(1, NO / 128, no_in / 128), false);
+        Tensor<__bf16> ty(y.data(), Shape(1, 1, NO), false);
+        quant_gemm(tao, two, tsao, tswo, true, false, ty);
+    }
+};
 
+// Every thread builds the inputs of its sequences first; the clock runs only
+// over the reference's compute.  WARMUP untimed steps, then STEPS timed ones;
+// a step is one decode token of each of SEQS sequences over THREADS threads.
 static int mode_bench_decode(int argc, char** argv) {
     if (argc < 10) return 1;
     int threads = atoi(argv[2]), seqs = atoi(argv[3]), H = atoi(argv[4]), C = atoi(argv[5]);
     int ctx = atoi(argv[6]), Dc = atoi(argv[7]), NQ = atoi(argv[8]), NO = atoi(argv[9]);
-    auto t0 = std::chrono::steady_clock::now();
-    std::vector<std::thread> pool;
-    for (int t = 0; t < threads; t++) {
-        pool.emplace_back([=]() {
-            for (int s = t; s < seqs; s += threads) one_token(H, C, ctx, Dc, NQ, NO, 1234u + s);
-        });
+    int steps = argc > 10 ? atoi(argv[10]) : 1, warmup = argc > 11 ? atoi(argv[11]) : 0;
+    std::vector<std::vector<TokenData>> data(threads);
+    {
+        std::vector<std::thread> pool;
+        for (int t = 0; t < threads; t++)
+            pool.emplace_back([&, t]() {
+                for (int s = t; s < seqs; s += threads)
+                    data[t].emplace_back(H, C, ctx, Dc, NQ, NO, 1234u + s);
+            });
+        for (auto& th : pool) th.join();
     }
-    for (auto& th : pool) th.join();
-    auto t1 = std::chrono::steady_clock::now();
-    double sec = std::chrono::duration<double>(t1 - t0).count();
-    printf("{\"seconds\": %.6f, \"seqs\": %d, \"threads\": %d}\n", sec, seqs, threads);
+    auto one_step = [&]() {
+        std::vector<std::thread> pool;
+        for (int t = 0; t < threads; t++)
+            pool.emplace_back([&, t]() {
+                for (auto& d : data[t]) d.run();
+            });
+        for (auto& th : pool) th.join();
+    };
+    for (int w = 0; w < warmup; w++) one_step();
+    std::vector<double> per;
+    for (int k = 0; k < steps; k++) {
+        auto t0 = std::chrono::steady_clock::now();
+        one_step();
+        auto t1 = std::chrono::steady_clock::now();
+        per.push_back(std::chrono::duration<double>(t1 - t0).count());
+    }
+    double sec = 0;
+    for (double x : per) sec += x;
+    printf("{\"seconds\": %.6f, \"steps\": %d, \"seqs\": %d, \"threads\": %d, \"step_seconds\": [",
+           sec, steps, seqs, threads);
+    for (size_t i = 0; i < per.size(); i++) printf("%s%.6f", i ? ", " : "", per[i]);
+    printf("]}\n");
     return 0;
 }
 

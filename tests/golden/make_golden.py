@@ -1,8 +1,10 @@
 """Generate the committed golden fixtures under tests/golden/.
 
-Run in a container that has the reference checkout at /root/reference:
+Run where the reference checkout is readable; its root is taken from
+QCAU_REFERENCE_ROOT, else a directory named `reference` beside this
+repository's parent:
 
-    python tests/golden/make_golden.py
+    QCAU_REFERENCE_ROOT=<reference root> python tests/golden/make_golden.py
 
 Outputs (compressed .npz, raw bit patterns: bf16 as uint16, fp8/e8m0 as uint8):
 
@@ -27,13 +29,15 @@ from __future__ import annotations
 
 import importlib.util
 import json
+import os
 import sys
 from pathlib import Path
 
 import numpy as np
 import torch
 
-REF = Path("/root/reference")
+REF = Path(os.environ.get("QCAU_REFERENCE_ROOT") or
+           Path(__file__).resolve().parents[3] / "reference")
 FW = REF / "QCAU/QCAU_inference/framework"
 VEC = FW / "test_vectors"
 INF = REF / "QCAU/QCAU_inference/inference"
@@ -219,7 +223,7 @@ def synthetic():
 
 if __name__ == "__main__":
     if not VEC.exists():
-        sys.exit("reference test vectors not found under /root/reference")
+        sys.exit(f"reference test vectors not found under {REF} (set QCAU_REFERENCE_ROOT)")
     goldens()
     synthetic()
     for f in sorted(OUT.glob("*.npz")):

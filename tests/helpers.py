@@ -3,11 +3,13 @@ tolerance checks used throughout.
 
 Tolerances (stated once, used by every floating-point parity test):
   * attention / QCAU / decode-layer outputs: cosine >= 0.999 and
-    max |diff| <= 2e-2 * RMS(reference)   (the bar stated for this path),
-    where an element may also differ by one bf16 ulp of its reference value:
-    for peaked attention an output element can be ~10x the RMS, and one bf16
-    rounding step of it (2^-8 relative) then exceeds 2e-2 * RMS even though
-    both sides are correctly rounded;
+    max |diff| <= 2e-2 * RMS(reference)   (the bar stated for this path).
+    With strict=False an element may also differ by one bf16 ulp of its
+    reference value: for peaked attention an output element can be ~10x the
+    RMS, and one bf16 rounding step of it (2^-8 relative) then exceeds
+    2e-2 * RMS even though both sides are correctly rounded.  The number of
+    elements that pass only through that allowance is recorded
+    (ULP_ONLY_LOG) and returned; strict=True allows none;
   * GEMM-only outputs additionally: >= 99% of bf16 values within one ulp.
 Integer / byte outputs (FP8 codes, E8M0 scales) must be bit-exact.
 """
@@ -49,8 +51,16 @@ def cosine(a, b) -> float:
     return float(a @ b / (na * nb + 1e-300))
 
 
-def assert_close_attn(got, ref, what=""):
-    """The path's floating-point bar: cosine >= 0.999, max-abs <= 2e-2 * RMS."""
+# (what, elements within 1 bf16 ulp but beyond 2e-2 * RMS, total elements) of
+# every non-strict comparison that needed the allowance
+ULP_ONLY_LOG: list = []
+
+
+def assert_close_attn(got, ref, what="", strict=False):
+    """The path's floating-point bar: cosine >= 0.999, max-abs <= 2e-2 * RMS.
+
+    Returns (cosine, max |diff|, n_ulp_only): the elements that pass only by
+    the one-ulp allowance (always 0 with strict=True)."""
     got = np.asarray(got, dtype=np.float32)
     ref = np.asarray(ref, dtype=np.float32)
     assert got.shape == ref.shape, (what, got.shape, ref.shape)
@@ -60,9 +70,18 @@ def assert_close_attn(got, ref, what=""):
     diff = np.abs(got - ref)
     m = float(diff.max()) if got.size else 0.0
     assert c >= COS_MIN, f"{what}: cosine {c}"
+    bar = np.float32(MAXABS_RMS * max(rms, 1e-6))
+    beyond = diff > bar
+    if strict:
+        bad = int(np.sum(beyond))
+        assert bad == 0, (f"{what}: {bad} elements beyond 2e-2*rms; max|diff| {m}, "
+                          f"rms {rms}, max|diff|/rms {m / max(rms, 1e-30):.4f}")
+        return c, m, 0
     ulp = np.spacing(np.abs(ref).astype(np.float32)) * np.float32(65536.0)  # bf16 ulp
-    tol = np.maximum(np.float32(MAXABS_RMS * max(rms, 1e-6)), ulp)
-    bad = int(np.sum(diff > tol))
+    bad = int(np.sum(beyond & (diff > ulp)))
     assert bad == 0, (f"{what}: {bad} elements beyond max(2e-2*rms, 1 bf16 ulp); "
                       f"max|diff| {m}, rms {rms}")
-    return c, m
+    n_ulp = int(np.sum(beyond))
+    if n_ulp:
+        ULP_ONLY_LOG.append((what, n_ulp, int(got.size)))
+    return c, m, n_ulp

@@ -1,12 +1,26 @@
 """C ABI checks that need no GPU: the library loads, exports exactly what the
 header declares, and rejects bad arguments with the reference's error kinds
-before touching the device."""
+before touching the device.
+
+The pointer arguments are real host buffers.  With a CUDA device present
+the argument checks are left to the GPU tests, which pass real device
+buffers: a call that reached a launch here would hand a kernel host memory.
+"""
 import re
 from pathlib import Path
 
+import numpy as np
 import pytest
+import torch
 
 from qcau_b200 import _lib
+
+# eight 1 MiB host buffers standing for the calls' tensors
+_HOST = [np.zeros(1 << 20, dtype=np.uint8) for _ in range(8)]
+P = [int(a.ctypes.data) for a in _HOST]
+
+no_device = pytest.mark.skipif(torch.cuda.is_available(),
+                               reason="argument checks with host buffers run without a device")
 
 HEADER = Path(__file__).resolve().parent.parent / "include" / "qcau_b200.h"
 
@@ -35,35 +49,39 @@ def _expect(rc, exc):
         _lib.check(rc, "call")
 
 
+@no_device
 def test_act_quant_rejects_bad_block():
     L = _lib.lib()
-    rc = L.qcau_act_quant(16, 32, 64, 4, 100, 128, 0, 0, 0, None)
+    rc = L.qcau_act_quant(P[0], P[1], P[2], 4, 100, 128, 0, 0, 0, None)
     _expect(rc, ValueError)
     assert b"divisible" in L.qcau_last_error()
-    rc = L.qcau_act_quant(16, 32, 64, 4, 128, 96, 0, 0, 0, None)
+    rc = L.qcau_act_quant(P[0], P[1], P[2], 4, 128, 96, 0, 0, 0, None)
     _expect(rc, ValueError)
-    rc = L.qcau_act_quant(16, 32, 64, 4, 128, 128, 0, 1, 0, None)  # e8m0 needs round_scale
+    rc = L.qcau_act_quant(P[0], P[1], P[2], 4, 128, 128, 0, 1, 0, None)  # e8m0 needs round_scale
     _expect(rc, ValueError)
 
 
+@no_device
 def test_fp8_gemm_rejects_bad_k():
     L = _lib.lib()
-    rc = L.qcau_fp8_gemm(16, 16, 16, 16, 16, 4, 128, 100, 0, 0, None)
+    rc = L.qcau_fp8_gemm(P[0], P[1], P[2], P[3], P[4], 4, 128, 100, 0, 0, None)
     _expect(rc, ValueError)
     assert b"multiple of 128" in L.qcau_last_error()
 
 
+@no_device
 def test_attention_widths_unsupported_raise_not_implemented():
     L = _lib.lib()
-    rc = L.qcau_sparse_attn(16, 16, None, 16, 16, 1, 1, 4, 8, 8, 8, 4, 2, 1.0, 0, None, 0, 0, 0,
-                            None)
+    rc = L.qcau_sparse_attn(P[0], P[1], None, P[2], P[3], 1, 1, 4, 8, 8, 8, 4, 2, 1.0, 0, None, 0,
+                            0, 0, None)
     _expect(rc, NotImplementedError)
 
 
+@no_device
 def test_sparse_attn_rejects_empty_kv():
     L = _lib.lib()
-    rc = L.qcau_sparse_attn(16, 16, None, 16, 16, 1, 1, 4, 512, 512, 512, 0, 2, 1.0, 0, None, 0,
-                            0, 0, None)
+    rc = L.qcau_sparse_attn(P[0], P[1], None, P[2], P[3], 1, 1, 4, 512, 512, 512, 0, 2, 1.0, 0,
+                            None, 0, 0, 0, None)
     _expect(rc, ValueError)
     assert b"at least one latent row" in L.qcau_last_error()
 
@@ -85,29 +103,32 @@ def test_decode_split_counts_measured_best():
     assert L.qcau_decode_attn_workspace_size(16, 128, 512, 32768) == ws(16, 4)
 
 
+@no_device
 def test_workspace_errors_before_launch():
     L = _lib.lib()
     need = L.qcau_decode_attn_workspace_size(128, 128, 512, 32768)
     assert need > 0
-    rc = L.qcau_decode_attn_paged(16, 16, 16, 16, None, 16, 128, 128, 576, 512, 576, 64, 512,
-                                  65536, 32768, 0.07, 16, need - 1, None)
+    rc = L.qcau_decode_attn_paged(P[0], P[1], P[2], P[3], None, P[4], 128, 128, 576, 512, 576, 64,
+                                  512, 65536, 32768, 0.07, P[5], need - 1, None)
     _expect(rc, ValueError)
     assert b"workspace too small" in L.qcau_last_error()
 
 
+@no_device
 def test_forward_freqs_coverage_error():
     L = _lib.lib()
-    rc = L.qcau_forward(16, 16, 16, 0, 1, None, 16, 16, 16, 16, 16, 1, 4, 2, 512, 1024, 8, 8,
-                        64, 3, 0, 1e-6, 0.04, 16, 1 << 30, None)
+    rc = L.qcau_forward(P[0], P[1], P[2], 0, 1, None, P[3], P[4], P[5], P[6], P[7], 1, 4, 2, 512,
+                        1024, 8, 8, 64, 3, 0, 1e-6, 0.04, P[0], 1 << 20, None)
     _expect(rc, ValueError)
     assert b"freqs_cis" in L.qcau_last_error()
 
 
+@no_device
 def test_mla_decode_rejects_bad_layout():
     L = _lib.lib()
     d = _lib.MlaDims(batch=4, n_heads=16, dc=1536, d_nope=64, d_rope=64, kv_lora=512, d_v=128,
                      dim=7168, page_size=64, max_pages=4, num_pages=16, max_seqlen=256,
                      npos=512, softmax_scale=0.07, w_scale_dtype=0, act_round_scale=0,
                      out_dtype=0)
-    rc = L.qcau_mla_decode(d, *([16] * 12), 16, 1 << 30, None)
+    rc = L.qcau_mla_decode(d, *(P + P[:4]), P[4], 1 << 20, None)
     _expect(rc, ValueError)

@@ -78,6 +78,9 @@ def test_noalloc_matches_workspace_entry_point_twice(h, first, second):
     c2["o"].fill_(0)
     torch.cuda.synchronize()
 
+    # The first call on a device resolves the scratch's device address; the
+    # array itself was placed when the library's module was loaded (the
+    # workspace calls above already loaded it), so it is not counted here.
     _noalloc(c1)
     torch.cuda.synchronize()
     free_before = torch.cuda.mem_get_info()[0]
@@ -91,13 +94,30 @@ def test_noalloc_matches_workspace_entry_point_twice(h, first, second):
     assert _lib.device_error() == 0
 
 
+@pytest.mark.gpu
 def test_noalloc_rejects_oversize_before_launch():
-    """batch 128 x 128 heads at 32K context needs ~134 MB of partials."""
+    """batch 128 x 128 heads at 32K context needs ~134 MB of partials, more
+    than the static scratch holds: the call is refused before any launch.
+    Every buffer is a real allocation of the size the call names (a one-page
+    cache that the all-zero block table points at), so the only thing wrong
+    with the call is the scratch size."""
     L = _lib.lib()
-    need = L.qcau_decode_attn_workspace_size(128, 128, D_V, 32768)
+    b, h, ctx = 128, 128, 32768
+    need = L.qcau_decode_attn_workspace_size(b, h, D_V, ctx)
     assert need > _lib.DECODE_STATIC_SCRATCH_BYTES
-    rc = L.qcau_decode_attn_paged_noalloc(16, 16, 16, 16, None, 16, 128, 128, WIDTH, D_V, WIDTH,
-                                          PAGE, 512, 65536, 32768, 0.07, None)
+    q = torch.zeros(b, h, WIDTH, device="cuda", dtype=torch.bfloat16)
+    o = torch.empty(b, h, D_V, device="cuda", dtype=torch.bfloat16)
+    cache = torch.zeros(1, PAGE, WIDTH, device="cuda", dtype=torch.bfloat16)
+    table = torch.zeros(b, ctx // PAGE, device="cuda", dtype=torch.int32)
+    seqlens = torch.full((b,), ctx, device="cuda", dtype=torch.int32)
+    o.fill_(1.0)
+    torch.cuda.synchronize()
+    rc = L.qcau_decode_attn_paged_noalloc(q.data_ptr(), cache.data_ptr(), table.data_ptr(),
+                                          seqlens.data_ptr(), None, o.data_ptr(), b, h, WIDTH,
+                                          D_V, WIDTH, PAGE, table.size(1), cache.size(0), ctx,
+                                          0.07, _lib.stream_ptr())
     with pytest.raises(ValueError, match="static scratch"):
         _lib.check(rc, "decode_attn_paged_noalloc")
     assert str(need).encode() in L.qcau_last_error()
+    torch.cuda.synchronize()
+    assert bool((o == 1.0).all()), "the refused call wrote its output"
