@@ -2,6 +2,7 @@
 // reporting, workspace layout and the orchestration of the multi-kernel
 // entry points.  No entry point synchronises the host or allocates device
 // memory; qcau_device_error() is the only call that synchronises.
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -174,22 +175,70 @@ int sm100_splits(int64_t b, int64_t h, int64_t max_len) {
   return best;
 }
 
+// Splits of the tcgen05 gather kernel: one CTA (one per SM) per (query row,
+// head group, split); the count minimises waves x (set-up + tiles of 64 rows
+// per split), the set-up (TMEM, barriers, Q, the first gathers) worth about
+// three tiles, plus one tile's worth for the merge of several splits.
+int gather_splits(int64_t rows, int64_t h, int64_t d_qk, int64_t max_len) {
+  const int nh = gather_heads_per_cta(h, d_qk);
+  const int64_t ctas = rows * ((h + nh - 1) / nh);
+  const int64_t tiles = max_len > 0 ? (max_len + 63) / 64 : 1;
+  int best = 1;
+  double best_cost = 1e300;
+  for (int s = 1; s <= 64 && s <= tiles; s++) {
+    const int64_t units = ctas * s;
+    const double waves = (double)((units + kNumSms - 1) / kNumSms);
+    const double cost = waves * (3.0 + (double)((tiles + s - 1) / s)) + (s > 1 ? 1.0 : 0.0);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
+// Gathered-row attention: the tcgen05 gather kernel where it takes the shape,
+// else the general split-KV kernel.
+cudaError_t run_gather(const AttnArgs& a, cudaStream_t st) {
+  if (attn_gather_sm100_supported(a)) return launch_attn_gather_sm100(a, st);
+  return launch_attn_general(a, st);
+}
+
 size_t attn_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int splits) {
   if (splits <= 1) return 0;
   return align256((size_t)rows * splits * h * d_v * 4) + align256((size_t)rows * splits * h * 2 * 4);
 }
 
+// Workspace of run_decode_attn for `rows` query tokens.  Head counts that
+// the two-CTA kernel takes (with 576-wide keys and 64-token pages) are sized
+// for its split count; the gather kernel, which runs the other shapes, caps
+// its split count to the same size.
+size_t decode_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int64_t max_len) {
+  const bool pair_heads = d_v == 512 && (h % 128 == 0 || h == 64 || h == 32 || h == 16);
+  if (pair_heads) return attn_ws_bytes(rows, h, d_v, sm100_splits(rows, h, max_len));
+  return attn_ws_bytes(rows, h, d_v,
+                       std::max(gather_splits(rows, h, 576, max_len),
+                                gather_splits(rows, h, 512, max_len)));
+}
+
 // Runs paged attention for a.b sequences x a.s query tokens (s = 1: decode;
 // s > 1: token t sees the prefix up to its own position) with partials in
-// `ws` when the KV range is split (size checked by the caller).
+// `ws` when the KV range is split (its size, decode_ws_bytes, checked by the
+// caller).
 int run_decode_attn(AttnArgs a, void* ws, cudaStream_t st) {
   const bool sm100 = decode_attn_sm100_supported(a);
   const int64_t rows = a.b * a.s;
-  a.splits = sm100 ? sm100_splits(rows, a.h, a.max_len) : general_splits(rows, a.h, a.max_len);
+  if (sm100) {
+    a.splits = sm100_splits(rows, a.h, a.max_len);
+  } else {
+    a.splits = gather_splits(rows, a.h, a.d_qk, a.max_len);
+    const size_t room = decode_ws_bytes(rows, a.h, a.d_v, a.max_len);
+    while (a.splits > 1 && attn_ws_bytes(rows, a.h, a.d_v, a.splits) > room) a.splits--;
+  }
   const bool partials = a.splits > 1;
   if (partials) {
     // the pair kernel keeps its O partials as O / l in fp16 (half the bytes
-    // written and merged; the workspace is sized for fp32, the general
+    // written and merged; the workspace is sized for fp32, the gather
     // kernel's format)
     a.part_f16 = sm100 ? 1 : 0;
     a.part_o = reinterpret_cast<float*>(ws);
@@ -200,17 +249,10 @@ int run_decode_attn(AttnArgs a, void* ws, cudaStream_t st) {
   if (sm100) {
     QCAU_CHECK_CUDA(launch_decode_attn_sm100(a, st));
   } else {
-    QCAU_CHECK_CUDA(launch_attn_general(a, st));
+    QCAU_CHECK_CUDA(run_gather(a, st));
   }
   if (partials) QCAU_CHECK_CUDA(launch_attn_combine(a, st));
   return QCAU_OK;
-}
-
-// Workspace of run_decode_attn for `rows` query tokens, whichever kernel runs.
-size_t decode_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int64_t max_len) {
-  const size_t w1 = attn_ws_bytes(rows, h, d_v, general_splits(rows, h, max_len));
-  const size_t w2 = attn_ws_bytes(rows, h, d_v, sm100_splits(rows, h, max_len));
-  return w1 > w2 ? w1 : w2;
 }
 
 }  // namespace
@@ -343,7 +385,7 @@ int qcau_sparse_attn(const void* q, const void* kv, const float* attn_sink,
   a.inv_rope = inv_rope;
   a.rope_dim = (int)rope_dim;
   a.pos0 = pos0;
-  QCAU_CHECK_CUDA(launch_attn_general(a, to_stream(stream)));
+  QCAU_CHECK_CUDA(run_gather(a, to_stream(stream)));
   return QCAU_OK;
 }
 
@@ -402,7 +444,7 @@ int qcau_forward(const void* c_q, const void* wq_b, const void* wq_b_scale, int3
   a.inv_rope = 1;
   a.rope_dim = (int)rope_dim;
   a.pos0 = pos0;
-  QCAU_CHECK_CUDA(launch_attn_general(a, st));
+  QCAU_CHECK_CUDA(run_gather(a, st));
   return QCAU_OK;
 }
 
@@ -491,7 +533,7 @@ int qcau_decode_attn_paged_blocked(const void* q, int64_t q_hblock, const void* 
 }
 
 size_t qcau_sparse_attn_fp8_workspace_size(int64_t b, int64_t s, int64_t h, int64_t topk) {
-  return attn_ws_bytes(b * s, h, 512, general_splits(b * s, h, topk));
+  return attn_ws_bytes(b * s, h, 512, gather_splits(b * s, h, 576, topk));
 }
 
 int qcau_sparse_attn_fp8(const void* q, const void* kv_latent, const float* kv_scale,
@@ -527,13 +569,13 @@ int qcau_sparse_attn_fp8(const void* q, const void* kv_latent, const float* kv_s
   a.kv_rope = kv_rope;
   a.kv = kv_latent;
   cudaStream_t st = to_stream(stream);
-  a.splits = general_splits(b * s, h, topk);
+  a.splits = gather_splits(b * s, h, 576, topk);
   if (a.splits > 1) {
     a.part_o = reinterpret_cast<float*>(workspace);
     a.part_ml = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
                                          align256((size_t)b * s * a.splits * h * 512 * 4));
   }
-  QCAU_CHECK_CUDA(launch_attn_general(a, st));
+  QCAU_CHECK_CUDA(run_gather(a, st));
   if (a.splits > 1) QCAU_CHECK_CUDA(launch_attn_combine(a, st));
   return QCAU_OK;
 }

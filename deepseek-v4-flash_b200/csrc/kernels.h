@@ -123,6 +123,16 @@ struct AttnArgs {
 // a timeout raises QCAU_DEVERR_TIMEOUT.  One block.
 cudaError_t launch_wait_flags(const uint32_t* flags, int n, uint32_t epoch, cudaStream_t st);
 
+// tcgen05 split-KV attention over gathered rows (attn_gather_sm100.cu): the
+// top-k rows of each query (bf16, or FP8 codes + row scale + bf16 rope), or a
+// paged cache in token order.  One split writes bf16 output (with the sink
+// and the optional inverse RoPE); several write fp32 partials (part_o /
+// part_ml, [rows][splits][h]) for attn_combine.
+cudaError_t launch_attn_gather_sm100(const AttnArgs& args, cudaStream_t st);
+bool attn_gather_sm100_supported(const AttnArgs& args);
+// Heads per CTA of the gather kernel: 16, 32 or 64 (the MMAs' N).
+int gather_heads_per_cta(int64_t h, int64_t d_qk);
+
 // General split-KV kernel, mma.sync 16-head tiles (attn_general.cu).
 cudaError_t launch_attn_general(const AttnArgs& args, cudaStream_t st);
 
