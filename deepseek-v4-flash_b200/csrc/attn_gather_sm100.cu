@@ -15,26 +15,29 @@
 // added once after the loop (kernel.py:331-348), and no output for a row
 // without any valid key (QCAU/QCAU_inference/inference/QCAU.py:201-242).
 //
-// One CTA = one query row x one group of NH heads (16, 32 or 64) x one KV
-// split.  Every gathered row is loaded once per head group, and the heads are
-// the N dimension of both MMAs, so a 16-head shard does not pad the tensor
-// work to 64 or 128 rows:
-//   QK : tcgen05 kind::f16, M = 64 gathered rows, N = NH heads, K = d_qk in
-//        chunks of 64: S^T in TMEM (M = 64 layout: rows 16q..16q+15 in lanes
-//        32q..32q+15), two buffers;
-//   PV : M = 128 latent dims (4 MMAs cover 512), N = NH heads, K = 64 rows:
-//        A = the same staged rows read MN-major (dims contiguous), B = P^T
-//        (K-major [head][row]); O^T in TMEM, lanes = dims, one column a head.
-// Rows are staged in 128-byte-swizzled 64-dim chunks [chunk][64 rows][128 B]
-// (the UMMA K-major layout), two tile slots.  Two groups of four producer
-// warps gather alternate tiles (group g fills slot g), so two tiles are in
-// flight: bf16 rows by 16-byte cp.async, FP8 codes through registers (loaded
-// before the slot is free, converted after).  Softmax: four warps read S^T
-// (a thread per row), stage it in shared memory as [head][row], and then
-// NH heads x (128 / NH) threads each reduce, exponentiate and write P^T; a
-// tile that raises a head's max rescales that head's O^T column in TMEM.
+// One CTA = one query row x one group of NH heads (16 or 32) x one KV split.
+// Every gathered row is loaded once per head group, and the heads are the N
+// dimension of both MMAs, so a 16-head shard does not pad the tensor work.
+// At that N a tcgen05 MMA costs its issue floor (about 52 cycles for N <= 32
+// on B200, whatever M), so the tile is as tall as one MMA allows:
+//   QK : kind::f16, M = 128 gathered rows, N = NH, K = d_qk in 64-value
+//        chunks: S^T in TMEM, lane = row, a column per head, two buffers;
+//   PV : M = 128 latent dims (4 MMAs cover 512), N = NH, K = 128 rows:
+//        A = the staged rows read MN-major (dims contiguous), B = P^T
+//        (K-major [head][row]); O^T in TMEM, lane = dim, a column per head.
+// Staging: 64-value chunks of 128 rows, 128-byte swizzled ([128 rows][128 B],
+// the UMMA K-major layout), in a ring of 10 value chunks (the 8 of a tile
+// plus 2: a PV block frees a chunk pair, which the next tile's chunks 2..7
+// fill in order, so its QK follows PV block by block) and a small ring for
+// the rope chunk (dims 512..575).  Producers: 8 warps, two lanes a row; FP8
+// rows go through registers (codes, rope and scale of the next tile are
+// loaded while the current one computes, converted chunk by chunk as the
+// ring frees), bf16 rows by 16-byte cp.async.  Softmax: a thread per row;
+// per-head maxima by a halving butterfly (lane l ends with head l), then
+// NH threads update the running max; a tile that raises a head's max
+// rescales that head's O^T column.
 // Warps: 0-3 softmax / epilogue, 4 QK issuer + TMEM allocator, 5 PV issuer,
-// 6-9 and 10-13 the two producer groups.
+// 6-13 producers.
 // With one split the epilogue normalises, adds the sink, applies the
 // optional inverse RoPE (V4 mode, QCAU.py:313-319) and writes bf16; with
 // several it writes fp32 partials (O relative to its max, max in log2 units,
@@ -47,49 +50,50 @@
 namespace qcau {
 namespace {
 
-constexpr int kTok = 64;        // gathered rows per tile
-constexpr int kSoft = 128;      // softmax / epilogue threads (warps 0-3)
+constexpr int kTok = 128;       // gathered rows per tile
+constexpr int kVSlots = 10;     // value-chunk ring
+constexpr int kChunkBytes = kTok * 128;
 constexpr int kQkWarp = 4;
 constexpr int kPvWarp = 5;
 constexpr int kProd0 = 6;       // first producer warp
-constexpr int kGroupWarps = 4;  // warps per producer group
-constexpr int kThreads = (kProd0 + 2 * kGroupWarps) * 32;  // 448
+constexpr int kProdWarps = 8;
+constexpr int kThreads = (kProd0 + kProdWarps) * 32;  // 448
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct GatherShared {
-  uint64_t kv_full[2];   // producer group g filled slot g (128 arrivals)
-  uint64_t kv_empty[2];  // PV of the slot's tile done
-  uint64_t q_full;       // Q staged (producer group 0)
-  uint64_t s_full[2];    // QK done into S^T buffer b
-  uint64_t s_free[2];    // the 4 softmax warps read S^T buffer b
-  uint64_t p_full;       // P^T written and O^T rescaled (4 softmax warps)
-  uint64_t p_free;       // PV done with P^T and O^T
-  uint64_t o_full;       // last PV done
-  uint64_t xa, xb, xc;   // softmax warps: S staged / alphas written / denominators written
+  uint64_t vfull[kVSlots];   // value chunk staged (256 producer threads)
+  uint64_t vempty[kVSlots];  // PV done with it
+  uint64_t rfull[2];         // rope chunk staged
+  uint64_t rempty[2];        // QK done with it
+  uint64_t q_full;           // Q staged
+  uint64_t s_full[2];        // QK done into S^T buffer b
+  uint64_t s_free[2];        // the 4 softmax warps read S^T buffer b
+  uint64_t p_full;           // P^T written and O^T rescaled (4 softmax warps)
+  uint64_t p_free;           // PV done with P^T and O^T
+  uint64_t o_full;           // last PV done
+  uint64_t xa, xb, xc, xd;   // softmax warps: maxima / running max / sums / finals
   int valid[2][kTok];
-  int resc[4];
-  float alpha[64];
-  float m_fin[64];
-  float l_fin[64];
+  float xmax[4][32];
+  float xsum[4][32];
+  float m_cur[32];
+  float alpha[32];
+  float fin[32];
+  int resc;
   uint32_t tmem_base;
   int abort;
 };
 
 template <int NH, int DQK>
 struct GCfg {
-  static constexpr int kChunks = DQK / 64;
-  static constexpr int kQBytes = NH * DQK * 2;       // [chunk][NH rows][128 B]
-  static constexpr int kSlotBytes = kChunks * 8192;  // [chunk][64 rows][128 B]
-  static constexpr int kPBytes = NH * 128;           // P^T [NH rows][64 rows of the tile]
-  static constexpr int kSBytes = NH * kTok * 4;      // S^T staged as [head][row] fp32
-  static constexpr uint32_t kColO = 0;               // O^T: 4 blocks of NH columns
-  static constexpr uint32_t kColS = 4 * NH;          // S^T: 2 buffers of NH columns
-  static constexpr uint32_t kCols = 6 * NH <= 128 ? 128 : (6 * NH <= 256 ? 256 : 512);
-  static constexpr int kTph = kSoft / NH;            // softmax threads per head
-  static constexpr int kTpt = kTok / kTph;           // rows per softmax thread
-  static constexpr size_t kSmem = 1024 + (size_t)kQBytes + 2 * (size_t)kSlotBytes + kPBytes +
-                                  kSBytes + sizeof(GatherShared);
-  static_assert(NH == 16 || NH == 32 || NH == 64, "heads per CTA");
+  static constexpr int kRSlots = DQK == 576 ? (NH == 16 ? 2 : 1) : 0;
+  static constexpr int kQBytes = NH * DQK * 2;         // [chunk][NH rows][128 B]
+  static constexpr int kPBytes = 2 * NH * 128;         // P^T [2 row halves][NH rows][128 B]
+  static constexpr uint32_t kColO = 0;                 // O^T: 4 blocks of NH columns
+  static constexpr uint32_t kColS = 4 * NH;            // S^T: 2 buffers of NH columns
+  static constexpr uint32_t kCols = 6 * NH <= 128 ? 128 : 256;
+  static constexpr size_t kSmem = 1024 + (size_t)kQBytes + (size_t)(kVSlots + kRSlots) * kChunkBytes +
+                                  kPBytes + sizeof(GatherShared);
+  static_assert(NH == 16 || NH == 32, "heads per CTA");
   static_assert(DQK == 512 || DQK == 576, "key width");
   static_assert(kSmem <= 232448, "shared memory budget");
 };
@@ -126,8 +130,18 @@ __device__ __forceinline__ void st_shared16(uint32_t dst, uint4 v) {
                "r"(v.w)
                : "memory");
 }
+__device__ __forceinline__ void st_shared_u16(uint32_t dst, uint16_t v) {
+  asm volatile("st.shared.b16 [%0], %1;" ::"r"(dst), "h"(v) : "memory");
+}
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// 32 bytes (32-byte aligned) by one 256-bit load
+__device__ __forceinline__ void ldg_nc32(const void* p, uint4& lo, uint4& hi) {
+  asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w), "=r"(hi.x), "=r"(hi.y), "=r"(hi.z),
+                 "=r"(hi.w)
+               : "l"(p));
 }
 __device__ __forceinline__ uint4 ldg_nc16(const void* p) {
   uint4 v;
@@ -136,10 +150,10 @@ __device__ __forceinline__ uint4 ldg_nc16(const void* p) {
                : "l"(p));
   return v;
 }
-__device__ __forceinline__ int64_t shfl_i64(int64_t v, int src) {
-  const int lo = __shfl_sync(0xffffffffu, (int)(uint32_t)(uint64_t)v, src);
-  const int hi = __shfl_sync(0xffffffffu, (int)(uint32_t)((uint64_t)v >> 32), src);
-  return (int64_t)(((uint64_t)(uint32_t)hi << 32) | (uint32_t)lo);
+
+// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) into L2.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 // Eight e4m3 codes times the row scale as eight bf16: e4m3 -> f16 is exact,
@@ -173,7 +187,8 @@ __device__ __forceinline__ void inv_rope(float& x, float& y, float2 cs) {
   y = im;
 }
 
-// All lanes wait; the warp agrees on the outcome.
+// All lanes wait; the warp agrees on the outcome.  (Lane 0 alone waiting,
+// then __syncwarp, measured slower here and in the decode kernel.)
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   const bool ok = mbar_wait(bar, parity, abort);
   return __all_sync(0xffffffffu, ok);
@@ -186,14 +201,42 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
     tmem_ld16(taddr, *reinterpret_cast<float(*)[16]>(v));
     tmem_ld_wait_regs16(v);
   } else {
-#pragma unroll
-    for (int c = 0; c < NH / 32; c++)
-      tmem_ld32(taddr + c * 32, *reinterpret_cast<float(*)[32]>(v + 32 * c));
-#pragma unroll
-    for (int c = 0; c < NH / 32; c++) tmem_ld_wait_regs(v + 32 * c);
+    tmem_ld32(taddr, *reinterpret_cast<float(*)[32]>(v));
+    tmem_ld_wait_regs(v);
   }
 }
 
+// Per-head reduction of v[NH] over the warp's 32 lanes by halving exchanges:
+// at each step a lane keeps half of its heads and takes the partner's
+// values of them.  Returns the result for head lane (NH = 32) or lane / 2
+// (NH = 16).  kMax: max, else sum.
+template <int NH, bool kMax>
+__device__ __forceinline__ float warp_head_reduce(float* v, int lane) {
+  int n = NH;
+#pragma unroll
+  for (int m = 16; m >= 1 && n > 1; m >>= 1) {
+    const bool up = (lane & m) != 0;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      if (i < n / 2) {
+        const float send = up ? v[i] : v[i + n / 2];
+        const float keep = up ? v[i + n / 2] : v[i];
+        const float got = __shfl_xor_sync(0xffffffffu, send, m);
+        v[i] = kMax ? fmaxf(keep, got) : keep + got;
+      }
+    }
+    n >>= 1;
+  }
+  float r = v[0];
+  if constexpr (NH == 16) {  // lanes l and l ^ 1 hold head l / 2 over other rows
+    const float got = __shfl_xor_sync(0xffffffffu, r, 1);
+    r = kMax ? fmaxf(r, got) : r + got;
+  }
+  return r;
+}
+
+// 14 warps: the sub-partition that runs four of them holds 4 x 32 x 128
+// registers, its whole register file.
 template <int NH, int DQK, bool kFp8>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_gather_sm100_kernel(const __grid_constant__ GatherParams p) {
@@ -201,10 +244,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* sQ = smem_raw + pad;
-  uint8_t* sKV = sQ + C::kQBytes;
-  uint8_t* sP = sKV + 2 * C::kSlotBytes;
-  float* sS = reinterpret_cast<float*>(sP + C::kPBytes);
-  GatherShared* sh = reinterpret_cast<GatherShared*>(sS + NH * kTok);
+  uint8_t* sV = sQ + C::kQBytes;
+  uint8_t* sR = sV + kVSlots * kChunkBytes;
+  uint8_t* sP = sR + C::kRSlots * kChunkBytes;
+  GatherShared* sh = reinterpret_cast<GatherShared*>(sP + C::kPBytes);
   volatile int* abort = &sh->abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -224,19 +267,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int h0 = hg * NH;
 
   if (threadIdx.x == 0) {
+    for (int i = 0; i < kVSlots; i++) {
+      mbar_init(&sh->vfull[i], kProdWarps * 32);
+      mbar_init(&sh->vempty[i], 1);
+    }
     for (int i = 0; i < 2; i++) {
-      mbar_init(&sh->kv_full[i], kGroupWarps * 32);
-      mbar_init(&sh->kv_empty[i], 1);
+      mbar_init(&sh->rfull[i], kProdWarps * 32);
+      mbar_init(&sh->rempty[i], 1);
       mbar_init(&sh->s_full[i], 1);
       mbar_init(&sh->s_free[i], 4);
     }
-    mbar_init(&sh->q_full, kGroupWarps * 32);
+    mbar_init(&sh->q_full, kProdWarps * 32);
     mbar_init(&sh->p_full, 4);
     mbar_init(&sh->p_free, 1);
     mbar_init(&sh->o_full, 1);
     mbar_init(&sh->xa, 4);
     mbar_init(&sh->xb, 4);
     mbar_init(&sh->xc, 4);
+    mbar_init(&sh->xd, 4);
     sh->abort = 0;
     fence_barrier_init();
   }
@@ -248,137 +296,216 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp >= kProd0) {
     // ------------------------------------------------ producers
-    const int grp = (warp - kProd0) / kGroupWarps;
-    const int pw = (warp - kProd0) % kGroupWarps;
-    const int gt = threadIdx.x - (kProd0 + grp * kGroupWarps) * 32;  // 0..127 in the group
-    if (grp == 0) {
-      // Q of the head group: NH rows of d_qk values, K-major chunks [NH][128 B]
-      for (int i = gt; i < NH * (DQK / 8); i += kGroupWarps * 32) {
-        const int r = i / (DQK / 8), u = i % (DQK / 8);
-        const uint32_t dst = smem_u32(sQ + (u >> 3) * (NH * 128) + r * 128 + (((u & 7) ^ (r & 7)) << 4));
-        if (h0 + r < p.h && T > 0)
-          cp_async16(dst, p.q + (row * p.h + h0 + r) * p.q_row_stride + u * 8);
-        else
-          st_shared16(dst, make_uint4(0u, 0u, 0u, 0u));
-      }
-      cp_async_wait_all();
-      fence_proxy_async_smem();
-      mbar_arrive(&sh->q_full);
+    const int pt = threadIdx.x - kProd0 * 32;        // 0..255
+    const int prow = 16 * (warp - kProd0) + (lane >> 1), half = lane & 1;
+    const uint32_t row_sw = (uint32_t)(prow & 7);
+    // Q of the head group: NH rows of d_qk values, K-major chunks [NH][128 B]
+    for (int i = pt; i < NH * (DQK / 8); i += kProdWarps * 32) {
+      const int r = i / (DQK / 8), u = i % (DQK / 8);
+      const uint32_t dst = smem_u32(sQ + (u >> 3) * (NH * 128) + r * 128 + (((u & 7) ^ (r & 7)) << 4));
+      if (h0 + r < p.h && T > 0)
+        cp_async16(dst, p.q + (row * p.h + h0 + r) * p.q_row_stride + u * 8);
+      else
+        st_shared16(dst, make_uint4(0u, 0u, 0u, 0u));
     }
+    cp_async_wait_all();
+    fence_proxy_async_smem();
+    mbar_arrive(&sh->q_full);
+
+    // key of this thread's row in tile n: the top-k index, or the block-table
+    // entry of its page; `has` = the row exists in the key list
+    auto load_key = [&](int n, bool& has) -> int64_t {
+      const int64_t j = (int64_t)(t_begin + n) * kTok + prow;
+      has = j < len;
+      if (!has) return -1;
+      if (paged) {
+        const int64_t col = j / p.page_size;
+        return col < p.max_pages ? (int64_t)p.table[bidx * p.max_pages + col] : -1;
+      }
+      return (int64_t)p.idx[row * p.topk + j];
+    };
+    // latent row of the key, or -1 (a masked key)
+    auto row_of = [&](int n, int64_t key, bool has) -> int64_t {
+      if (!has) return -1;
+      if (paged) {
+        if (key >= 0 && key < p.num_pages) {
+          const int64_t j = (int64_t)(t_begin + n) * kTok + prow;
+          return key * p.page_size + j % p.page_size;
+        }
+        if (half == 0) raise_dev_error(p.err, QCAU_DEVERR_INDEX);
+        return -1;
+      }
+      return (key >= 0 && key < p.n_kv) ? bidx * p.n_kv + key : -1;
+    };
+
+    // bf16 rows: a tile's rows are prefetched into L2 one tile ahead of their
+    // copies (keys two tiles ahead).  FP8 rows: the codes of chunk c of the
+    // next tile are loaded into the registers of chunk c as soon as this
+    // tile's chunk c is stored, a tile ahead of their use, so the loads are
+    // spread over the tile instead of queued together (a burst of them stalls
+    // the softmax warps' shared-memory accesses behind it)
+    auto prefetch_row = [&](int64_t r) {
+      if (r >= 0) prefetch_l2(p.kv + r * p.d_kv + half * (DQK / 2), DQK);  // half a row
+    };
     bool ok = true;
-    for (int n = grp; n < T && ok; n += 2) {
-      const int64_t t0 = (int64_t)(t_begin + n) * kTok;
-      // lane k < 16 resolves row pw + 4k of the tile: its latent row, or -1
-      int64_t my_row = -1;
-      float my_scale = 0.f;
-      if (lane < 16) {
-        const int64_t j = t0 + pw + 4 * lane;
-        if (j < len) {
-          if (paged) {
-            const int64_t col = j / p.page_size;
-            const int64_t pg = col < p.max_pages ? p.table[bidx * p.max_pages + col] : -1;
-            if (pg >= 0 && pg < p.num_pages)
-              my_row = pg * p.page_size + j % p.page_size;
-            else
-              raise_dev_error(p.err, QCAU_DEVERR_INDEX);
-          } else {
-            const int64_t id = p.idx[row * p.topk + j];
-            if (id >= 0 && id < p.n_kv) my_row = bidx * p.n_kv + id;
-          }
-        }
-        if (kFp8 && my_row >= 0) my_scale = __ldg(p.kv_scale + my_row);
-      }
-      // FP8: the codes are loaded before the slot is free (lane l: codes
-      // [16l, 16l+16) of each of the warp's 16 rows)
-      uint4 codes[kFp8 ? 16 : 1];
+    bool has = false, has1 = false;
+    int64_t key = T > 0 ? load_key(0, has) : -1;
+    int64_t key1 = T > 1 ? load_key(1, has1) : -1;
+    // FP8: codes [64c + 32 half, +32) of chunk c of the tile in codes[2c],
+    // codes[2c+1] (one 32-byte load: the row's two lanes read 64 contiguous
+    // bytes), and the row's scale
+    uint4 codes[kFp8 ? 16 : 1];
+    float sc = 0.f;
+    auto load_codes = [&](int64_t r, float& scale_out) {
       if constexpr (kFp8) {
+        if (r >= 0) {
+          const uint8_t* src = p.kv_fp8 + r * 512 + 32 * half;
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
-          const int64_t rr = shfl_i64(my_row, k);
-          codes[k] = rr >= 0 ? ldg_nc16(p.kv_fp8 + rr * 512 + lane * 16) : make_uint4(0u, 0u, 0u, 0u);
+          for (int c = 0; c < 8; c++) ldg_nc32(src + 64 * c, codes[2 * c], codes[2 * c + 1]);
+          scale_out = __ldg(p.kv_scale + r);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; c++) codes[c] = make_uint4(0u, 0u, 0u, 0u);
+          scale_out = 0.f;
         }
       }
-      // slot grp is free once PV of tile n - 2 has completed
-      if (n >= 2 && !(ok = warp_wait(&sh->kv_empty[grp], ((n >> 1) - 1) & 1, abort))) break;
-      uint8_t* slot = sKV + grp * C::kSlotBytes;
-      if (lane < 16) sh->valid[grp][pw + 4 * lane] = my_row >= 0 ? 1 : 0;
+    };
+    if constexpr (kFp8) {
+      load_codes(row_of(0, key, has), sc);
+    } else {
+      prefetch_row(row_of(0, key, has));
+    }
+    for (int n = 0; n < T && ok; n++) {
+      const int64_t rr = row_of(n, key, has);
+      const int64_t rn = n + 1 < T ? row_of(n + 1, key1, has1) : -1;  // next tile's row
+      if constexpr (!kFp8) {
+        if (n + 1 < T) prefetch_row(rn);
+      }
+      float sc_next = 0.f;
       if constexpr (kFp8) {
-        // dims [16l, 16l+16) = chunk l/4, 16-byte units 2(l%4) and 2(l%4)+1;
-        // odd chunks store their second unit first (no bank conflicts)
-        const int c = lane >> 2, u0 = 2 * (lane & 3);
+        if (rn >= 0) sc_next = __ldg(p.kv_scale + rn);
+      }
+      bool has2 = false;
+      const int64_t key2 = n + 2 < T ? load_key(n + 2, has2) : -1;
+      // rope chunk (dims 512..575): bf16 in both formats, copied as soon as
+      // its ring slot is free (QK of the tile before has read it)
+      const int rs = DQK == 576 ? n % C::kRSlots : 0, ru = DQK == 576 ? n / C::kRSlots : 0;
+      if constexpr (DQK == 576) {
+        if (ru >= 1 && !(ok = warp_wait(&sh->rempty[rs], (ru - 1) & 1, abort))) break;
+        const __nv_bfloat16* src = kFp8 ? p.kv_rope + (rr >= 0 ? rr : 0) * 64
+                                        : p.kv + (rr >= 0 ? rr : 0) * p.d_kv + 512;
+        uint8_t* dstrow = sR + rs * kChunkBytes + prow * 128;
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
-          const int r = pw + 4 * k;
-          const float sc = __shfl_sync(0xffffffffu, my_scale, k);
-          const uint4 lo = e4m3x8_to_bf16(codes[k].x, codes[k].y, sc);
-          const uint4 hi = e4m3x8_to_bf16(codes[k].z, codes[k].w, sc);
-          const uint32_t rb = smem_u32(slot + c * 8192 + r * 128);
-          const uint32_t a0 = rb + ((u0 ^ (r & 7)) << 4), a1 = rb + (((u0 + 1) ^ (r & 7)) << 4);
-          if (c & 1) {
-            st_shared16(a1, hi);
-            st_shared16(a0, lo);
-          } else {
-            st_shared16(a0, lo);
-            st_shared16(a1, hi);
-          }
-        }
-        // rope part: chunk 8, 8 units a row; lane l takes unit l%8 of rows
-        // pw + 4(l/8 + 4j)
-#pragma unroll
-        for (int jj = 0; jj < 4; jj++) {
-          const int k = (lane >> 3) + 4 * jj, u = lane & 7, r = pw + 4 * k;
-          const int64_t rr = shfl_i64(my_row, k);
-          const uint32_t dst = smem_u32(slot + 8 * 8192 + r * 128 + ((u ^ (r & 7)) << 4));
+        for (int i = 0; i < 4; i++) {
+          const uint32_t dst = smem_u32(dstrow + (((uint32_t)(4 * half + i) ^ row_sw) << 4));
           if (rr >= 0)
-            cp_async16(dst, p.kv_rope + rr * 64 + u * 8);
+            cp_async16(dst, src + 32 * half + 8 * i);
           else
             st_shared16(dst, make_uint4(0u, 0u, 0u, 0u));
         }
-      } else {
-        // bf16 rows: DQK/8 units a row; lane l takes units l, l + 32 (, l + 64)
-#pragma unroll 4
-        for (int k = 0; k < 16; k++) {
-          const int r = pw + 4 * k;
-          const int64_t rr = shfl_i64(my_row, k);
-          const __nv_bfloat16* src = p.kv + (rr >= 0 ? rr : 0) * p.d_kv;
+      }
+      const __nv_bfloat16* brow = kFp8 ? nullptr : p.kv + (rr >= 0 ? rr : 0) * p.d_kv;
+      // value chunks 0..7, each into the ring slot that PV has freed
 #pragma unroll
-          for (int u = lane; u < DQK / 8; u += 32) {
-            const uint32_t dst =
-                smem_u32(slot + (u >> 3) * 8192 + r * 128 + (((u & 7) ^ (r & 7)) << 4));
+      for (int c = 0; c < 8; c++) {
+        const int q = 8 * n + c, slot = q % kVSlots, u = q / kVSlots;
+        if (u >= 1 && !(ok = warp_wait(&sh->vempty[slot], (u - 1) & 1, abort))) break;
+        if (c == 0 && half == 0) sh->valid[n & 1][prow] = rr >= 0 ? 1 : 0;
+        uint8_t* dstrow = sV + slot * kChunkBytes + prow * 128;
+        if constexpr (kFp8) {
+          if (c == 0 && DQK == 576) {
+            // the rope copies of this tile have landed long since
+            cp_async_wait_all();
+            fence_proxy_async_smem();
+            mbar_arrive(&sh->rfull[rs]);
+          }
+          // dims 64c + 32 half + [0, 32) -> units 4 half .. 4 half + 3
+          const uint4 w0 = e4m3x8_to_bf16(codes[2 * c].x, codes[2 * c].y, sc);
+          const uint4 w1 = e4m3x8_to_bf16(codes[2 * c].z, codes[2 * c].w, sc);
+          const uint4 w2 = e4m3x8_to_bf16(codes[2 * c + 1].x, codes[2 * c + 1].y, sc);
+          const uint4 w3 = e4m3x8_to_bf16(codes[2 * c + 1].z, codes[2 * c + 1].w, sc);
+          const uint32_t u0 = (uint32_t)(4 * half);
+          st_shared16(smem_u32(dstrow + ((u0 ^ row_sw) << 4)), w0);
+          st_shared16(smem_u32(dstrow + (((u0 + 1) ^ row_sw) << 4)), w1);
+          st_shared16(smem_u32(dstrow + (((u0 + 2) ^ row_sw) << 4)), w2);
+          st_shared16(smem_u32(dstrow + (((u0 + 3) ^ row_sw) << 4)), w3);
+          fence_proxy_async_smem();
+          mbar_arrive(&sh->vfull[slot]);
+          // refill: chunk c of the next tile
+          if (rn >= 0) {
+            ldg_nc32(p.kv_fp8 + rn * 512 + 32 * half + 64 * c, codes[2 * c], codes[2 * c + 1]);
+          } else {
+            codes[2 * c] = make_uint4(0u, 0u, 0u, 0u);
+            codes[2 * c + 1] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const uint32_t dst = smem_u32(dstrow + (((uint32_t)(4 * half + i) ^ row_sw) << 4));
             if (rr >= 0)
-              cp_async16(dst, src + u * 8);
+              cp_async16(dst, brow + 64 * c + 32 * half + 8 * i);
             else
               st_shared16(dst, make_uint4(0u, 0u, 0u, 0u));
           }
         }
       }
-      cp_async_wait_all();
-      fence_proxy_async_smem();
-      mbar_arrive(&sh->kv_full[grp]);
+      if (!ok) break;
+      if constexpr (!kFp8) {
+        // bf16 rows: the tile's copies land together
+        cp_async_wait_all();
+        fence_proxy_async_smem();
+        if constexpr (DQK == 576) mbar_arrive(&sh->rfull[n % C::kRSlots]);
+#pragma unroll 1
+        for (int c = 0; c < 8; c++) mbar_arrive(&sh->vfull[(8 * n + c) % kVSlots]);
+      }
+      sc = sc_next;
+      key = key1;
+      has = has1;
+      key1 = key2;
+      has1 = has2;
     }
     cp_async_wait_all();
   } else if (warp == kQkWarp) {
     // ------------------------------------------------ QK issuer
     if (lane == 0) {
-      const uint32_t idesc = make_idesc(64, NH, kFmtBF16, kFmtBF16, false, false);
-      const uint32_t q_addr = smem_u32(sQ), kv_addr = smem_u32(sKV);
+      const uint32_t idesc = make_idesc(128, NH, kFmtBF16, kFmtBF16, false, false);
+      const uint32_t q_addr = smem_u32(sQ), v_addr = smem_u32(sV), r_addr = smem_u32(sR);
       uint64_t* last = nullptr;
       int last_phase = 0;
       bool ok = true;
       for (int n = 0; n < T && ok; n++) {
         const int b = n & 1;
         if (n == 0 && !(ok = mbar_wait(&sh->q_full, 0, abort))) break;
-        if (!(ok = mbar_wait(&sh->kv_full[b], (n >> 1) & 1, abort))) break;
         if (n >= 2 && !(ok = mbar_wait(&sh->s_free[b], ((n >> 1) - 1) & 1, abort))) break;
-        tc_fence_after();
-        const uint32_t slot = kv_addr + b * C::kSlotBytes;
-#pragma unroll
-        for (int c = 0; c < C::kChunks; c++)
+        bool first = true;
+        if constexpr (DQK == 576) {
+          // the rope chunk first: its ring is free ahead of the value chunks
+          const int rs = n % C::kRSlots, ru = n / C::kRSlots;
+          if (!(ok = mbar_wait(&sh->rfull[rs], ru & 1, abort))) break;
+          tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 4; kk++)
-            mma_bf16(tmem + C::kColS + b * NH, make_sdesc(slot + c * 8192 + kk * 32, 16, 1024),
+            mma_bf16(tmem + C::kColS + b * NH,
+                     make_sdesc(r_addr + rs * kChunkBytes + kk * 32, 16, 1024),
+                     make_sdesc(q_addr + 8 * (NH * 128) + kk * 32, 16, 1024), idesc,
+                     kk != 0 ? 1u : 0u);
+          tc_commit(&sh->rempty[rs]);
+          first = false;
+        }
+#pragma unroll 1
+        for (int c = 0; c < 8 && ok; c++) {
+          const int q = 8 * n + c, slot = q % kVSlots, u = q / kVSlots;
+          if (!(ok = mbar_wait(&sh->vfull[slot], u & 1, abort))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++)
+            mma_bf16(tmem + C::kColS + b * NH,
+                     make_sdesc(v_addr + slot * kChunkBytes + kk * 32, 16, 1024),
                      make_sdesc(q_addr + c * (NH * 128) + kk * 32, 16, 1024), idesc,
-                     (c | kk) != 0 ? 1u : 0u);
+                     (first && kk == 0) ? 0u : 1u);
+          first = false;
+        }
+        if (!ok) break;
         tc_commit(&sh->s_full[b]);
         last = &sh->s_full[b];
         last_phase = (n >> 1) & 1;
@@ -393,26 +520,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ PV issuer
     if (lane == 0) {
       const uint32_t idesc = make_idesc(128, NH, kFmtBF16, kFmtBF16, true, false);
-      const uint32_t p_addr = smem_u32(sP), kv_addr = smem_u32(sKV);
+      const uint32_t p_addr = smem_u32(sP), v_addr = smem_u32(sV);
       uint64_t* last = nullptr;
       int last_phase = 0;
       bool ok = true;
       for (int n = 0; n < T && ok; n++) {
         if (!(ok = mbar_wait(&sh->p_full, n & 1, abort))) break;
         tc_fence_after();
-        const uint32_t slot = kv_addr + (n & 1) * C::kSlotBytes;
-        // block j: dims [128j, 128j+128) = chunks 2j, 2j+1 (8192 bytes apart),
-        // 16 rows (2048 bytes) per MMA
+        // block j: dims [128j, +128) = value chunks 2j, 2j+1 of the tile, in
+        // ring slots s0 and s0 + 1 (s0 even: a pair never wraps); 16 rows
+        // (2048 bytes) a MMA
+#pragma unroll 1
+        for (int j = 0; j < 4; j++) {
+          const int s0 = (8 * n + 2 * j) % kVSlots;
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-#pragma unroll
-          for (int kk = 0; kk < 4; kk++)
+          for (int kk = 0; kk < 8; kk++)
             mma_bf16(tmem + C::kColO + j * NH,
-                     make_sdesc(slot + 2 * j * 8192 + kk * 2048, 8192, 1024),
-                     make_sdesc(p_addr + kk * 32, 16, 1024), idesc,
-                     (n > 0 || kk > 0) ? 1u : 0u);
+                     make_sdesc(v_addr + s0 * kChunkBytes + kk * 2048, kChunkBytes, 1024),
+                     make_sdesc(p_addr + (kk >> 2) * (NH * 128) + (kk & 3) * 32, 16, 1024),
+                     idesc, (n > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&sh->vempty[s0]);
+          tc_commit(&sh->vempty[s0 + 1]);
+        }
         tc_commit(&sh->p_free);
-        tc_commit(&sh->kv_empty[n & 1]);
         last = &sh->p_free;
         last_phase = n & 1;
       }
@@ -425,84 +555,71 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------ softmax / epilogue
-    const int tid = threadIdx.x;             // TMEM lane of O^T (a latent dim of each block)
-    const int hh = tid / C::kTph, g = tid % C::kTph;  // softmax stage: head, row group
+    const int t = threadIdx.x;  // TMEM lane: tile row t of S^T, latent dim t of each O^T block
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     const float sl2 = p.scale * kLog2e;
-    float m_run = -INFINITY, l_part = 0.f;
+    float m_run = -INFINITY;    // threads t < NH: running max of head t (log2 units)
+    float l_part[NH];           // this row's share of each head's denominator
+#pragma unroll
+    for (int h = 0; h < NH; h++) l_part[h] = 0.f;
     bool ok = true;
     for (int n = 0; n < T && ok; n++) {
       const int b = n & 1;
       if (!(ok = warp_wait(&sh->s_full[b], (n >> 1) & 1, abort))) break;
-      if (!(ok = warp_wait(&sh->kv_full[b], (n >> 1) & 1, abort))) break;  // valid flags
+      {  // the valid flags of the tile arrived with its first value chunk
+        const int q0 = 8 * n;
+        if (!(ok = warp_wait(&sh->vfull[q0 % kVSlots], (q0 / kVSlots) & 1, abort))) break;
+      }
       tc_fence_after();
+      float s[NH];
+      tmem_ld_cols<NH>(tmem + lane_base + C::kColS + b * NH, s);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->s_free[b]);
+      const bool vld = sh->valid[b][t] != 0;
       {
         float v[NH];
-        tmem_ld_cols<NH>(tmem + lane_base + C::kColS + b * NH, v);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sh->s_free[b]);
-        if (lane < 16) {
-          const int m = 16 * warp + lane;  // the tile row in this TMEM lane (M = 64 layout)
 #pragma unroll
-          for (int h = 0; h < NH; h++) sS[h * kTok + m] = v[h];
-        }
+        for (int h = 0; h < NH; h++) v[h] = vld ? s[h] : -INFINITY;
+        const float wm = warp_head_reduce<NH, true>(v, lane);
+        if (NH == 32 || (lane & 1) == 0) sh->xmax[warp][NH == 32 ? lane : lane >> 1] = wm;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh->xa);
       if (!(ok = warp_wait(&sh->xa, n & 1, abort))) break;
-      // head hh, rows [g * kTpt, +kTpt)
-      float s[C::kTpt];
-#pragma unroll
-      for (int i = 0; i < C::kTpt; i += 4) {
-        const float4 f = *reinterpret_cast<const float4*>(sS + hh * kTok + g * C::kTpt + i);
-        s[i] = f.x;
-        s[i + 1] = f.y;
-        s[i + 2] = f.z;
-        s[i + 3] = f.w;
-      }
-      const int* vld = sh->valid[b] + g * C::kTpt;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < C::kTpt; i++)
-        if (vld[i]) mx = fmaxf(mx, s[i]);
-#pragma unroll
-      for (int o = 1; o < C::kTph; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      mx = mx == -INFINITY ? -INFINITY : mx * sl2;
-      const float m_new = fmaxf(m_run, mx);
-      float alpha = 1.f;
-      if (m_new != m_run) alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
-      m_run = m_new;
-      uint32_t pk[C::kTpt / 2];
-      float psum = 0.f;
-#pragma unroll
-      for (int i = 0; i < C::kTpt; i += 2) {
-        float p0 = 0.f, p1 = 0.f;
-        if (m_new != -INFINITY) {
-          if (vld[i]) p0 = ex2_approx(fmaf(s[i], sl2, -m_new));
-          if (vld[i + 1]) p1 = ex2_approx(fmaf(s[i + 1], sl2, -m_new));
+      if (warp == 0) {
+        float alpha = 1.f;
+        if (t < NH) {
+          float tm = fmaxf(fmaxf(sh->xmax[0][t], sh->xmax[1][t]), fmaxf(sh->xmax[2][t], sh->xmax[3][t]));
+          tm = tm == -INFINITY ? -INFINITY : tm * sl2;
+          const float m_new = fmaxf(m_run, tm);
+          if (m_new != m_run) alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
+          m_run = m_new;
+          sh->m_cur[t] = m_new;
+          sh->alpha[t] = alpha;
         }
-        psum += p0 + p1;
-        __nv_bfloat162 t2 = __floats2bfloat162_rn(p0, p1);
-        pk[i / 2] = *reinterpret_cast<uint32_t*>(&t2);
+        const bool any = __any_sync(0xffffffffu, alpha != 1.f);
+        if (lane == 0) sh->resc = any ? 1 : 0;
       }
-      l_part = l_part * alpha + psum;
-      if (g == 0) sh->alpha[hh] = alpha;
-      const bool any = __any_sync(0xffffffffu, alpha != 1.f);
-      if (lane == 0) {
-        sh->resc[warp] = any ? 1 : 0;
-        mbar_arrive(&sh->xb);
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->xb);
       if (!(ok = warp_wait(&sh->xb, n & 1, abort))) break;
-      const bool resc = (sh->resc[0] | sh->resc[1] | sh->resc[2] | sh->resc[3]) != 0;
+      const bool resc = sh->resc != 0;
       // P^T of tile n reuses the buffer of tile n-1, and O^T holds tiles < n,
       // once PV(n-1) is done
       if (n >= 1 && !(ok = warp_wait(&sh->p_free, (n - 1) & 1, abort))) break;
+      {
+        // P of this row for every head, stored as column t of P^T
+        const uint32_t pbase = smem_u32(sP + (t >> 6) * (NH * 128)) + (t & 7) * 2;
+        const uint32_t unit = (uint32_t)((t & 63) >> 3);
 #pragma unroll
-      for (int u = 0; u < C::kTpt / 8; u++) {
-        const int unit = g * (C::kTpt / 8) + u;
-        st_shared16(smem_u32(sP + hh * 128 + ((unit ^ (hh & 7)) << 4)),
-                    make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]));
+        for (int h = 0; h < NH; h++) {
+          const float m = sh->m_cur[h];
+          const float pv = (vld && m != -INFINITY) ? ex2_approx(fmaf(s[h], sl2, -m)) : 0.f;
+          l_part[h] = l_part[h] * sh->alpha[h] + pv;
+          st_shared_u16(pbase + h * 128 + ((unit ^ (uint32_t)(h & 7)) << 4),
+                        __bfloat16_as_ushort(__float2bfloat16_rn(pv)));
+        }
       }
       if (resc && n >= 1) {
         // O^T column c (block c / NH, head c % NH) of this lane times alpha
@@ -524,16 +641,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&sh->p_full);
     }
     if (ok && T > 0) ok = warp_wait(&sh->o_full, 0, abort);
-    // per head: running max and denominator (the kTph threads' partial sums)
-    float l_tot = l_part;
-#pragma unroll
-    for (int o = 1; o < C::kTph; o <<= 1) l_tot += __shfl_xor_sync(0xffffffffu, l_tot, o);
+    // per head: the denominator over the 128 rows
+    {
+      const float ws = warp_head_reduce<NH, false>(l_part, lane);
+      if (NH == 32 || (lane & 1) == 0) sh->xsum[warp][NH == 32 ? lane : lane >> 1] = ws;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sh->xc);
+    if (ok) ok = warp_wait(&sh->xc, 0, abort);
     const bool direct = p.splits == 1;
-    if (g == 0) {
-      sh->m_fin[hh] = m_run;
+    if (ok && t < NH) {
+      const float l_tot = sh->xsum[0][t] + sh->xsum[1][t] + sh->xsum[2][t] + sh->xsum[3][t];
       if (direct) {
         // O / (l + 2^(sink log2e - m)), as attn_combine does for one part
-        const int head = h0 + hh;
+        const int head = h0 + t;
         const bool has_sink = p.sink != nullptr && head < p.h;
         const float sk = has_sink ? p.sink[head] * kLog2e : -INFINITY;
         float den;
@@ -541,14 +662,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           den = l_tot + exp2f(sk - m_run);
         else
           den = l_tot + ((has_sink && isfinite(p.sink[head])) ? 1.f : 0.f);
-        sh->l_fin[hh] = 1.f / fmaxf(den, 1.17549435e-38f);
-      } else {
-        sh->l_fin[hh] = l_tot;
+        sh->fin[t] = 1.f / fmaxf(den, 1.17549435e-38f);
+      } else if (h0 + t < p.h) {
+        const int64_t prow = (row * p.splits + split) * p.h + h0 + t;
+        p.part_ml[prow * 2] = m_run;
+        p.part_ml[prow * 2 + 1] = l_tot;
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sh->xc);
-    if (ok) ok = warp_wait(&sh->xc, 0, abort);
+    if (lane == 0) mbar_arrive(&sh->xd);
+    if (ok) ok = warp_wait(&sh->xd, 0, abort);
     if (ok) {
       tc_fence_after();
 #pragma unroll 1
@@ -561,9 +684,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; i++) o[i] = 0.f;
         }
-        // 16 columns of one block (NH is a multiple of 16): dim 128 j + tid
+        // 16 columns of one block (NH is a multiple of 16): dim 128 j + t
         const int j = c0 / NH;
-        const int dim = 128 * j + tid;
+        const int dim = 128 * j + t;
         if (direct) {
           const bool rope = p.inv_rope && dim >= 512 - p.rope_dim;
           float2 cs = make_float2(1.f, 0.f);
@@ -573,7 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; i++) {
             const int h = (c0 + i) % NH;
-            float x = o[i] * sh->l_fin[h];
+            float x = o[i] * sh->fin[h];
             const float other = __shfl_xor_sync(0xffffffffu, x, 1);  // the pair's other dim
             if (rope) {
               float re = (lane & 1) ? other : x, im = (lane & 1) ? x : other;
@@ -590,11 +713,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               p.part_o[((row * p.splits + split) * p.h + h0 + h) * 512 + dim] = o[i];
           }
         }
-      }
-      if (!direct && g == 0 && h0 + hh < p.h) {
-        const int64_t prow = (row * p.splits + split) * p.h + h0 + hh;
-        p.part_ml[prow * 2] = m_run;
-        p.part_ml[prow * 2 + 1] = sh->l_fin[hh];
       }
     }
   }
@@ -629,11 +747,7 @@ cudaError_t launch_t(const GatherParams& p, int64_t units, cudaStream_t st) {
 
 }  // namespace
 
-int gather_heads_per_cta(int64_t h, int64_t d_qk) {
-  if (h <= 16) return 16;
-  if (h <= 32 || d_qk == 576) return 32;
-  return 64;
-}
+int gather_heads_per_cta(int64_t h, int64_t /*d_qk*/) { return h <= 16 ? 16 : 32; }
 
 bool attn_gather_sm100_supported(const AttnArgs& a) {
   const bool fp8 = a.kv_fp8 != nullptr;
@@ -647,8 +761,8 @@ bool attn_gather_sm100_supported(const AttnArgs& a) {
   const bool rope = !a.inv_rope || (a.freqs != nullptr && a.rope_dim > 0 && a.rope_dim <= 512 &&
                                     a.rope_dim % 2 == 0);
   const bool aligned = (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 && a.q_row_stride % 8 == 0 &&
-                       (fp8 ? ((reinterpret_cast<uintptr_t>(a.kv_fp8) |
-                                reinterpret_cast<uintptr_t>(a.kv_rope)) & 15) == 0
+                       (fp8 ? (reinterpret_cast<uintptr_t>(a.kv_fp8) & 31) == 0 &&
+                                  (reinterpret_cast<uintptr_t>(a.kv_rope) & 15) == 0
                             : (reinterpret_cast<uintptr_t>(a.kv) & 15) == 0);
   return widths && mode && plain && rope && aligned && a.h > 0 && a.splits >= 1 &&
          (a.splits == 1 || (a.part_o != nullptr && a.part_ml != nullptr)) && sm100_device();
@@ -701,8 +815,7 @@ cudaError_t launch_attn_gather_sm100(const AttnArgs& a, cudaStream_t st) {
     return launch_t<32, 576, false>(p, units, st);
   }
   if (nh == 16) return launch_t<16, 512, false>(p, units, st);
-  if (nh == 32) return launch_t<32, 512, false>(p, units, st);
-  return launch_t<64, 512, false>(p, units, st);
+  return launch_t<32, 512, false>(p, units, st);
 }
 
 }  // namespace qcau

@@ -176,19 +176,19 @@ int sm100_splits(int64_t b, int64_t h, int64_t max_len) {
 }
 
 // Splits of the tcgen05 gather kernel: one CTA (one per SM) per (query row,
-// head group, split); the count minimises waves x (set-up + tiles of 64 rows
+// head group, split); the count minimises waves x (set-up + tiles of 128 rows
 // per split), the set-up (TMEM, barriers, Q, the first gathers) worth about
-// three tiles, plus one tile's worth for the merge of several splits.
+// one and a half tiles, plus half a tile for the merge of several splits.
 int gather_splits(int64_t rows, int64_t h, int64_t d_qk, int64_t max_len) {
   const int nh = gather_heads_per_cta(h, d_qk);
   const int64_t ctas = rows * ((h + nh - 1) / nh);
-  const int64_t tiles = max_len > 0 ? (max_len + 63) / 64 : 1;
+  const int64_t tiles = max_len > 0 ? (max_len + 127) / 128 : 1;
   int best = 1;
   double best_cost = 1e300;
   for (int s = 1; s <= 64 && s <= tiles; s++) {
     const int64_t units = ctas * s;
     const double waves = (double)((units + kNumSms - 1) / kNumSms);
-    const double cost = waves * (3.0 + (double)((tiles + s - 1) / s)) + (s > 1 ? 1.0 : 0.0);
+    const double cost = waves * (1.5 + (double)((tiles + s - 1) / s)) + (s > 1 ? 0.5 : 0.0);
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
       best = s;
