@@ -118,18 +118,6 @@ namespace {
 
 constexpr int kNumSms = 148;
 
-// Number of KV splits of the general split-KV kernel: enough CTAs for two
-// waves over the SMs, at least 4 tiles of 64 keys per split, at most 64.
-int general_splits(int64_t b, int64_t h, int64_t max_len) {
-  const int64_t ctas = b * ((h + 15) / 16);
-  int64_t want = (2 * kNumSms + ctas - 1) / (ctas > 0 ? ctas : 1);
-  const int64_t cap = (max_len + 255) / 256;
-  if (want > cap) want = cap;
-  if (want < 1) want = 1;
-  if (want > 64) want = 64;
-  return (int)want;
-}
-
 // Splits of the tcgen05 two-CTA decode kernel: one CTA pair per (sequence,
 // 128-head group, split), one pair per two SMs, at least 4 tiles of 128
 // tokens per split.  The count minimises an estimate of the launch time
@@ -197,11 +185,10 @@ int gather_splits(int64_t rows, int64_t h, int64_t d_qk, int64_t max_len) {
   return best;
 }
 
-// Gathered-row attention: the tcgen05 gather kernel where it takes the shape,
-// else the general split-KV kernel.
+// Gathered-row attention on the tcgen05 gather kernel; a shape or device it
+// does not take is an error (there is no other path).
 cudaError_t run_gather(const AttnArgs& a, cudaStream_t st) {
-  if (attn_gather_sm100_supported(a)) return launch_attn_gather_sm100(a, st);
-  return launch_attn_general(a, st);
+  return launch_attn_gather_sm100(a, st);
 }
 
 size_t attn_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int splits) {
@@ -545,9 +532,9 @@ int qcau_sparse_attn_fp8(const void* q, const void* kv_latent, const float* kv_s
                  "sparse_attn_fp8: NULL pointer");
   QCAU_CHECK_ARG(b >= 0 && s >= 0 && h > 0 && topk > 0, "sparse_attn_fp8: bad shape");
   QCAU_CHECK_ARG(n_kv > 0, "sparse_attn_fp8: kv must contain at least one latent row");
-  QCAU_CHECK_ARG((reinterpret_cast<uintptr_t>(kv_latent) & 15) == 0 &&
+  QCAU_CHECK_ARG((reinterpret_cast<uintptr_t>(kv_latent) & 31) == 0 &&
                      (reinterpret_cast<uintptr_t>(kv_rope) & 15) == 0,
-                 "sparse_attn_fp8: kv_latent and kv_rope must be 16-byte aligned");
+                 "sparse_attn_fp8: kv_latent must be 32-byte and kv_rope 16-byte aligned");
   const size_t need = qcau_sparse_attn_fp8_workspace_size(b, s, h, topk);
   if (workspace_bytes < need || (need && !workspace))
     return fail(QCAU_ERR_WORKSPACE, "sparse_attn_fp8: workspace too small (need " +

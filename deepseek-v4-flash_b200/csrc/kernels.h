@@ -133,10 +133,8 @@ bool attn_gather_sm100_supported(const AttnArgs& args);
 // Heads per CTA of the gather kernel: 16, 32 or 64 (the MMAs' N).
 int gather_heads_per_cta(int64_t h, int64_t d_qk);
 
-// General split-KV kernel, mma.sync 16-head tiles (attn_general.cu).
-cudaError_t launch_attn_general(const AttnArgs& args, cudaStream_t st);
-
-// Merge split-KV partials into bf16 outputs (+ optional inverse RoPE).
+// Merge split-KV partials into bf16 outputs (+ optional inverse RoPE)
+// (attn_combine.cu).
 cudaError_t launch_attn_combine(const AttnArgs& args, cudaStream_t st);
 
 // tcgen05 two-CTA paged decode attention (h % 64 == 0, d_qk 576, d_v 512,

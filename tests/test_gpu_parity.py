@@ -324,7 +324,7 @@ def _decode_abi(q, cache, table, seqlens, sink, scale, d_v, max_seqlen):
     return o
 
 
-# 8 and 48 heads run the general split-KV kernel, 128 the tcgen05 pair kernel
+# 8 and 48 heads run the tcgen05 gather kernel (paged mode), 128 the tcgen05 pair kernel
 @pytest.mark.parametrize("h,seqlens", [(8, [1, 100, 1000]), (128, [4096, 64, 777]),
                                        (48, [0, 2000, 513])])
 def test_decode_paged_vs_oracle(h, seqlens):
@@ -515,7 +515,7 @@ def _prefill_oracle(q, cache, table, seqlens, sink, scale, rows):
                                None if sink is None else sink.cpu().numpy(), scale, 512)
 
 
-# 128 heads run the tcgen05 pair kernel, 48 the general kernel
+# 128 heads run the tcgen05 pair kernel, 48 the tcgen05 gather kernel (paged mode)
 @pytest.mark.parametrize("h", [128, 48])
 def test_prefill_paged_vs_oracle(h):
     """Causal prefill of 200 new tokens: sequence 0 holds only them, sequence

@@ -60,7 +60,8 @@ def _noalloc(c):
                "decode_attn_paged_noalloc")
 
 
-# (128 heads: the tcgen05 two-CTA kernel; 16 heads: the general split-KV kernel)
+# (128 heads: the tcgen05 two-CTA kernel over one 128-head group; 16 heads: the
+# same kernel as a 16-head shard)
 @pytest.mark.gpu
 @pytest.mark.parametrize("h,first,second", [
     (128, [4096, 64, 777, 1], [0, 130, 2000]),
