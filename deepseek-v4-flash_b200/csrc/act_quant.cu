@@ -17,15 +17,6 @@
 
 namespace qcau {
 
-__device__ __forceinline__ float act_scale(float amax, int round_scale) {
-  amax = fmaxf(amax, 1e-4f);
-  float t = __fdiv_rn(amax, 448.0f);
-  if (!round_scale) return t;
-  uint32_t bits = __float_as_uint(t);
-  int e = (int)((bits >> 23) & 0xff) - 127 + ((bits & 0x7fffffu) != 0 ? 1 : 0);
-  return __uint_as_float((uint32_t)(e + 127) << 23);
-}
-
 template <int kPer>  // values per lane = block / 32
 __global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, uint8_t* __restrict__ y,
                                  void* __restrict__ s, __nv_bfloat16* __restrict__ x_inplace,

@@ -690,6 +690,106 @@ int qcau_dequant_fp8_weight(const void* w, const void* w_scale, int32_t scale_dt
   return QCAU_OK;
 }
 
+size_t qcau_gopu_workspace_size(int64_t rows, int64_t groups, int64_t rank_dim) {
+  const int64_t k2 = groups * rank_dim;
+  return align256((size_t)(rows * k2 * 2)) + align256((size_t)(rows * k2)) +
+         align256((size_t)(rows * (k2 / 128) * 4));
+}
+
+int qcau_gopu(const void* o, const void* wo_a, const void* wo_b, const void* wo_b_scale,
+              int32_t scale_dtype, int32_t act_round_scale, void* y, int32_t out_dtype,
+              int64_t rows, int64_t groups, int64_t group_dim, int64_t rank_dim, int64_t dim,
+              void* workspace, size_t workspace_bytes, void* stream) {
+  QCAU_CHECK_ARG(o && wo_a && wo_b && wo_b_scale && y, "gopu: NULL pointer");
+  QCAU_CHECK_ARG(rows >= 0 && groups > 0 && group_dim > 0 && rank_dim > 0 && dim > 0,
+                 "gopu: bad shape");
+  QCAU_CHECK_ARG(group_dim % 64 == 0, "gopu: the group width must be a multiple of 64");
+  QCAU_CHECK_ARG(rank_dim % 128 == 0, "gopu: o_lora_rank must be a multiple of 128");
+  QCAU_CHECK_ARG(dim % 128 == 0, "gopu: the output width must be a multiple of 128");
+  QCAU_CHECK_ARG(scale_dtype == QCAU_SCALE_F32 || scale_dtype == QCAU_SCALE_E8M0,
+                 "gopu: bad scale dtype");
+  QCAU_CHECK_ARG(out_dtype == QCAU_OUT_BF16 || out_dtype == QCAU_OUT_F32, "gopu: bad out dtype");
+  QCAU_CHECK_ARG(((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(wo_a) |
+                   reinterpret_cast<uintptr_t>(wo_b) | reinterpret_cast<uintptr_t>(y)) & 15) == 0,
+                 "gopu: operands must be 16-byte aligned");
+  const size_t need = qcau_gopu_workspace_size(rows, groups, rank_dim);
+  if (workspace_bytes < need || (need && !workspace))
+    return fail(QCAU_ERR_WORKSPACE,
+                "gopu: workspace too small (need " + std::to_string(need) + " bytes)");
+  if (rows == 0) return QCAU_OK;
+  cudaStream_t st = to_stream(stream);
+  const int64_t k2 = groups * rank_dim;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  void* h = ws;                                        // [rows, groups, rank_dim] bf16
+  void* xq = ws + align256((size_t)(rows * k2 * 2));  // its FP8 codes
+  void* sq = reinterpret_cast<uint8_t*>(xq) + align256((size_t)(rows * k2));
+  // wo_a: h[r, g, :] = o[r, g, :] . wo_a[g]^T  (model.py:537-541, bf16 einsum)
+  BmmArgs b{};
+  b.a = o;
+  b.a_bstride = group_dim;
+  b.a_rstride = groups * group_dim;
+  b.b = wo_a;
+  b.b_bstride = rank_dim * group_dim;
+  b.b_rstride = group_dim;
+  b.b_kmajor = 1;
+  b.c = h;
+  b.c_bstride = rank_dim;
+  b.c_rstride = k2;
+  b.batch = groups;
+  b.m = rows;
+  b.n = rank_dim;
+  b.k = group_dim;
+  QCAU_CHECK_CUDA(launch_bf16_bmm(b, st));
+  // wo_b: linear() -> act_quant + fp8_gemm (model.py:108-120, 166-180)
+  const int a_e8 = act_round_scale ? 1 : 0;
+  QCAU_CHECK_CUDA(launch_act_quant(h, xq, sq, rows, k2, 128, act_round_scale, a_e8, 0, st));
+  QCAU_CHECK_CUDA(launch_fp8_gemm(xq, sq, wo_b, wo_b_scale, y, rows, dim, k2, a_e8,
+                                  scale_dtype == QCAU_SCALE_E8M0, out_dtype == QCAU_OUT_F32, st));
+  return QCAU_OK;
+}
+
+int qcau_kv_build(const void* kv_in, void* kv_out, int64_t rows, int64_t d,
+                  const float* norm_weight, int64_t norm_dim, float eps, const float* freqs,
+                  const int32_t* positions, int64_t npos, int64_t rope_dim, int64_t quant_dims,
+                  int32_t round_scale, void* cache, const int32_t* cache_slots,
+                  int64_t cache_rows, void* stream) {
+  QCAU_CHECK_ARG(kv_in != nullptr, "kv_build: kv_in is NULL");
+  QCAU_CHECK_ARG(rows >= 0 && d > 0 && d % 64 == 0 && d <= 1024,
+                 "kv_build: d must be a multiple of 64 up to 1024");
+  QCAU_CHECK_ARG(norm_dim >= 0 && norm_dim % 64 == 0 && norm_dim <= d,
+                 "kv_build: norm_dim must be a multiple of 64 up to d");
+  QCAU_CHECK_ARG(rope_dim >= 0 && rope_dim % 2 == 0 && rope_dim <= d, "kv_build: bad rope_dim");
+  QCAU_CHECK_ARG(rope_dim == 0 || (freqs != nullptr && positions != nullptr && npos > 0),
+                 "kv_build: RoPE needs freqs_cis and positions");
+  QCAU_CHECK_ARG(quant_dims >= 0 && quant_dims % 64 == 0 && quant_dims <= d - rope_dim,
+                 "kv_build: quant_dims must be a multiple of 64 below the rope values");
+  QCAU_CHECK_ARG(cache == nullptr || (cache_slots != nullptr && cache_rows >= 0),
+                 "kv_build: a cache needs cache_slots");
+  QCAU_CHECK_ARG(kv_out != nullptr || cache != nullptr, "kv_build: no destination");
+  QCAU_CHECK_ARG(((reinterpret_cast<uintptr_t>(kv_in) | reinterpret_cast<uintptr_t>(kv_out) |
+                   reinterpret_cast<uintptr_t>(cache)) & 3) == 0,
+                 "kv_build: rows must be 4-byte aligned");
+  KvBuildArgs a{};
+  a.in = kv_in;
+  a.out = kv_out;
+  a.rows = rows;
+  a.d = d;
+  a.norm_weight = norm_weight;
+  a.norm_dim = (int)norm_dim;
+  a.eps = eps;
+  a.freqs = freqs;
+  a.positions = positions;
+  a.npos = npos;
+  a.rope_dim = (int)rope_dim;
+  a.quant_dims = (int)quant_dims;
+  a.round_scale = round_scale ? 1 : 0;
+  a.cache = cache;
+  a.slots = cache ? cache_slots : nullptr;
+  a.cache_rows = cache_rows;
+  QCAU_CHECK_CUDA(launch_kv_build(a, to_stream(stream)));
+  return QCAU_OK;
+}
+
 // Workspace layout of the absorbed decode layer.
 struct MlaWs {
   size_t xq, sq, q, qabs, olat, ov, xo, so, attn, total;

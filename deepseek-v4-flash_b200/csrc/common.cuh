@@ -471,6 +471,18 @@ __device__ __forceinline__ float bf16_round(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+// Scale of one FP8 activation block: amax floored at 1e-4, amax / 448
+// correctly rounded (kernel_fallback.py:27-28), or with round_scale the power
+// of two 2^(exponent + (mantissa != 0)) of it (kernel.py:22-37, UE8M0).
+__device__ __forceinline__ float act_scale(float amax, int round_scale) {
+  amax = fmaxf(amax, 1e-4f);
+  float t = __fdiv_rn(amax, 448.0f);
+  if (!round_scale) return t;
+  uint32_t bits = __float_as_uint(t);
+  int e = (int)((bits >> 23) & 0xff) - 127 + ((bits & 0x7fffffu) != 0 ? 1 : 0);
+  return __uint_as_float((uint32_t)(e + 127) << 23);
+}
+
 __device__ __forceinline__ uint8_t f32_to_e4m3(float x) {
   return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
 }

@@ -41,6 +41,28 @@ cudaError_t launch_fp8_gemm(const void* a, const void* a_s, const void* b, const
                             void* c, int64_t m, int64_t n, int64_t k, int a_e8m0, int b_e8m0,
                             int out_f32, cudaStream_t st);
 
+// The latent KV row of new tokens: RMSNorm (fp32, weight), RoPE of the last
+// rope_dim values, FP8 block-64 round trip of the first quant_dims values,
+// then the bf16 row to out[r] and to cache row slots[r] (kv_build.cu).
+struct KvBuildArgs {
+  const void* in;      // [rows, d] bf16 (the wkv projection)
+  void* out;           // [rows, d] bf16 or nullptr (may equal in)
+  int64_t rows, d;     // d a multiple of 64, <= 1024
+  const float* norm_weight;  // [norm_dim] fp32 or nullptr (ones)
+  int norm_dim;        // 0: no norm
+  float eps;
+  const float* freqs;  // [npos, rope_dim/2, 2] fp32
+  const int32_t* positions;  // [rows]
+  int64_t npos;
+  int rope_dim;        // 0: no RoPE
+  int quant_dims;      // a multiple of 64; 0: no FP8 round trip
+  int round_scale;     // UE8M0 (power-of-two) scales
+  void* cache;         // [cache_rows, d] bf16 or nullptr
+  const int32_t* slots;  // [rows]: destination cache row, -1 to skip
+  int64_t cache_rows;
+};
+cudaError_t launch_kv_build(const KvBuildArgs& args, cudaStream_t st);
+
 // Batched bf16 GEMM on tcgen05 for the absorbed-MLA projections:
 //   for each batch g:  C_g[m, n] = A_g[m, k] . B_g^T  with
 //   A_g row r at a + g*a_bstride + r*a_rstride (K contiguous),

@@ -99,6 +99,11 @@ SIGNATURES = {
                                        _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                                        _I64, _F, _I32, _P], ctypes.c_int),
     "qcau_wait_flags": ([_P, _I64, ctypes.c_uint32, _P], ctypes.c_int),
+    "qcau_gopu_workspace_size": ([_I64, _I64, _I64], _SZ),
+    "qcau_gopu": ([_P, _P, _P, _P, _I32, _I32, _P, _I32, _I64, _I64, _I64, _I64, _I64, _P, _SZ,
+                   _P], ctypes.c_int),
+    "qcau_kv_build": ([_P, _P, _I64, _I64, _P, _I64, _F, _P, _P, _I64, _I64, _I64, _I32, _P, _P,
+                       _I64, _P], ctypes.c_int),
 }
 
 _lib = None

@@ -281,6 +281,56 @@ int qcau_decode_attn_paged_noalloc(const void* q, const void* cache,
                                    int64_t max_seqlen, float softmax_scale, void* stream);
 
 /* ------------------------------------------------------------------------
+ * gopu -- the V4 output side of the attention block after the QCAU output
+ * o (Deepseek_origin/inference/model.py:536-542): the grouped low-rank
+ * projection wo_a (einsum "bsgd,grd->bsgr", a bf16 weight) and the
+ * row-parallel wo_b (RowParallelLinear :166-180 -> linear() :108-120:
+ * act_quant of the activation, FP8 GEMM with 128x128 block scales).
+ *   o [rows, groups, group_dim] bf16 (the heads of a group side by side:
+ *   group_dim = heads / groups * head_dim); wo_a [groups, rank_dim,
+ *   group_dim] bf16; wo_b [dim, groups*rank_dim] e4m3 + wo_b_scale
+ *   [dim/128, groups*rank_dim/128] (scale_dtype); y [rows, dim] bf16 or
+ *   fp32 (out_dtype).  act_round_scale selects UE8M0 activation scales (the
+ *   model's scale_fmt).  A head shard passes its own groups and wo_b
+ *   columns; the partial y of the ranks is summed by the caller (the
+ *   reference all-reduces in fp32, model.py:174-177).
+ *   Workspace: qcau_gopu_workspace_size(rows, groups, rank_dim).
+ * ---------------------------------------------------------------------- */
+size_t qcau_gopu_workspace_size(int64_t rows, int64_t groups, int64_t rank_dim);
+int qcau_gopu(const void* o, const void* wo_a, const void* wo_b, const void* wo_b_scale,
+              int32_t scale_dtype, int32_t act_round_scale, void* y, int32_t out_dtype,
+              int64_t rows, int64_t groups, int64_t group_dim, int64_t rank_dim,
+              int64_t dim, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * kv_build -- the latent KV row of new tokens, from the wkv projection to the
+ * cache: Deepseek_origin/inference/model.py:502-506 (kv_norm, RoPE of the
+ * last rope_dim values, act_quant(kv[..., :-rd], 64, scale_fmt, inplace))
+ * and the cache writes :517-533 (window ring kv_cache[b, pos % win]), also
+ * the Compressor's tail :362-376 on its pooled rows.
+ *   kv_in [rows, d] bf16 (d a multiple of 64, <= 1024); kv_out [rows, d]
+ *   bf16 or NULL, may equal kv_in;
+ *   norm_weight [norm_dim] fp32 or NULL (ones); norm_dim 0 (no norm), or a
+ *   multiple of 64 <= d: RMSNorm of values [0, norm_dim) in fp32
+ *   (model.py:182-195);
+ *   freqs [npos, rope_dim/2, 2] fp32, positions [rows] int32: RoPE of the
+ *   last rope_dim values (rope_dim 0: none);
+ *   quant_dims: a multiple of 64 <= d - rope_dim: FP8 e4m3 round trip of
+ *   values [0, quant_dims) in 1x64 blocks, UE8M0 scales with round_scale
+ *   (scale_fmt "ue8m0") else fp32 amax/448;
+ *   cache [cache_rows, d] bf16 or NULL; cache_slots [rows] int32: the cache
+ *   row of each input row, -1 to skip (a window ring: b * ring + pos % win;
+ *   a paged cache: page * page_size + pos % page_size).
+ * A position or slot out of range is skipped and raises QCAU_DEVERR_INDEX.
+ * ---------------------------------------------------------------------- */
+int qcau_kv_build(const void* kv_in, void* kv_out, int64_t rows, int64_t d,
+                  const float* norm_weight, int64_t norm_dim, float eps,
+                  const float* freqs, const int32_t* positions, int64_t npos,
+                  int64_t rope_dim, int64_t quant_dims, int32_t round_scale,
+                  void* cache, const int32_t* cache_slots, int64_t cache_rows,
+                  void* stream);
+
+/* ------------------------------------------------------------------------
  * Absorbed-MLA decode layer (BASELINE decode configs; the reference's V4
  * attention has no wkv_b, so these extend its surface).  Weights:
  *   wq_b   [h*(d_nope+d_rope), dc] e4m3 + scale [.. /128, dc/128]

@@ -55,6 +55,8 @@ def lib() -> ctypes.CDLL:
         _lib.orc_paged_decode_attn.argtypes = [P, P, P, P, P, I, I, I, I, I, I, I, F, P, P]
         _lib.orc_mla_absorb.argtypes = [P, I, P, I, I, I, I, I, P, I]
         _lib.orc_mla_vup.argtypes = [P, P, I, I, I, I, I, P]
+        _lib.orc_kv_build.argtypes = [P, I, I, P, I, F, P, P, I, I, i32]
+        _lib.orc_grouped_proj.argtypes = [P, P, I, I, I, I, P]
         _lib.orc_f32_to_bf16_n.argtypes = [P, P, I]
         _lib.orc_f32_to_e4m3_n.argtypes = [P, P, I]
         _lib.orc_e4m3_to_f32.argtypes = [ctypes.c_uint8]
@@ -127,6 +129,32 @@ def act_quant_inplace(x_bf16: np.ndarray, block: int, round_scale: bool) -> np.n
     n = x.shape[-1]
     lib().orc_act_quant_inplace(_p(x), x.size // n, n, block, int(round_scale))
     return x
+
+
+def kv_build(x_bf16: np.ndarray, weight: np.ndarray | None, norm_dim: int, eps: float,
+             freqs: np.ndarray, positions: np.ndarray, rope_dim: int, quant_dims: int,
+             round_scale: bool) -> np.ndarray:
+    """model.py:502-506 on rows [rows, d] bf16: RMSNorm, RoPE, FP8 round trip."""
+    x = np.array(x_bf16, dtype=np.uint16, copy=True, order="C")
+    d = x.shape[-1]
+    w = None if weight is None else np.ascontiguousarray(weight, dtype=np.float32)
+    f = np.ascontiguousarray(freqs, dtype=np.float32)
+    pos = np.ascontiguousarray(positions, dtype=np.int32)
+    lib().orc_kv_build(_p(x), x.size // d, d, _p(w), norm_dim, float(eps), _p(f),
+                       _p(pos), rope_dim, quant_dims, int(round_scale))
+    return x
+
+
+def grouped_proj(o_bf16: np.ndarray, w_bf16: np.ndarray) -> np.ndarray:
+    """model.py:537-541 einsum bsgd,grd->bsgr: o [rows, G, gd], w [G, R, gd]
+    -> [rows, G, R] bf16 (fp32 sums)."""
+    o = np.ascontiguousarray(o_bf16, dtype=np.uint16)
+    w = np.ascontiguousarray(w_bf16, dtype=np.uint16)
+    G, R, gd = w.shape
+    rows = o.size // (G * gd)
+    h = np.empty((rows, G, R), dtype=np.uint16)
+    lib().orc_grouped_proj(_p(o), _p(w), rows, G, gd, R, _p(h))
+    return h
 
 
 def fp8_gemm(a_u8, a_s, b_u8, b_s) -> np.ndarray:

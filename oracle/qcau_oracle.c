@@ -259,6 +259,39 @@ void orc_rope(uint16_t* x, int64_t rows, int64_t row_stride, int64_t d,
 }
 
 /* ------------------------------------------------------------------ */
+/* KV build: Deepseek_origin/inference/model.py:502-506, in place on   */
+/* rows [rows, d] bf16:                                                */
+/*   RMSNorm of values [0, norm_dim) (model.py:182-195): fp32 squares, */
+/*   var = mean, x * (1 / sqrt(var + eps)) (torch's CPU rsqrt), times  */
+/*   the fp32 weight, rounded to bf16 once                             */
+/*   RoPE of the last rope_dim values at positions[r] (:231-243)       */
+/*   act_quant(kv[..., :quant_dims], 64, fmt, inplace=True) (:505)     */
+/* ------------------------------------------------------------------ */
+void orc_kv_build(uint16_t* x, int64_t rows, int64_t d, const float* w,
+                  int64_t norm_dim, float eps, const float* freqs,
+                  const int32_t* positions, int64_t rope_dim,
+                  int64_t quant_dims, int round_scale) {
+    for (int64_t r = 0; r < rows; r++) {
+        uint16_t* xr = x + r * d;
+        if (norm_dim > 0) {
+            float acc = 0.0f;
+            for (int64_t j = 0; j < norm_dim; j++) {
+                float v = orc_bf16_to_f32(xr[j]);
+                acc += v * v;
+            }
+            float rs = 1.0f / sqrtf(acc / (float)norm_dim + eps);
+            for (int64_t j = 0; j < norm_dim; j++) {
+                float v = orc_bf16_to_f32(xr[j]) * rs;
+                xr[j] = orc_f32_to_bf16((w ? w[j] : 1.0f) * v);
+            }
+        }
+        if (rope_dim > 0)
+            orc_rope(xr, 1, d, d, rope_dim, freqs, 1, 1, positions[r], 0);
+        if (quant_dims > 0) orc_act_quant_inplace(xr, 1, quant_dims, 64, round_scale);
+    }
+}
+
+/* ------------------------------------------------------------------ */
 /* Attention core: Deepseek_origin/inference/kernel.py:276-352 with    */
 /* the guards of QCAU/QCAU_inference/inference/QCAU.py:176-242 and the */
 /* bf16 rounding of P before P.V (kernel.py:340, check/QCAU.py:263).   */
@@ -429,6 +462,26 @@ void orc_mla_vup(const uint16_t* o_lat, const uint16_t* wkv, int64_t bsz, int64_
                 for (int64_t c = 0; c < kv_lora; c++)
                     acc += orc_bf16_to_f32(o[c]) * orc_bf16_to_f32(w[d * kv_lora + c]);
                 o_v[(b * h + hh) * d_v + d] = orc_f32_to_bf16(acc);
+            }
+        }
+}
+
+/* Grouped low-rank projection wo_a: Deepseek_origin/inference/model.py:  */
+/* 537-541, einsum("bsgd,grd->bsgr", o, wo_a) in bf16 (fp32 sums, bf16   */
+/* result): o [rows, groups, gd], w [groups, rank, gd] -> h [rows, groups, */
+/* rank].                                                                 */
+void orc_grouped_proj(const uint16_t* o, const uint16_t* w, int64_t rows, int64_t groups,
+                      int64_t gd, int64_t rank, uint16_t* h) {
+    #pragma omp parallel for collapse(2)
+    for (int64_t r = 0; r < rows; r++)
+        for (int64_t g = 0; g < groups; g++) {
+            const uint16_t* a = o + (r * groups + g) * gd;
+            for (int64_t j = 0; j < rank; j++) {
+                const uint16_t* b = w + (g * rank + j) * gd;
+                float acc = 0.0f;
+                for (int64_t c = 0; c < gd; c++)
+                    acc += orc_bf16_to_f32(a[c]) * orc_bf16_to_f32(b[c]);
+                h[(r * groups + g) * rank + j] = orc_f32_to_bf16(acc);
             }
         }
 }

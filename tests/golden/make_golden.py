@@ -19,6 +19,11 @@ Outputs (compressed .npz, raw bit patterns: bf16 as uint16, fp8/e8m0 as uint8):
   and sequence-length-16 cases keep 4 (heads are independent in the MQA core,
   kernel.py:301-343, so a head subset is an exact sub-problem); length-1 cases
   keep all 64.
+* kv_build.npz -- the reference's KV build (model.py RMSNorm, RoPE with the
+  YaRN freqs of a compressed layer, kernel_fallback.act_quant in place, block
+  64, UE8M0) on seeded rows.
+* gopu.npz -- the reference's output side (the wo_a einsum and wo_b through
+  linear() on kernel_fallback's FP8 kernels) on seeded tensors.
 * ref_synthetic.npz -- seeded synthetic inputs run through the reference's
   own PyTorch CPU path, imported here by file path:
   kernel_fallback.act_quant / fp8_gemm (QCAU/QCAU_inference/inference/
@@ -51,17 +56,16 @@ def load_module(name: str, path: Path):
     return mod
 
 
-def read_shape(case: Path, name: str):
-    return tuple(int(x) for x in (case / f"{name}.shape.txt").read_text().split())
+sys.path.insert(0, str(Path(__file__).resolve().parents[2] / "deepseek-v4-flash_b200"))
+from qcau_b200.golden_io import read_shape, read_tensor  # noqa: E402  (the library's reader)
 
 
 def read_hex(case: Path, fname: str, dtype) -> np.ndarray:
-    vals = [int(line, 16) for line in (case / fname).read_text().split()]
-    return np.asarray(vals, dtype=dtype)
+    return read_tensor(case, fname.split(".")[0]).ravel().astype(dtype)
 
 
 def read_text(case: Path, fname: str, dtype) -> np.ndarray:
-    return np.asarray((case / fname).read_text().split(), dtype=np.float64).astype(dtype)
+    return read_tensor(case, fname.split(".")[0]).ravel().astype(dtype)
 
 
 def head_subset(seq: int, n_heads: int) -> np.ndarray:
@@ -221,10 +225,76 @@ def synthetic():
     np.savez_compressed(OUT / "ref_synthetic.npz", **out)
 
 
+def kv_build_fixture():
+    """kv_build.npz: the reference's KV build (Deepseek_origin/inference/
+    model.py:502-505) run by its own code on seeded rows: RMSNorm
+    (model.py:182-195), apply_rotary_emb of the last 64 values (:231-243) with
+    the YaRN freqs_cis of a compressed layer (precompute_freqs_cis :198-228),
+    then kernel_fallback.act_quant(kv[..., :-64], 64, "ue8m0", inplace=True)
+    (the QCAU package's CPU kernels standing in for kernel.py)."""
+    kf = load_module("kernel_fallback_kv", INF / "kernel_fallback.py")
+    sys.modules["kernel"] = kf
+    model = load_module("ref_model_v4", REF / "Deepseek_origin/inference/model.py")
+    g = torch.Generator().manual_seed(11)
+    rows, d, rd = 96, 512, 64
+    x = (torch.randn(rows, d, generator=g) * 3.0).to(torch.bfloat16)
+    w = 1.0 + 0.1 * torch.randn(d, generator=g)
+    pos = torch.randint(0, 8192, (rows,), generator=g)
+    freqs = model.precompute_freqs_cis(rd, 8192, 65536, 160000.0, 16.0, 32, 1)
+    # the table rows the positions use, so the fixture stays small: row r of
+    # "freqs" is freqs_cis[positions[r]] (the kernel reads it at position r)
+    out = {"x": u16(x), "weight": w.numpy().astype(np.float32),
+           "positions": pos.numpy().astype(np.int32),
+           "freqs": torch.view_as_real(freqs[pos]).numpy().astype(np.float32)}
+    norm = model.RMSNorm(d, 1e-6)
+    with torch.no_grad():
+        norm.weight.copy_(w)
+        kv = norm(x.unsqueeze(0))                         # [1, rows, 512] bf16
+        model.apply_rotary_emb(kv[..., -rd:], freqs[pos])
+        out["after_norm_rope"] = u16(kv[0].clone())
+        kf.act_quant(kv[..., :-rd], 64, "ue8m0", torch.float8_e8m0fnu, True)
+    out["kv"] = u16(kv[0])
+    np.savez_compressed(OUT / "kv_build.npz", **out)
+
+
+def gopu_fixture():
+    """gopu.npz: the reference's output side (model.py:536-542) run by its own
+    code on seeded tensors at reduced widths (8 heads of 512 in 2 groups,
+    o_lora_rank 128, dim 256): the bf16 einsum with wo_a, then wo_b through
+    linear() (model.py:108-120) on kernel_fallback's act_quant / fp8_gemm with
+    UE8M0 scales."""
+    kf = load_module("kernel_fallback_gopu", INF / "kernel_fallback.py")
+    sys.modules["kernel"] = kf
+    model = load_module("ref_model_v4_gopu", REF / "Deepseek_origin/inference/model.py")
+    model.scale_fmt, model.scale_dtype = "ue8m0", torch.float8_e8m0fnu
+    g = torch.Generator().manual_seed(13)
+    B, S, H, D, G, R, dim = 2, 3, 8, 512, 2, 128, 256
+    o = torch.randn(B, S, H, D, generator=g).to(torch.bfloat16)
+    wo_a = (torch.randn(G * R, H * D // G, generator=g) * 0.02).to(torch.bfloat16)
+    w = torch.randn(dim, G * R, generator=g) * 0.02
+    blk = w.view(dim // 128, 128, G * R // 128, 128)
+    sc = torch.exp2(torch.ceil(torch.log2(blk.abs().amax(dim=(1, 3)).clamp_min(1e-4) / 448.0)))
+    wq = (blk / sc[:, None, :, None]).clamp(-448, 448).view(dim, G * R).to(torch.float8_e4m3fn)
+    wq.scale = sc.to(torch.float8_e8m0fnu)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)  # the model's (generate.py), fp8_gemm's out dtype
+    try:
+        with torch.no_grad():
+            h = torch.einsum("bsgd,grd->bsgr", o.view(B, S, G, -1), wo_a.view(G, R, -1))
+            y = model.linear(h.flatten(2), wq)
+    finally:
+        torch.set_default_dtype(prev)
+    out = {"o": u16(o), "wo_a": u16(wo_a), "wo_b": wq.view(torch.uint8).numpy(),
+           "wo_b_scale": wq.scale.view(torch.uint8).numpy(), "h": u16(h), "y": u16(y)}
+    np.savez_compressed(OUT / "gopu.npz", **out)
+
+
 if __name__ == "__main__":
     if not VEC.exists():
         sys.exit(f"reference test vectors not found under {REF} (set QCAU_REFERENCE_ROOT)")
     goldens()
     synthetic()
+    kv_build_fixture()
+    gopu_fixture()
     for f in sorted(OUT.glob("*.npz")):
         print(f.name, f.stat().st_size)
