@@ -169,15 +169,16 @@ cudaError_t launch_bf16_bmm(const BmmArgs& p, cudaStream_t st) {
                    CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
   }
+  const int64_t b_rows = p.b_rows > 0 ? p.b_rows : p.n;
   if (p.b_kmajor) {
-    const uint64_t dims[3] = {(uint64_t)p.k, (uint64_t)p.n, (uint64_t)p.batch};
+    const uint64_t dims[3] = {(uint64_t)p.k, (uint64_t)b_rows, (uint64_t)p.batch};
     const uint64_t strides[2] = {(uint64_t)p.b_rstride * 2, (uint64_t)p.b_bstride * 2};
     const uint32_t box[3] = {BK, BN, 1};
     if (!make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, p.b, dims, strides, box,
                    CU_TENSOR_MAP_SWIZZLE_128B))
       return cudaErrorInvalidValue;
   } else {
-    const uint64_t dims[3] = {(uint64_t)p.n, (uint64_t)p.k, (uint64_t)p.batch};
+    const uint64_t dims[3] = {(uint64_t)b_rows, (uint64_t)p.k, (uint64_t)p.batch};
     const uint64_t strides[2] = {(uint64_t)p.b_rstride * 2, (uint64_t)p.b_bstride * 2};
     const uint32_t box[3] = {64, BK, 1};
     if (!make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, p.b, dims, strides, box,

@@ -748,6 +748,128 @@ int qcau_gopu(const void* o, const void* wo_a, const void* wo_b, const void* wo_
   return QCAU_OK;
 }
 
+int qcau_rotate_fp4(void* x, int64_t rows, int64_t d, int32_t hadamard, int32_t fp4,
+                    void* stream) {
+  QCAU_CHECK_ARG(x != nullptr, "rotate_fp4: x is NULL");
+  QCAU_CHECK_ARG(rows >= 0 && d == 128, "rotate_fp4: rows of 128 values are supported");
+  QCAU_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 7) == 0, "rotate_fp4: x must be 8-byte aligned");
+  QCAU_CHECK_CUDA(launch_rotate_fp4(x, rows, hadamard ? 1 : 0, fp4 ? 1 : 0, to_stream(stream)));
+  return QCAU_OK;
+}
+
+static int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+static size_t indexer_raw_bytes(int64_t b, int64_t s, int64_t h, int64_t t) {
+  return align256((size_t)(b * s * h * round_up(t > 0 ? t : 1, 128) * 2));
+}
+
+size_t qcau_indexer_scores_workspace_size(int64_t b, int64_t s, int64_t h, int64_t t) {
+  return indexer_raw_bytes(b, s, h, t);
+}
+
+size_t qcau_indexer_topk_workspace_size(int64_t b, int64_t s, int64_t h, int64_t t) {
+  return indexer_raw_bytes(b, s, h, t) + align256((size_t)(b * s * t * 4));
+}
+
+int qcau_indexer_scores(const void* q, const void* kv, const void* weights, float* score,
+                        int64_t b, int64_t s, int64_t h, int64_t d, int64_t t, int64_t kv_rows,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  QCAU_CHECK_ARG(q && kv && weights && score, "indexer_scores: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && s >= 0 && h > 0 && t >= 0 && kv_rows >= t,
+                 "indexer_scores: bad shape");
+  QCAU_CHECK_ARG(d % 64 == 0 && d > 0, "indexer_scores: head_dim must be a multiple of 64");
+  QCAU_CHECK_ARG(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kv)) & 15) == 0,
+                 "indexer_scores: q and kv must be 16-byte aligned");
+  const size_t need = indexer_raw_bytes(b, s, h, t);
+  if (workspace_bytes < need || !workspace)
+    return fail(QCAU_ERR_WORKSPACE,
+                "indexer_scores: workspace too small (need " + std::to_string(need) + " bytes)");
+  if (b * s == 0 || t == 0) return QCAU_OK;
+  cudaStream_t st = to_stream(stream);
+  const int64_t tp = round_up(t, 128);
+  // raw[b, (s, h), u] = q[b, s, h, :] . kv[b, u, :], the bf16 einsum
+  // (model.py:518); the B tensor map holds the t rows that exist, the rest of
+  // the last 128-row tile reads as zeros
+  BmmArgs m{};
+  m.a = q;
+  m.a_bstride = s * h * d;
+  m.a_rstride = d;
+  m.b = kv;
+  m.b_bstride = kv_rows * d;
+  m.b_rstride = d;
+  m.b_kmajor = 1;
+  m.b_rows = t;
+  m.c = workspace;
+  m.c_bstride = s * h * tp;
+  m.c_rstride = tp;
+  m.batch = b;
+  m.m = s * h;
+  m.n = tp;
+  m.k = d;
+  QCAU_CHECK_CUDA(launch_bf16_bmm(m, st));
+  QCAU_CHECK_CUDA(launch_index_score(workspace, weights, score, b * s, (int)h, t, tp, st));
+  return QCAU_OK;
+}
+
+int qcau_topk(const float* score, int32_t* topk_idxs, int64_t rows, int64_t t, int64_t k,
+              int64_t seqlen, int64_t mask_ratio, int64_t offset, void* stream) {
+  QCAU_CHECK_ARG((score || rows * t == 0) && (topk_idxs || rows * k == 0), "topk: NULL pointer");
+  QCAU_CHECK_ARG(rows >= 0 && t >= 0 && k >= 0 && k <= 2048, "topk: k up to 2048 is supported");
+  QCAU_CHECK_ARG(mask_ratio >= 0 && (mask_ratio == 0 || seqlen > 0),
+                 "topk: the prefill mask needs seqlen");
+  QCAU_CHECK_CUDA(launch_topk(score, rows, t, (int)k, topk_idxs, offset, seqlen, (int)mask_ratio,
+                              to_stream(stream)));
+  return QCAU_OK;
+}
+
+int qcau_indexer_topk(const void* q, const void* kv, const void* weights, int32_t* topk_idxs,
+                      int64_t b, int64_t s, int64_t h, int64_t d, int64_t t, int64_t kv_rows,
+                      int64_t k, int64_t start_pos, int64_t ratio, int64_t offset,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  QCAU_CHECK_ARG(topk_idxs != nullptr, "indexer_topk: topk_idxs is NULL");
+  QCAU_CHECK_ARG(k >= 0 && k <= 2048, "indexer_topk: index_topk up to 2048 is supported");
+  QCAU_CHECK_ARG(ratio > 0 && start_pos >= 0, "indexer_topk: bad ratio or start_pos");
+  const size_t need = qcau_indexer_topk_workspace_size(b, s, h, t);
+  if (workspace_bytes < need || !workspace)
+    return fail(QCAU_ERR_WORKSPACE,
+                "indexer_topk: workspace too small (need " + std::to_string(need) + " bytes)");
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  const size_t raw_bytes = indexer_raw_bytes(b, s, h, t);
+  float* score = reinterpret_cast<float*>(ws + raw_bytes);
+  const int rc =
+      qcau_indexer_scores(q, kv, weights, score, b, s, h, d, t, kv_rows, ws, raw_bytes, stream);
+  if (rc != QCAU_OK) return rc;
+  return qcau_topk(score, topk_idxs, b * s, t, k, s, start_pos == 0 ? ratio : 0, offset, stream);
+}
+
+int qcau_index_lists(int32_t* topk_idxs, int64_t bsz, int64_t seqlen, int64_t start_pos,
+                     int64_t window, int64_t ratio, int64_t offset, const int32_t* selected,
+                     int64_t selected_width, void* stream) {
+  QCAU_CHECK_ARG(topk_idxs != nullptr, "index_lists: output is NULL");
+  QCAU_CHECK_ARG(bsz >= 0 && seqlen >= 0 && start_pos >= 0 && window > 0 && ratio >= 0,
+                 "index_lists: bad arguments");
+  QCAU_CHECK_ARG(start_pos == 0 || seqlen == 1, "index_lists: decode steps have one token");
+  const int64_t win_w = start_pos == 0 ? (seqlen < window ? seqlen : window) : window;
+  int64_t comp_w = 0;
+  if (selected) {
+    comp_w = selected_width;
+  } else if (ratio > 0) {
+    comp_w = start_pos > 0 ? (start_pos + 1) / ratio : seqlen / ratio;
+  }
+  QCAU_CHECK_CUDA(launch_index_lists(topk_idxs, bsz, seqlen, start_pos, (int)window,
+                                     (int)(ratio > 0 ? ratio : 1), offset, (int)win_w,
+                                     (int)comp_w, selected, to_stream(stream)));
+  return QCAU_OK;
+}
+
+int64_t qcau_index_lists_width(int64_t seqlen, int64_t start_pos, int64_t window, int64_t ratio,
+                               int64_t selected_width) {
+  const int64_t win_w = start_pos == 0 ? (seqlen < window ? seqlen : window) : window;
+  if (selected_width > 0) return win_w + selected_width;
+  if (ratio <= 0) return win_w;
+  return win_w + (start_pos > 0 ? (start_pos + 1) / ratio : seqlen / ratio);
+}
+
 int qcau_kv_build(const void* kv_in, void* kv_out, int64_t rows, int64_t d,
                   const float* norm_weight, int64_t norm_dim, float eps, const float* freqs,
                   const int32_t* positions, int64_t npos, int64_t rope_dim, int64_t quant_dims,

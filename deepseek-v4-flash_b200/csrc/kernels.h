@@ -78,8 +78,22 @@ struct BmmArgs {
   void* c;
   int64_t c_bstride, c_rstride;
   int64_t batch, m, n, k;
+  int64_t b_rows;  // rows of B that exist (0: n); TMA zero-fills the rest
 };
 cudaError_t launch_bf16_bmm(const BmmArgs& args, cudaStream_t st);
+
+// Indexer pieces (indexer.cu): the score scaling of its 128-wide rows
+// (Walsh-Hadamard, FP4 e2m1 block-32 round trip), the weighted ReLU head sum
+// of the raw scores with the prefill mask, the top-k selection, and the
+// window / compressed index lists.
+cudaError_t launch_rotate_fp4(void* x, int64_t rows, int hadamard, int fp4, cudaStream_t st);
+cudaError_t launch_index_score(const void* raw, const void* w, float* score, int64_t rows, int h,
+                               int64_t t_len, int64_t t_pad, cudaStream_t st);
+cudaError_t launch_topk(const float* score, int64_t rows, int64_t t_len, int k, int32_t* out,
+                        int64_t offset, int64_t s_len, int mask_ratio, cudaStream_t st);
+cudaError_t launch_index_lists(int32_t* out, int64_t bsz, int64_t seqlen, int64_t start_pos,
+                               int window, int ratio, int64_t offset, int win_w, int comp_w,
+                               const int32_t* sel, cudaStream_t st);
 
 // Split-KV attention arguments (gather by index or dense paged).
 struct AttnArgs {

@@ -331,6 +331,72 @@ int qcau_kv_build(const void* kv_in, void* kv_out, int64_t rows, int64_t d,
                   void* stream);
 
 /* ------------------------------------------------------------------------
+ * Index-list producers: what the sparse attention's topk_idxs come from.
+ *
+ * qcau_rotate_fp4 -- in place on rows of 128 bf16 values: the Walsh-Hadamard
+ *   rotation rotate_activation (QCAU/QCAU_inference/inference/model.py:302-
+ *   323: Sylvester order, fp32 butterflies, times 128^-1/2, back to bf16;
+ *   the reference's own restatement of the third-party fast_hadamard_
+ *   transform) when `hadamard`, then, when `fp4`, fp4_act_quant(x, 32,
+ *   inplace=True) (Deepseek_origin/inference/kernel.py:128-200: per 1x32
+ *   block s = 2^ceil(log2(max(amax, 6*2^-126) * (1/6))), x/s clamped to
+ *   +-6 and rounded to FP4 e2m1, times s, to bf16).  The Indexer applies both
+ *   to its queries (model.py:512-514) and its Compressor to the pooled key
+ *   rows (model.py:466-468).  d must be 128.
+ *
+ * qcau_indexer_topk -- Indexer.forward after the projections
+ *   (model.py:518-533): with q [b, s, h, d] bf16 (rotated + FP4), kv the
+ *   indexer's compressed cache [b, kv_rows, d] bf16 of which the first
+ *   t = end_pos / ratio rows of each sequence are read,
+ *   weights [b, s, h] bf16 (weights_proj(x) * softmax_scale * h^-1/2),
+ *     score[b, s, u] = bf16(sum_h bf16(relu(bf16(q[b,s,h] . kv[b,u])) * w[b,s,h]))
+ *   masked to -inf at prefill (start_pos == 0) where u >= (s + 1) / ratio,
+ *   then topk_idxs [b, s, k] int32 = the k largest per row (score
+ *   descending, equal scores by index ascending) + offset; entries past a
+ *   row's finite scores are -1, as the reference's mask makes them.  k is
+ *   min(index_topk, t) in the reference (<= 2048 here); d a multiple of 64.
+ *   The workspace holds the raw scores and the score rows:
+ *   qcau_indexer_topk_workspace_size(b, s, h, t) bytes.
+ *   Its two halves, for head-sharded ranks that all-reduce the score rows
+ *   between them (model.py:520-521):
+ *   qcau_indexer_scores -- score [b, s, t] fp32 (bf16 values), unmasked;
+ *     workspace qcau_indexer_scores_workspace_size(b, s, h, t) bytes.
+ *   qcau_topk -- topk_idxs [rows, k] of score [rows, t]: the k largest of a
+ *     row, score descending then index ascending, + offset, -1 past the
+ *     row's candidates; -inf is never taken, and with mask_ratio > 0 (a
+ *     prefill: the indexer's ratio) neither are positions >= (row % seqlen
+ *     + 1) / mask_ratio.  A drop-in for score.topk(k, dim=-1)[1] whenever
+ *     the row's k-th score has no equal outside the selection.
+ *
+ * qcau_index_lists -- the [bsz, seqlen, W] int32 index list the attention
+ *   reads: get_window_topk_idxs(window, bsz, seqlen, start_pos)
+ *   (model.py:326-357) followed by either `selected` [bsz, seqlen,
+ *   selected_width] (the indexer's list, offset included) or, when
+ *   `selected` is NULL and ratio > 0, get_compress_topk_idxs(ratio, bsz,
+ *   seqlen, start_pos, offset) (model.py:359-376), as Attention.forward
+ *   concatenates them (model.py:614-624).  W = qcau_index_lists_width(...).
+ *   Decode steps (start_pos > 0) have seqlen 1.
+ * ---------------------------------------------------------------------- */
+int qcau_rotate_fp4(void* x, int64_t rows, int64_t d, int32_t hadamard, int32_t fp4,
+                    void* stream);
+size_t qcau_indexer_topk_workspace_size(int64_t b, int64_t s, int64_t h, int64_t t);
+size_t qcau_indexer_scores_workspace_size(int64_t b, int64_t s, int64_t h, int64_t t);
+int qcau_indexer_scores(const void* q, const void* kv, const void* weights, float* score,
+                        int64_t b, int64_t s, int64_t h, int64_t d, int64_t t, int64_t kv_rows,
+                        void* workspace, size_t workspace_bytes, void* stream);
+int qcau_topk(const float* score, int32_t* topk_idxs, int64_t rows, int64_t t, int64_t k,
+              int64_t seqlen, int64_t mask_ratio, int64_t offset, void* stream);
+int qcau_indexer_topk(const void* q, const void* kv, const void* weights, int32_t* topk_idxs,
+                      int64_t b, int64_t s, int64_t h, int64_t d, int64_t t, int64_t kv_rows,
+                      int64_t k, int64_t start_pos, int64_t ratio, int64_t offset,
+                      void* workspace, size_t workspace_bytes, void* stream);
+int64_t qcau_index_lists_width(int64_t seqlen, int64_t start_pos, int64_t window,
+                               int64_t ratio, int64_t selected_width);
+int qcau_index_lists(int32_t* topk_idxs, int64_t bsz, int64_t seqlen, int64_t start_pos,
+                     int64_t window, int64_t ratio, int64_t offset, const int32_t* selected,
+                     int64_t selected_width, void* stream);
+
+/* ------------------------------------------------------------------------
  * Absorbed-MLA decode layer (BASELINE decode configs; the reference's V4
  * attention has no wkv_b, so these extend its surface).  Weights:
  *   wq_b   [h*(d_nope+d_rope), dc] e4m3 + scale [.. /128, dc/128]

@@ -22,6 +22,9 @@ Outputs (compressed .npz, raw bit patterns: bf16 as uint16, fp8/e8m0 as uint8):
 * kv_build.npz -- the reference's KV build (model.py RMSNorm, RoPE with the
   YaRN freqs of a compressed layer, kernel_fallback.act_quant in place, block
   64, UE8M0) on seeded rows.
+* indexer.npz -- the index-list producers (window / compressed lists, the
+  Hadamard rotation, and Indexer.forward of a small seeded indexer) run by
+  the QCAU package's model.py on kernel_fallback.
 * gopu.npz -- the reference's output side (the wo_a einsum and wo_b through
   linear() on kernel_fallback's FP8 kernels) on seeded tensors.
 * ref_synthetic.npz -- seeded synthetic inputs run through the reference's
@@ -289,6 +292,131 @@ def gopu_fixture():
     np.savez_compressed(OUT / "gopu.npz", **out)
 
 
+def load_qcau_inference_model():
+    """QCAU/QCAU_inference/inference/model.py imported as a package module
+    whose `.kernel` is kernel_fallback.py (the TileLang kernels need a GPU);
+    its rotate_activation then runs its own fp32 Hadamard restatement, since
+    fast_hadamard_transform is not installed."""
+    import types
+
+    name = "qcau_ref_inference"
+    if f"{name}.model" in sys.modules:
+        return sys.modules[f"{name}.model"]
+    pkg = types.ModuleType(name)
+    pkg.__path__ = [str(INF)]
+    sys.modules[name] = pkg
+
+    def load(sub):
+        spec = importlib.util.spec_from_file_location(f"{name}.{sub}", INF / f"{sub}.py")
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[spec.name] = mod
+        spec.loader.exec_module(mod)
+        return mod
+
+    sys.modules[f"{name}.kernel"] = load("kernel_fallback")
+    return load("model")
+
+
+def indexer_fixture():
+    """indexer.npz: the index-list producers run by the reference's own code
+    (QCAU/QCAU_inference/inference/model.py):
+
+    * lists/<i>: get_window_topk_idxs and get_compress_topk_idxs concatenated
+      as Attention.forward does (model.py:614-624), for the (window, ratio,
+      bsz, seqlen, start_pos, offset) of list_params[i];
+    * rot_x / rot_y: rotate_activation on seeded rows (its fp32 restatement);
+    * step<i>/...: Indexer.forward (model.py:500-534) of a seeded small
+      indexer (8 heads of 128, index_topk 8, ratio 4, bf16 projections) over
+      a 64-token prefill of 2 sequences and 4 decode steps: the queries before
+      rotation (q_pre) and as the einsum reads them (q), the compressed keys
+      (kv = kv_cache[:b, :end_pos // 4]), the head weights (w), the masked
+      score rows (score, recomputed from those tensors by the same expressions)
+      and the returned topk_idxs (idx).  kernel_fallback's fp4_act_quant does
+      not round to FP4, so q equals rotate_activation(q_pre) here."""
+    model = load_qcau_inference_model()
+    out = {}
+    params = []
+    cases = [(8, 4, 2, 5, 0, 5), (8, 4, 2, 21, 0, 21), (128, 4, 1, 300, 0, 300),
+             (128, 128, 2, 300, 0, 300), (128, 0, 2, 130, 0, 0), (8, 4, 3, 1, 3, 8),
+             (8, 4, 3, 1, 7, 8), (8, 4, 3, 1, 8, 8), (8, 4, 2, 1, 22, 8),
+             (128, 4, 2, 1, 131, 128), (128, 128, 2, 1, 1000, 128), (128, 128, 2, 1, 127, 128),
+             (128, 4, 1, 1, 126, 128), (128, 0, 2, 1, 200, 128)]
+    for i, (win, ratio, bsz, seqlen, sp, off) in enumerate(cases):
+        w = model.get_window_topk_idxs(win, bsz, seqlen, sp)
+        if ratio:
+            c = model.get_compress_topk_idxs(ratio, bsz, seqlen, sp, off)
+            w = torch.cat([w, c], dim=-1)
+        out[f"lists/{i}"] = w.int().numpy()
+        params.append((win, ratio, bsz, seqlen, sp, off))
+    out["list_params"] = np.array(params, dtype=np.int64)
+
+    g = torch.Generator().manual_seed(17)
+    x = (torch.randn(64, 128, generator=g) * 2).to(torch.bfloat16)
+    out["rot_x"] = u16(x)
+    out["rot_y"] = u16(model.rotate_activation(x))
+
+    args = model.ModelArgs(max_batch_size=2, max_seq_len=256, dim=256, q_lora_rank=128,
+                           index_n_heads=8, index_head_dim=128, index_topk=8)
+    torch.manual_seed(19)
+    prev_dtype = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)  # the model's (generate.py): bf16 kv_cache buffers
+    idx = model.Indexer(args, 4)
+    with torch.no_grad():
+        for n, p in idx.named_parameters():
+            if n.endswith("norm.weight"):
+                p.copy_(1.0 + 0.1 * torch.randn(p.shape, generator=g))
+            elif n.endswith("ape"):
+                p.copy_(0.1 * torch.randn(p.shape, generator=g))
+            else:
+                p.copy_((torch.randn(p.shape, generator=g) / p.shape[-1] ** 0.5).to(p.dtype))
+    idx.freqs_cis = model.precompute_freqs_cis(64, 256, 0, 10000.0, 40, 32, 1)
+    rec = {}
+    real_rot, real_fp4 = model.rotate_activation, model.fp4_act_quant
+
+    def rot(t):
+        y = real_rot(t)
+        if t.dim() == 4:
+            rec["q_pre"] = t.clone()
+        return y
+
+    def fp4(t, block, inplace=False):
+        y = real_fp4(t, block, inplace)
+        if t.dim() == 4:
+            rec["q"] = t.clone()
+        return y
+
+    model.rotate_activation, model.fp4_act_quant = rot, fp4
+    idx.weights_proj.register_forward_hook(lambda m, a, o: rec.__setitem__("w_proj", o.clone()))
+    try:
+        B, S = 2, 64
+        steps = [(0, S)] + [(S + i, 1) for i in range(4)]
+        for i, (sp, sl) in enumerate(steps):
+            x = torch.randn(B, sl, 256, generator=g).to(torch.bfloat16)
+            qr = torch.randn(B, sl, 128, generator=g).to(torch.bfloat16)
+            offset = sl if sp == 0 else 128  # Attention.forward: kv.size(1) at prefill, else win
+            with torch.no_grad():
+                topk_idxs = idx(x, qr, sp, offset)
+                end = sp + sl
+                kv = idx.kv_cache[:B, :end // 4]
+                w = rec["w_proj"] * (idx.softmax_scale * idx.n_heads ** -0.5)
+                sc = torch.einsum("bshd,btd->bsht", rec["q"], kv)
+                sc = (sc.relu_() * w.unsqueeze(-1)).sum(dim=2)
+                if sp == 0:
+                    mask = torch.arange(sl // 4).repeat(sl, 1) >= torch.arange(1, sl + 1).unsqueeze(1) // 4
+                    sc += torch.where(mask, float("-inf"), 0)
+            out[f"step{i}/meta"] = np.array([sp, sl, offset], dtype=np.int64)
+            out[f"step{i}/q_pre"] = u16(rec["q_pre"])
+            out[f"step{i}/q"] = u16(rec["q"])
+            out[f"step{i}/kv"] = u16(kv.contiguous())
+            out[f"step{i}/w"] = u16(w)
+            out[f"step{i}/score"] = sc.float().numpy()
+            out[f"step{i}/idx"] = topk_idxs.int().numpy()
+    finally:
+        model.rotate_activation, model.fp4_act_quant = real_rot, real_fp4
+        torch.set_default_dtype(prev_dtype)
+    np.savez_compressed(OUT / "indexer.npz", **out)
+
+
 if __name__ == "__main__":
     if not VEC.exists():
         sys.exit(f"reference test vectors not found under {REF} (set QCAU_REFERENCE_ROOT)")
@@ -296,5 +424,6 @@ if __name__ == "__main__":
     synthetic()
     kv_build_fixture()
     gopu_fixture()
+    indexer_fixture()
     for f in sorted(OUT.glob("*.npz")):
         print(f.name, f.stat().st_size)
