@@ -6,9 +6,10 @@ sm_100a kernels of libqcau_b200.so.  Installing this module as
 ``sys.modules["kernel"]`` makes the reference ``model.py`` (which does
 ``from kernel import ...``, model.py:12) run its QCAU path on these kernels.
 
-The FP4 and mHC kernels of the reference module (fp4_act_quant, fp4_gemm,
-hc_split_sinkhorn) are outside the QCAU path; they are exported so the import
-succeeds, and raise NotImplementedError when called.
+fp4_act_quant serves the indexer's in-place FP4 round trip (kernel.py:186-200
+with inplace=True).  The FP4 GEMM and the mHC kernel of the reference module
+(fp4_gemm, hc_split_sinkhorn) are outside the QCAU path; they are exported so
+the import succeeds, and raise NotImplementedError when called.
 """
 from __future__ import annotations
 
@@ -124,6 +125,32 @@ def _outside(name: str):
     return f
 
 
-fp4_act_quant = _outside("fp4_act_quant")
+def fp4_act_quant(x: torch.Tensor, block_size: int = 32, inplace: bool = False) -> torch.Tensor:
+    """Block-wise FP4 e2m1 quantisation (kernel.py:186-200).  With
+    inplace=True x is overwritten by the round trip (1x32 blocks, power-of-two
+    scales, values rounded to e2m1 and scaled back to bf16); the packed FP4
+    output of inplace=False feeds only the FP4 GEMM, which is outside this
+    library."""
+    N = x.size(-1)
+    assert N % block_size == 0
+    if not inplace:
+        raise NotImplementedError("fp4_act_quant without inplace feeds fp4_gemm, outside qcau_b200")
+    if block_size != 32:
+        raise NotImplementedError("fp4_act_quant: block_size 32 is supported")
+    require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("fp4_act_quant: x must be bfloat16")
+    z = x.contiguous()
+    if z.numel() % 128:
+        raise NotImplementedError("fp4_act_quant: the element count must be a multiple of 128")
+    # 32-value blocks are contiguous runs of z, so any row width that is a
+    # multiple of 32 is processed as rows of 128
+    check(lib().qcau_rotate_fp4(z.data_ptr(), z.numel() // 128, 128, 0, 1, stream_ptr(z.device)),
+          "fp4_act_quant")
+    if z.data_ptr() != x.data_ptr():
+        x.copy_(z)
+    return x
+
+
 fp4_gemm = _outside("fp4_gemm")
 hc_split_sinkhorn = _outside("hc_split_sinkhorn")

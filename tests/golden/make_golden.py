@@ -25,6 +25,10 @@ Outputs (compressed .npz, raw bit patterns: bf16 as uint16, fp8/e8m0 as uint8):
 * indexer.npz -- the index-list producers (window / compressed lists, the
   Hadamard rotation, and Indexer.forward of a small seeded indexer) run by
   the QCAU package's model.py on kernel_fallback.
+* attention_trace.npz -- every call the reference's Attention.forward
+  (Deepseek_origin/inference/model.py) makes into its `kernel` module, with
+  arguments as passed and results, on a small seeded V4-width layer run with
+  kernel_fallback as that module.
 * gopu.npz -- the reference's output side (the wo_a einsum and wo_b through
   linear() on kernel_fallback's FP8 kernels) on seeded tensors.
 * ref_synthetic.npz -- seeded synthetic inputs run through the reference's
@@ -417,6 +421,130 @@ def indexer_fixture():
     np.savez_compressed(OUT / "indexer.npz", **out)
 
 
+_TRACE_DTYPES = {torch.bfloat16: "bf16", torch.float32: "fp32", torch.float8_e4m3fn: "e4m3",
+                 torch.float8_e8m0fnu: "e8m0", torch.int32: "int32", torch.int64: "int64"}
+
+
+class _TraceWriter:
+    """Records the calls a reference module makes into its `kernel` module:
+    every tensor argument as its base tensor's bits plus the view (size,
+    stride, offset) the call saw, the results, and for in-place calls the base
+    tensor after the call.  Identical arrays (the weights, read every step)
+    are stored once."""
+
+    def __init__(self):
+        self.arrays, self.calls, self._by_hash = {}, [], {}
+
+    def _store(self, t: torch.Tensor) -> str:
+        raw = t.detach().contiguous().view(-1)
+        if t.dtype in (torch.bfloat16,):
+            a = raw.view(torch.int16).numpy().view(np.uint16)
+        elif t.dtype in (torch.float8_e4m3fn, torch.float8_e8m0fnu):
+            a = raw.view(torch.uint8).numpy()
+        else:
+            a = raw.numpy()
+        key = (a.dtype.str, a.tobytes())
+        h = hash(key)
+        if h not in self._by_hash:
+            name = f"a{len(self.arrays)}"
+            self.arrays[name] = a.copy()
+            self._by_hash[h] = name
+        return self._by_hash[h]
+
+    def spec(self, v):
+        if isinstance(v, torch.Tensor):
+            base = v._base if v._base is not None else v
+            return {"t": self._store(base), "dtype": _TRACE_DTYPES[v.dtype],
+                    "base_size": list(base.shape), "size": list(v.shape), "stride": list(v.stride()),
+                    "offset": v.storage_offset() - base.storage_offset()}
+        if isinstance(v, torch.dtype):
+            return {"dtype_arg": _TRACE_DTYPES[v]}
+        if isinstance(v, (tuple, list)):
+            return {"seq": [self.spec(x) for x in v]}
+        return {"v": v}
+
+    def wrap(self, fn_name, fn):
+        def call(*args, **kwargs):
+            rec = {"fn": fn_name, "args": [self.spec(a) for a in args],
+                   "kwargs": {k: self.spec(v) for k, v in kwargs.items()},
+                   "default_dtype": _TRACE_DTYPES[torch.get_default_dtype()]}
+            out = fn(*args, **kwargs)
+            rec["out"] = self.spec(out)
+            if isinstance(out, torch.Tensor) and out._base is not None:  # in place on a view
+                rec["out_base_after"] = self.spec(out._base)
+            self.calls.append(rec)
+            return out
+        return call
+
+
+def attention_trace_fixture():
+    """attention_trace.npz: the calls the reference's own Attention.forward
+    (Deepseek_origin/inference/model.py:484-543, the module that does
+    `from kernel import ...`, model.py:12) makes into its kernel module, run on
+    the CPU with kernel_fallback as that module: a seeded V4-width layer
+    (4 heads of 512, rope 64, q_lora_rank 128, FP8 weights with UE8M0 scales,
+    window 16, compress ratio 4 with the Lightning indexer: 4 heads of 128,
+    index_topk 8) over a 24-token prefill of 2 sequences and 2 decode steps.
+    rotate_activation is the QCAU package's fp32 restatement (model.py:302-
+    323 there; fast_hadamard_transform is not installed).  Each call keeps its
+    arguments as the call site passed them (views included), its results, and
+    the layer outputs are kept as out/<step>."""
+    load_qcau_inference_model()  # kernel_fallback inside its package: sparse_attn imports .QCAU
+    kf = sys.modules["qcau_ref_inference.kernel_fallback"]
+    tw = _TraceWriter()
+    shim = type(sys)("kernel")
+    for n in ("act_quant", "fp8_gemm", "sparse_attn", "fp4_act_quant", "fp4_gemm",
+              "hc_split_sinkhorn"):
+        setattr(shim, n, tw.wrap(n, getattr(kf, n)))
+    sys.modules["kernel"] = shim
+    model = load_module("ref_model_v4_trace", REF / "Deepseek_origin/inference/model.py")
+    model.rotate_activation = load_qcau_inference_model().rotate_activation
+    model.scale_fmt, model.scale_dtype = "ue8m0", torch.float8_e8m0fnu
+    model.default_dtype = torch.float8_e4m3fn
+    args = model.ModelArgs(max_batch_size=2, max_seq_len=64, dim=256, n_heads=4, q_lora_rank=128,
+                           head_dim=512, rope_head_dim=64, o_groups=2, o_lora_rank=128,
+                           window_size=16, compress_ratios=(4,), index_n_heads=4,
+                           index_head_dim=128, index_topk=8, original_seq_len=0)
+    g = torch.Generator().manual_seed(23)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    out = {}
+    try:
+        attn = model.Attention(0, args)
+        with torch.no_grad():
+            for name, p in attn.named_parameters():
+                if p.dtype == torch.float8_e4m3fn:
+                    n_out, n_in = p.shape
+                    w = torch.randn(n_out, n_in, generator=g) / n_in ** 0.5
+                    blk = w.view(n_out // 128, 128, n_in // 128, 128)
+                    sc = torch.exp2(torch.ceil(torch.log2(
+                        blk.abs().amax(dim=(1, 3)).clamp_min(1e-4) / 448.0)))
+                    p.copy_((blk / sc[:, None, :, None]).clamp(-448, 448).view(n_out, n_in)
+                            .to(torch.float8_e4m3fn))
+                    p.scale.copy_(sc.to(torch.float8_e8m0fnu))
+                elif name.endswith("scale"):
+                    continue
+                elif name.endswith("norm.weight"):
+                    p.copy_(1.0 + 0.1 * torch.randn(p.shape, generator=g))
+                elif name.endswith("ape") or name.endswith("attn_sink"):
+                    p.copy_(0.5 * torch.randn(p.shape, generator=g))
+                else:
+                    p.copy_((torch.randn(p.shape, generator=g) / p.shape[-1] ** 0.5).to(p.dtype))
+            steps = [(0, 24), (24, 1), (25, 1)]
+            for i, (sp, sl) in enumerate(steps):
+                x = torch.randn(2, sl, 256, generator=g).to(torch.bfloat16)
+                first = len(tw.calls)
+                y = attn(x, sp)
+                for c in tw.calls[first:]:
+                    c["step"] = i
+                out[f"out/{i}"] = u16(y)
+    finally:
+        torch.set_default_dtype(prev)
+    out.update(tw.arrays)
+    out["calls"] = np.array(json.dumps(tw.calls))
+    np.savez_compressed(OUT / "attention_trace.npz", **out)
+
+
 if __name__ == "__main__":
     if not VEC.exists():
         sys.exit(f"reference test vectors not found under {REF} (set QCAU_REFERENCE_ROOT)")
@@ -425,5 +553,6 @@ if __name__ == "__main__":
     kv_build_fixture()
     gopu_fixture()
     indexer_fixture()
+    attention_trace_fixture()
     for f in sorted(OUT.glob("*.npz")):
         print(f.name, f.stat().st_size)
