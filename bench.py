@@ -328,6 +328,42 @@ def sparse_fp8_only(local: int, heads: int):
                       "us": ms * 1e3, "GB/s": nbytes / ms / 1e6, "algorithmic_bytes": nbytes}))
 
 
+def stage_times(layer, q_lora, cache, table, seqlens, positions, freqs, y, dev, ws, steps):
+    """Per-stage device time (us, mean over `steps` steps, max over ranks) of
+    the row-split decode step: CUDA events recorded between its stages on the
+    compute stream.  NCCL collectives run on that stream too, so a collective's
+    time includes waiting for the slowest rank to reach it."""
+    layer.stage_events = []
+    split = layer.attn_split
+    layer.attn_split = "rows"
+    try:
+        for _ in range(2):
+            layer.forward_rows(q_lora, cache, table, seqlens, positions, freqs, CTX, y)
+        torch.cuda.synchronize(dev)
+        if ws > 1:
+            dist.barrier()
+        layer.stage_events = []
+        for _ in range(steps):
+            layer.forward_rows(q_lora, cache, table, seqlens, positions, freqs, CTX, y)
+        torch.cuda.synchronize(dev)
+        evs = layer.stage_events
+    finally:
+        layer.stage_events = None
+        layer.attn_split = split
+    names, acc = [], {}
+    for (n0, e0), (n1, e1) in zip(evs, evs[1:]):
+        if n1 == "start":
+            continue
+        if n1 not in acc:
+            names.append(n1)
+            acc[n1] = 0.0
+        acc[n1] += e0.elapsed_time(e1) * 1000.0 / steps
+    t = torch.tensor([acc[n] for n in names], device=dev, dtype=torch.float64)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return {n: round(float(v), 2) for n, v in zip(names, t.tolist())}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -350,6 +386,10 @@ def main():
     ap.add_argument("--exchange", default="nccl", choices=["nccl", "p2p"],
                     help="context split: partial states exchanged by an NCCL all-to-all, or "
                          "stored by the attention kernel into the owning rank's memory")
+    ap.add_argument("--stages", action="store_true",
+                    help="after the timed steps, time the row-split step's stages (q-up, "
+                         "all-to-alls, attention, out-projection, all-reduce) with CUDA "
+                         "events, max over ranks, and add them to the line as stages_us")
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--ctx", type=int, default=4096)
     args = ap.parse_args()
@@ -427,6 +467,9 @@ def main():
     ms_total = float(t.item())
     ms_step = ms_total / args.steps
     value = BATCH * args.steps / (ms_total / 1000.0)
+
+    stages = stage_times(layer, q_lora, cache, table, seqlens, positions, freqs, y, dev, ws,
+                         args.steps) if args.stages else None
 
     # ---- dominant kernel alone: the decode attention, timed on its stream
     L = _lib.lib()
@@ -608,6 +651,8 @@ def main():
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
+        if stages is not None:
+            line["stages_us"] = stages
         if ws == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
             v, sample = cpu_reference(3, 1, threads)

@@ -133,9 +133,6 @@ __device__ __forceinline__ void st_shared16(uint32_t dst, uint4 v) {
 __device__ __forceinline__ void st_shared_u16(uint32_t dst, uint16_t v) {
   asm volatile("st.shared.b16 [%0], %1;" ::"r"(dst), "h"(v) : "memory");
 }
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 // 32 bytes (32-byte aligned) by one 256-bit load
 __device__ __forceinline__ void ldg_nc32(const void* p, uint4& lo, uint4& hi) {
   asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"

@@ -161,6 +161,15 @@ __device__ __forceinline__ void st_shared_cluster_u32(uint32_t addr, uint32_t v)
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ float4 ld_shared_cluster_v4f32(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
@@ -180,6 +189,35 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, uint64_t
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// Bulk tensor store of a shared-memory tile (its layout per the map's
+// swizzle) to global memory; completion is tracked per thread by bulk groups.
+__device__ __forceinline__ void tma_store_2d(const void* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(map), "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until the committed bulk stores of this thread have completed (their
+// shared-memory sources read and their global writes performed).
+__device__ __forceinline__ void bulk_wait_group0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Generic-proxy shared-memory writes made visible to the async proxy (TMA
+// stores, MMA operand reads) that follow.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Barrier among `count` threads (a multiple of 32) of the CTA on barrier `id`.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const void* map, uint64_t* bar, int x,

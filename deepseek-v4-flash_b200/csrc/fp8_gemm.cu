@@ -11,11 +11,16 @@
 // CTA = 128 x 128 output tile, 320 threads:
 //   warp 0     TMA producer (A and B tiles, 128-byte swizzle, kStages ring)
 //   warp 1     TMEM allocator + single-thread MMA issuer
-//   warps 2-9  epilogue: TMEM -> registers, scale promotion, bf16/fp32 store;
-//              two warps per TMEM lane quarter, 64 columns each, so that one
-//              64-column load and one wait per K-block feed 32 packed FMAs
+//   warps 2-9  epilogue: TMEM -> registers, scale promotion; two warps per
+//              TMEM lane quarter, 64 columns each, so that one 64-column load
+//              and one wait per K-block feed 32 packed FMAs
 // Four TMEM accumulators (4 x 128 columns) let the MMA run up to three
-// K-blocks ahead of the promotion.
+// K-blocks ahead of the promotion.  The finished tile goes through shared
+// memory in the 128-byte swizzled layout (a warp's 16-byte row chunks land in
+// distinct banks) and leaves by TMA bulk stores; rows past m are clipped by
+// the store.  Split-K partial tiles are parked in padded rows (528 bytes
+// apart, conflict-free) and summed over distributed shared memory by 16-byte
+// loads, all issued before the first add.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -31,6 +36,8 @@ constexpr int kEpiWarps = 8;         // two per TMEM lane quarter, 64 columns ea
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kTmemCols = kAcc * BN;
 constexpr int64_t kNumSmsGemm = 148;
+constexpr int kRedStride = BN + 4;   // floats per row of a parked split-K partial tile
+constexpr int kOutTile = 128 * 128;  // bytes of one 128-row x 128-byte output box in smem
 
 struct GemmShared {
   uint64_t full[kStages];
@@ -45,9 +52,9 @@ constexpr size_t kSmemBytes = 1024 + (size_t)kStages * kStageBytes + sizeof(Gemm
 
 __global__ void __launch_bounds__(kThreads, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                    const void* __restrict__ sa, const void* __restrict__ sb, void* __restrict__ c,
-                    int64_t m, int64_t n, int64_t k, int a_e8m0, int b_e8m0, int out_f32,
-                    int splits, int* err) {
+                    const __grid_constant__ CUtensorMap tm_c, const void* __restrict__ sa,
+                    const void* __restrict__ sb, int64_t m, int64_t k, int a_e8m0, int b_e8m0,
+                    int out_f32, int splits, int* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
   uint8_t* tiles = smem_raw + pad;
@@ -82,6 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
+    tma_prefetch_desc(&tm_c);
   }
   if (warp == 1) tmem_alloc<1>(&sh->tmem_base, kTmemCols);
   tc_fence_before();
@@ -193,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (splits > 1) {
     // the other CTAs of the cluster park their fp32 partial tile in their
     // (now idle) stage buffers; CTA 0 adds them in cluster-rank order
-    float* red = reinterpret_cast<float*>(tiles) + row_local * BN + 64 * half;
+    float* red = reinterpret_cast<float*>(tiles) + row_local * kRedStride + 64 * half;
     if (warp >= 2 && epi_ok && z > 0) {
 #pragma unroll
       for (int i = 0; i < 16; i++) {
@@ -207,28 +215,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp >= 2 && epi_ok && z == 0) {
       for (int zz = 1; zz < splits; zz++) {
         const uint32_t src = mapa_shared(smem_u32(red), (uint32_t)zz);
+        float4 r[16];
 #pragma unroll
-        for (int i = 0; i < 32; i++) {
-          const float a0 = ld_shared_cluster_f32(src + 8 * i);
-          const float a1 = ld_shared_cluster_f32(src + 8 * i + 4);
-          acc[i] = f2_add(acc[i], f2_pack(a0, a1));
+        for (int i = 0; i < 16; i++) r[i] = ld_shared_cluster_v4f32(src + 16 * i);
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          acc[2 * i] = f2_add(acc[2 * i], f2_pack(r[i].x, r[i].y));
+          acc[2 * i + 1] = f2_add(acc[2 * i + 1], f2_pack(r[i].z, r[i].w));
         }
       }
     }
     cluster_sync();
   }
-  if (warp >= 2 && epi_ok && z == 0 && row < m) {
+  if (warp >= 2 && z == 0) {
+    // the tile into swizzled 128-row x 128-byte boxes: bf16 -> box `half`
+    // (64 columns), fp32 -> boxes 2 * half, 2 * half + 1 (32 columns each);
+    // 16-byte chunk j of row r sits at r * 128 + ((j ^ (r & 7)) * 16)
     float out[64];
 #pragma unroll
     for (int i = 0; i < 32; i++) f2_unpack(acc[i], out[2 * i], out[2 * i + 1]);
-    const int64_t col0 = n0 + 64 * half;
+    const int sw = row_local & 7;
     if (out_f32) {
-      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(c) + row * n + col0);
 #pragma unroll
-      for (int j = 0; j < 16; j++)
-        dst[j] = make_float4(out[4 * j], out[4 * j + 1], out[4 * j + 2], out[4 * j + 3]);
+      for (int q = 0; q < 2; q++) {
+        uint8_t* box = tiles + (size_t)(2 * half + q) * kOutTile + row_local * 128;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const float* v = out + 32 * q + 4 * j;
+          *reinterpret_cast<float4*>(box + ((j ^ sw) << 4)) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+      }
     } else {
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(c) + row * n + col0);
+      uint8_t* box = tiles + (size_t)half * kOutTile + row_local * 128;
 #pragma unroll
       for (int j = 0; j < 8; j++) {
         uint4 pk;
@@ -240,8 +258,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk.y = *reinterpret_cast<uint32_t*>(&h1);
         pk.z = *reinterpret_cast<uint32_t*>(&h2);
         pk.w = *reinterpret_cast<uint32_t*>(&h3);
-        dst[j] = pk;
+        *reinterpret_cast<uint4*>(box + ((j ^ sw) << 4)) = pk;
       }
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(1, 32 * kEpiWarps);
+    if (warp == 2 && lane == 0 && !*abort) {
+      if (out_f32) {
+        for (int t = 0; t < 4; t++) tma_store_2d(&tm_c, tiles + (size_t)t * kOutTile, (int)n0 + 32 * t, (int)m0);
+      } else {
+        for (int t = 0; t < 2; t++) tma_store_2d(&tm_c, tiles + (size_t)t * kOutTile, (int)n0 + 64 * t, (int)m0);
+      }
+      bulk_commit_group();
+      bulk_wait_group0();
     }
   }
   if (threadIdx.x == 0 && *abort) raise_dev_error(err, QCAU_DEVERR_TIMEOUT);
@@ -253,15 +282,22 @@ cudaError_t launch_fp8_gemm(const void* a, const void* a_s, const void* b, const
                             void* c, int64_t m, int64_t n, int64_t k, int a_e8m0, int b_e8m0,
                             int out_f32, cudaStream_t st) {
   if (m == 0) return cudaSuccess;
-  CUtensorMap ta, tb;
+  if (n % BN || k % BK) return cudaErrorInvalidValue;
+  CUtensorMap ta, tb, tc;
   const uint64_t da[2] = {(uint64_t)k, (uint64_t)m};
   const uint64_t db[2] = {(uint64_t)k, (uint64_t)n};
   const uint64_t sa_[1] = {(uint64_t)k};
   const uint32_t box[2] = {BK, BM};
+  // C as [m][n] of 2- or 4-byte values, stored in 128-byte-wide boxes
+  const uint64_t dc[2] = {(uint64_t)n, (uint64_t)m};
+  const uint64_t sc_[1] = {(uint64_t)n * (out_f32 ? 4 : 2)};
+  const uint32_t cbox[2] = {out_f32 ? 32u : 64u, (uint32_t)BM};
   if (!make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a, da, sa_, box,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, b, db, sa_, box,
-                 CU_TENSOR_MAP_SWIZZLE_128B))
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap(&tc, out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                 c, dc, sc_, cbox, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBytes);
@@ -286,7 +322,7 @@ cudaError_t launch_fp8_gemm(const void* a, const void* a_s, const void* b, const
   attr[0].val.clusterDim.z = (unsigned)splits;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, fp8_gemm_kernel, ta, tb, a_s, b_s, c, m, n, k, a_e8m0, b_e8m0,
+  return cudaLaunchKernelEx(&cfg, fp8_gemm_kernel, ta, tb, tc, a_s, b_s, m, k, a_e8m0, b_e8m0,
                             out_f32, splits, device_error_word());
 }
 

@@ -135,6 +135,9 @@ class MLADecodeLayer:
         self._cp = None
         self._rows = None
         self._peer = None
+        # (stage name, CUDA event) marks of the split steps, recorded on the
+        # compute stream when a caller sets this to a list (stage timing)
+        self.stage_events = None
         self.cfg = cfg
         self.device = torch.device(device)
         self.rank, self.world_size = rank, world_size
@@ -257,6 +260,12 @@ class MLADecodeLayer:
             dist.all_reduce(y, group=self.group)
         return y
 
+    def _mark(self, name: str) -> None:
+        if self.stage_events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(torch.cuda.current_stream(self.device))
+            self.stage_events.append((name, ev))
+
     def _rows_buffers(self, B: int, max_seqlen: int):
         """Stage buffers of the row-split step, kept across steps."""
         N, Hl, c, dev = self.world_size, self.n_local, self.cfg, self.device
@@ -293,21 +302,28 @@ class MLADecodeLayer:
         if y is None:
             y = torch.empty(B, self.cfg.dim, device=self.device, dtype=torch.bfloat16)
         d = self.dims(B, block_table.size(1), cache.size(0), max_seqlen, freqs.size(0))
+        self._mark("start")
         self._q_stage(d, q_lora, positions, freqs, buf["q_local"])
+        self._mark("q_up_rope_absorb")
         q_rows = buf["q_local"].view(N, Br, *buf["q_local"].shape[1:])
         if N > 1:   # block j of rank i: rows of rank j, heads of rank i
             dist.all_to_all_single(buf["q_rows"], q_rows, group=self.group)
             q_rows = buf["q_rows"]
+            self._mark("q_all_to_all")
         rows = slice(r * Br, (r + 1) * Br)
         self._rows_attn_stage(q_rows, cache, block_table[rows], seqlens[rows], max_seqlen,
                               buf["o_rows"], buf["ws"])
+        self._mark("attention")
         o_lat = buf["o_rows"].view(B, *buf["o_lat"].shape[1:])
         if N > 1:   # block j of rank i: heads of rank j, rows of rank i
             dist.all_to_all_single(buf["o_lat"], buf["o_rows"], group=self.group)
             o_lat = buf["o_lat"]
+            self._mark("o_all_to_all")
         self._out_stage(d, o_lat, y)
+        self._mark("v_up_o_proj")
         if N > 1:
             dist.all_reduce(y, group=self.group)
+            self._mark("y_all_reduce")
         return y
 
     def _rows_attn_stage(self, q_rows, cache, table_rows, seqlens_rows, max_seqlen, o_rows, ws):
