@@ -870,6 +870,25 @@ int64_t qcau_index_lists_width(int64_t seqlen, int64_t start_pos, int64_t window
   return win_w + (start_pos > 0 ? (start_pos + 1) / ratio : seqlen / ratio);
 }
 
+int qcau_compress(const float* kv, const float* score, const float* ape, float* kv_state,
+                  float* score_state, void* out, int64_t bsz, int64_t seqlen, int64_t d,
+                  int64_t ratio, int32_t overlap, int64_t start_pos, void* stream) {
+  QCAU_CHECK_ARG(bsz >= 0 && seqlen >= 0 && d > 0 && ratio > 0 && start_pos >= 0,
+                 "compress: bad shape");
+  QCAU_CHECK_ARG((overlap ? 2 : 1) * ratio <= 256, "compress: windows up to 256 entries");
+  QCAU_CHECK_ARG(start_pos == 0 || seqlen == 1, "compress: decode steps have one token");
+  QCAU_CHECK_ARG(bsz * seqlen == 0 || (kv && score && ape), "compress: NULL input");
+  QCAU_CHECK_ARG(start_pos == 0 || (kv_state && score_state && out),
+                 "compress: decode needs the state and an output row");
+  QCAU_CHECK_ARG(start_pos > 0 || seqlen < ratio || out, "compress: output is NULL");
+  QCAU_CHECK_ARG((kv_state == nullptr) == (score_state == nullptr),
+                 "compress: kv_state and score_state go together");
+  if (bsz * seqlen == 0) return QCAU_OK;
+  QCAU_CHECK_CUDA(launch_compress(kv, score, ape, kv_state, score_state, out, bsz, seqlen, (int)d,
+                                  (int)ratio, overlap ? 1 : 0, start_pos, to_stream(stream)));
+  return QCAU_OK;
+}
+
 int qcau_kv_build(const void* kv_in, void* kv_out, int64_t rows, int64_t d,
                   const float* norm_weight, int64_t norm_dim, float eps, const float* freqs,
                   const int32_t* positions, int64_t npos, int64_t rope_dim, int64_t quant_dims,

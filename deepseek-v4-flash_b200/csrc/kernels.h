@@ -91,6 +91,12 @@ cudaError_t launch_index_score(const void* raw, const void* w, float* score, int
                                int64_t t_len, int64_t t_pad, cudaStream_t st);
 cudaError_t launch_topk(const float* score, int64_t rows, int64_t t_len, int k, int32_t* out,
                         int64_t offset, int64_t s_len, int mask_ratio, cudaStream_t st);
+// KV compressor gated pooling (compress.cu): prefill rows of the complete
+// groups plus the state left behind, or one decode token into the state and,
+// at a group boundary, its pooled row.
+cudaError_t launch_compress(const float* kv, const float* score, const float* ape, float* kv_state,
+                            float* score_state, void* out, int64_t bsz, int64_t seqlen, int d,
+                            int ratio, int overlap, int64_t start_pos, cudaStream_t st);
 cudaError_t launch_index_lists(int32_t* out, int64_t bsz, int64_t seqlen, int64_t start_pos,
                                int window, int ratio, int64_t offset, int win_w, int comp_w,
                                const int32_t* sel, cudaStream_t st);

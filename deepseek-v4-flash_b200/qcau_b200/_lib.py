@@ -104,6 +104,7 @@ SIGNATURES = {
                    _P], ctypes.c_int),
     "qcau_kv_build": ([_P, _P, _I64, _I64, _P, _I64, _F, _P, _P, _I64, _I64, _I64, _I32, _P, _P,
                        _I64, _P], ctypes.c_int),
+    "qcau_compress": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I64, _P], ctypes.c_int),
     "qcau_rotate_fp4": ([_P, _I64, _I64, _I32, _I32, _P], ctypes.c_int),
     "qcau_indexer_topk_workspace_size": ([_I64, _I64, _I64, _I64], _SZ),
     "qcau_indexer_topk": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,

@@ -186,3 +186,96 @@ class PagedKVCache:
                 row[:len(self._pages[s])] = torch.tensor(self._pages[s], dtype=torch.int32)
             self.block_table[s].copy_(row)
             self.seqlens[s] = self._len[s]
+
+
+class Compressor:
+    """The KV compressor (QCAU/QCAU_inference/inference/model.py:376-476,
+    Compressor.forward) after its two fp32 projections: gated pooling of
+    every `compress_ratio` tokens (qcau_compress), then the compressor's
+    RMSNorm, RoPE at the group's first position and, for the attention's
+    compressor, the FP8 round trip of the non-rope values (qcau_kv_build), or
+    for the indexer's (rotate=True) the Hadamard rotation and FP4 round trip
+    (qcau_rotate_fp4); the rows are written to the cache.
+
+    head_dim / rope_dim / compress_ratio are the layer's (512 or 128, 64, 4 or
+    128); the ratio-4 compressor overlaps its windows (model.py:387).  The
+    cache is the caller's [max_batch, rows, head_dim] bf16 tensor; compressed
+    row i of sequence b goes to cache[b, cache_offset + i] (the attention's
+    compressed rows follow its window ring: cache_offset = window_size,
+    model.py:599-600).  freqs_cis [max_seq, rope_dim / 2] complex64.
+    """
+
+    def __init__(self, head_dim: int, compress_ratio: int = 4, rope_dim: int = 64,
+                 rotate: bool = False, max_batch: int = 4, norm_eps: float = 1e-6,
+                 scale_fmt: Optional[str] = "ue8m0", device="cuda"):
+        self.d, self.ratio, self.rd, self.rotate = head_dim, compress_ratio, rope_dim, rotate
+        self.overlap = compress_ratio == 4
+        coff = 2 if self.overlap else 1
+        self.eps, self.scale_fmt = norm_eps, scale_fmt
+        self.device = torch.device(device)
+        dev = self.device
+        self.ape = torch.zeros(compress_ratio, coff * head_dim, device=dev)
+        self.norm_weight = torch.ones(head_dim, device=dev)
+        self.kv_state = torch.zeros(max_batch, coff * compress_ratio, coff * head_dim, device=dev)
+        self.score_state = torch.full_like(self.kv_state, float("-inf"))
+        self.kv_cache: Optional[torch.Tensor] = None
+        self.cache_offset = 0
+        self.freqs_cis: Optional[torch.Tensor] = None
+
+    def forward(self, kv: torch.Tensor, score: torch.Tensor, start_pos: int) -> Optional[torch.Tensor]:
+        """kv, score [b, s, cw] fp32 (wkv / wgate of x.float(); cw = 2 * head_dim
+        with overlap): the compressed rows [b, n, head_dim] bf16 written to the
+        cache (n = s // ratio at prefill, 1 at a decode step that closes a
+        group), or None when a decode step closes none."""
+        require_cuda(kv, score)
+        b, s, cw = kv.shape
+        if kv.dtype != torch.float32 or score.dtype != torch.float32 or score.shape != kv.shape:
+            raise ValueError("kv and score must be fp32 of the same shape")
+        if cw != (2 if self.overlap else 1) * self.d:
+            raise ValueError("projection width must be 2 * head_dim with overlap, else head_dim")
+        if b > self.kv_state.size(0):
+            raise ValueError("batch above max_batch")
+        if self.kv_cache is None or self.freqs_cis is None:
+            raise ValueError("assign kv_cache and freqs_cis first")
+        if not self.kv_cache.is_contiguous() or self.kv_cache.dtype != torch.bfloat16:
+            raise ValueError("kv_cache must be a contiguous bf16 [batch, rows, head_dim] tensor")
+        ratio, d = self.ratio, self.d
+        kv, score = kv.contiguous(), score.contiguous()
+        if start_pos == 0:
+            n = s // ratio
+            positions = torch.arange(n, device=kv.device, dtype=torch.int32) * ratio
+            first = 0
+        else:
+            if s != 1:
+                raise ValueError("decode steps have one token")
+            n = 1 if (start_pos + 1) % ratio == 0 else 0
+            positions = torch.full((1,), start_pos + 1 - ratio, device=kv.device, dtype=torch.int32)
+            first = start_pos // ratio
+        pooled = torch.empty(b, max(n, 1), d, device=kv.device, dtype=torch.bfloat16)
+        # the state of the first b sequences (the reference's state[:bsz]) is
+        # contiguous because the state rows of a sequence are
+        ks, ss = self.kv_state[:b], self.score_state[:b]
+        check(lib().qcau_compress(kv.data_ptr(), score.data_ptr(), self.ape.data_ptr(),
+                                  ks.data_ptr(), ss.data_ptr(), pooled.data_ptr(), b, s, d, ratio,
+                                  int(self.overlap), start_pos, stream_ptr(kv.device)), "compress")
+        if n == 0:
+            return None
+        pooled = pooled[:, :n]
+        rows_per_seq = self.kv_cache.size(1)
+        slots = (torch.arange(b, device=kv.device, dtype=torch.int32).unsqueeze(1) * rows_per_seq
+                 + self.cache_offset + first
+                 + torch.arange(n, device=kv.device, dtype=torch.int32).unsqueeze(0)).reshape(-1)
+        pos = positions.repeat(b)
+        if not self.rotate:
+            out = kv_build(pooled.reshape(-1, d), self.norm_weight, self.freqs_cis, pos,
+                           rope_dim=self.rd, norm_dim=d, quant_dims=d - self.rd,
+                           scale_fmt=self.scale_fmt, eps=self.eps, cache=self.kv_cache, slots=slots)
+            return out.view(b, n, d)
+        from .indexer import rotate_fp4_
+        out = kv_build(pooled.reshape(-1, d), self.norm_weight, self.freqs_cis, pos,
+                       rope_dim=self.rd, norm_dim=d, quant_dims=0, eps=self.eps)
+        rotate_fp4_(out)
+        self.kv_cache.view(-1, d).index_copy_(0, slots.long(), out)
+        return out.view(b, n, d)
+
+    __call__ = forward

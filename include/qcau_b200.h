@@ -331,6 +331,30 @@ int qcau_kv_build(const void* kv_in, void* kv_out, int64_t rows, int64_t d,
                   void* stream);
 
 /* ------------------------------------------------------------------------
+ * compress -- the KV compressor's gated pooling, Compressor.forward
+ * (QCAU/QCAU_inference/inference/model.py:415-457; Deepseek_origin/inference/
+ * model.py:317-357) after its two fp32 projections:
+ *   kv, score [bsz, seqlen, cw] fp32 = wkv(x.float()), wgate(x.float()),
+ *   cw = 2d with overlap (the ratio-4 compressor), else d;
+ *   ape [ratio, cw] fp32; kv_state, score_state [bsz, slots, cw] fp32 with
+ *   slots = 2 * ratio (overlap) or ratio, the compressor's decode state.
+ * Prefill (start_pos 0): out [bsz, seqlen / ratio, d] bf16 = per channel the
+ *   softmax(score + ape)-weighted sum of each group's kv (with overlap the
+ *   window is the previous group on channels [0, d) and this group on
+ *   [d, 2d), model.py:406-413), rounded to bf16; the state (may be NULL) is
+ *   left as the reference leaves it: the last complete group (overlap) and
+ *   the remainder tokens, scores with ape added (model.py:422-429).
+ * Decode (seqlen 1, start_pos > 0): the token goes into the state; when
+ *   (start_pos + 1) % ratio == 0, out [bsz, d] bf16 is the pooled state (and
+ *   with overlap the state shifts by one group); else out is not written.
+ * The pooled rows then take the compressor's norm, RoPE and quantisation
+ * through qcau_kv_build (model.py:459-476).
+ * ---------------------------------------------------------------------- */
+int qcau_compress(const float* kv, const float* score, const float* ape, float* kv_state,
+                  float* score_state, void* out, int64_t bsz, int64_t seqlen, int64_t d,
+                  int64_t ratio, int32_t overlap, int64_t start_pos, void* stream);
+
+/* ------------------------------------------------------------------------
  * Index-list producers: what the sparse attention's topk_idxs come from.
  *
  * qcau_rotate_fp4 -- in place on rows of 128 bf16 values: the Walsh-Hadamard

@@ -29,6 +29,9 @@ Outputs (compressed .npz, raw bit patterns: bf16 as uint16, fp8/e8m0 as uint8):
   (Deepseek_origin/inference/model.py) makes into its `kernel` module, with
   arguments as passed and results, on a small seeded V4-width layer run with
   kernel_fallback as that module.
+* compressor.npz -- the reference's Compressor (gated pooling, norm, RoPE,
+  FP8 or Hadamard) over prefill and decode steps, with its projections,
+  outputs, cache and state.
 * gopu.npz -- the reference's output side (the wo_a einsum and wo_b through
   linear() on kernel_fallback's FP8 kernels) on seeded tensors.
 * ref_synthetic.npz -- seeded synthetic inputs run through the reference's
@@ -545,6 +548,73 @@ def attention_trace_fixture():
     np.savez_compressed(OUT / "attention_trace.npz", **out)
 
 
+def compressor_fixture():
+    """compressor.npz: the reference's Compressor.forward (QCAU/QCAU_inference/
+    inference/model.py:415-476) run by its own code on seeded projections:
+    c4 = the attention's compressor (ratio 4, overlapping windows, 512 wide,
+    FP8 round trip with UE8M0 scales), c8 = a non-overlapping one (ratio 8),
+    i4 = the indexer's (ratio 4, 128 wide, Hadamard rotation; kernel_fallback's
+    fp4_act_quant leaves the rotated values unchanged).  Each case is a prefill
+    and decode steps past two group boundaries; per step the projections the
+    compressor computed (kv, score: the wkv / wgate outputs), the rows it
+    returned (out, absent when it returned None) and the rows given to
+    rotate_activation (pre_rot, i4); the cache and the state after the
+    prefill and after the last step."""
+    model = load_qcau_inference_model()
+    model.scale_fmt, model.scale_dtype = "ue8m0", torch.float8_e8m0fnu
+    g = torch.Generator().manual_seed(29)
+    out = {}
+    cases = {"c4": (4, 512, False, 10, 6), "c8": (8, 512, False, 19, 5), "i4": (4, 128, True, 10, 6)}
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    real_rot = model.rotate_activation
+    rec = {}
+
+    def rot(t):
+        rec["pre_rot"] = t.clone()
+        return real_rot(t)
+
+    model.rotate_activation = rot
+    try:
+        for name, (ratio, d, rotate, s0, ndec) in cases.items():
+            args = model.ModelArgs(max_batch_size=2, max_seq_len=64, dim=128, rope_head_dim=64)
+            comp = model.Compressor(args, ratio, d, rotate)
+            with torch.no_grad():
+                comp.ape.copy_(0.5 * torch.randn(comp.ape.shape, generator=g))
+                comp.norm.weight.copy_(1.0 + 0.1 * torch.randn(d, generator=g))
+                for lin in (comp.wkv, comp.wgate):
+                    lin.weight.copy_(torch.randn(lin.weight.shape, generator=g) / 128 ** 0.5)
+            comp.kv_cache = torch.zeros(2, 64 // ratio, d, dtype=torch.bfloat16)
+            comp.freqs_cis = model.precompute_freqs_cis(64, 64, 0, 10000.0, 40, 32, 1)
+            comp.wkv.register_forward_hook(lambda m, a, o: rec.__setitem__("kv", o.clone()))
+            comp.wgate.register_forward_hook(lambda m, a, o: rec.__setitem__("score", o.clone()))
+            out[f"{name}/ape"] = comp.ape.detach().numpy().copy()
+            out[f"{name}/norm"] = comp.norm.weight.detach().numpy().copy()
+            out[f"{name}/freqs"] = torch.view_as_real(comp.freqs_cis).numpy().astype(np.float32)
+            steps = [(0, s0)] + [(s0 + i, 1) for i in range(ndec)]
+            for i, (sp, sl) in enumerate(steps):
+                x = torch.randn(2, sl, 128, generator=g).to(torch.bfloat16)
+                rec.pop("pre_rot", None)
+                with torch.no_grad():
+                    y = comp(x, sp)
+                k = f"{name}/step{i}"
+                out[f"{k}/meta"] = np.array([sp, sl], dtype=np.int64)
+                out[f"{k}/kv"] = rec["kv"].numpy().copy()
+                out[f"{k}/score"] = rec["score"].numpy().copy()
+                if y is not None:
+                    out[f"{k}/out"] = u16(y.contiguous())
+                if "pre_rot" in rec:
+                    out[f"{k}/pre_rot"] = u16(rec["pre_rot"].contiguous())
+                if i in (0, len(steps) - 1):  # after the prefill and at the end
+                    out[f"{k}/cache"] = u16(comp.kv_cache.clone())
+                    out[f"{k}/kv_state"] = comp.kv_state[:2].numpy().copy()
+                    out[f"{k}/score_state"] = comp.score_state[:2].numpy().copy()
+    finally:
+        model.rotate_activation = real_rot
+        torch.set_default_dtype(prev)
+    np.savez_compressed(OUT / "compressor.npz", **out)
+
+
 if __name__ == "__main__":
     if not VEC.exists():
         sys.exit(f"reference test vectors not found under {REF} (set QCAU_REFERENCE_ROOT)")
@@ -554,5 +624,6 @@ if __name__ == "__main__":
     gopu_fixture()
     indexer_fixture()
     attention_trace_fixture()
+    compressor_fixture()
     for f in sorted(OUT.glob("*.npz")):
         print(f.name, f.stat().st_size)
