@@ -295,15 +295,17 @@ def prefill_only(local: int):
                       "TFLOP/s": flops / ms / 1e9, "workspace_bytes": need}))
 
 
-def sparse_fp8_only(local: int, heads: int):
-    """Long-context sparse decode over an FP8 latent cache: batch 64, 131072
-    rows per sequence (e4m3 latent + fp32 row scale + bf16 rope), top-2048
-    indices, `heads` heads (16 = one rank of an 8-way head shard)."""
+def sparse_fp8_only(local: int, heads: int, rows: int = 131072):
+    """Long-context sparse decode over an FP8 latent cache: batch 64, `rows`
+    rows per sequence (131072 by default; e4m3 latent + fp32 row scale + bf16
+    rope), top-2048 indices, `heads` heads (16 = one rank of an 8-way head
+    shard).  Fewer rows gather the same bytes from a smaller cache (a
+    profiling case)."""
     from qcau_b200 import _lib
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    B, N, K = 64, 131072, 2048
+    B, N, K = 64, rows, 2048
     gen = torch.Generator(device=dev).manual_seed(2)
     codes = torch.randint(0, 0x7F, (B, N, 512), device=dev, generator=gen, dtype=torch.uint8)
     scale = torch.rand(B, N, device=dev, generator=gen) * 0.01 + 1e-3
@@ -324,8 +326,10 @@ def sparse_fp8_only(local: int, heads: int):
     ms = _time_ms(run)
     assert _lib.device_error() == 0
     nbytes = B * K * (512 + 4 + 128) + B * K * 4 + B * heads * (WIDTH + 512) * 2
+    hbm, _, peak_kind = peaks()
     print(json.dumps({"sparse_fp8_only": True, "batch": B, "rows": N, "topk": K, "heads": heads,
-                      "us": ms * 1e3, "GB/s": nbytes / ms / 1e6, "algorithmic_bytes": nbytes}))
+                      "us": ms * 1e3, "GB/s": nbytes / ms / 1e6, "algorithmic_bytes": nbytes,
+                      "frac_of_hbm": nbytes / ms / 1e6 / hbm, "peak_source": peak_kind}))
 
 
 def stage_times(layer, q_lora, cache, table, seqlens, positions, freqs, y, dev, ws, steps):
@@ -386,6 +390,8 @@ def main():
     ap.add_argument("--exchange", default="nccl", choices=["nccl", "p2p"],
                     help="context split: partial states exchanged by an NCCL all-to-all, or "
                          "stored by the attention kernel into the owning rank's memory")
+    ap.add_argument("--sparse-rows", type=int, default=131072,
+                    help="rows per sequence of the --sparse-fp8-only cache")
     ap.add_argument("--stages", action="store_true",
                     help="after the timed steps, time the row-split step's stages (q-up, "
                          "all-to-alls, attention, out-projection, all-reduce) with CUDA "
@@ -404,7 +410,7 @@ def main():
         prefill_only(local)
         return
     if args.sparse_fp8_only:
-        sparse_fp8_only(local, args.sparse_fp8_only)
+        sparse_fp8_only(local, args.sparse_fp8_only, args.sparse_rows)
         return
     if args.impl == "reference":
         run_reference_arm(args, rank)
