@@ -104,6 +104,7 @@ struct DecodeShared {
   float xsum[128];
   uint32_t tmem_base;
   int abort;
+  long long tiles[8];  // per warp: the batch's tiles (the balanced schedule's check)
 };
 
 constexpr size_t kSmemBytes = 1024 + kQBytes + kPBytes + (size_t)kKSlots * kKSlot +
@@ -136,6 +137,16 @@ struct DecodeParams {
   int o_hblock;   // direct mode: o as [h / o_hblock][rows][o_hblock][512]
   int64_t rows;
   int64_t units;  // work units; pair i of the grid runs units i, i + pairs, ...
+  // balanced schedule (stream != 0, one query token per sequence): pair i
+  // runs tiles [i G / pairs, (i + 1) G / pairs) of the G = rows x hgroups x
+  // nt tiles, row after row; a row's pieces fill its partial slots in pair
+  // order, and its last piece marks the slots after it empty.  It is taken
+  // when the sequences fill at least 90 % of the rows x nt tiles; otherwise
+  // the same launch runs `splits` equal splits of each row's own tiles,
+  // units looped over the pairs
+  int stream;
+  int64_t nt, gtiles;
+  int usplits;  // equal splits of a row in the unit enumeration (<= splits, the partial slots)
   void* blk_o[kMaxBlocks];     // fp32 O, or fp16 O / l when part_f16
   int part_f16;
   float* blk_ml[kMaxBlocks];
@@ -180,6 +191,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 struct DecodeUnit {
   int64_t b, bs;
   int split, seqlen, t_begin, T, head0;
+  int empty_from;  // partial slots [empty_from, splits) of row b are marked empty
 };
 
 __device__ __forceinline__ DecodeUnit decode_unit(const DecodeParams& p, int64_t unit,
@@ -187,10 +199,10 @@ __device__ __forceinline__ DecodeUnit decode_unit(const DecodeParams& p, int64_t
   DecodeUnit U;
   const int hg = (int)(unit % p.hgroups);
   const int64_t rest = unit / p.hgroups;
-  U.split = (int)(rest % p.splits);
+  U.split = (int)(rest % p.usplits);
   // query row r = (sequence bs, token t of qlen): token t sees the cached
   // prefix up to its own position, seqlens[bs] - (qlen - 1 - t) tokens
-  U.b = rest / p.splits;
+  U.b = rest / p.usplits;
   U.bs = U.b / p.qlen;
   U.seqlen = p.seqlens[U.bs] - (p.qlen - 1 - (int)(U.b % p.qlen));
   const int ntiles = (U.seqlen + kTile - 1) / kTile;
@@ -199,7 +211,58 @@ __device__ __forceinline__ DecodeUnit decode_unit(const DecodeParams& p, int64_t
   const int t_end = (int)((int64_t)ntiles * (gsplit + 1) / p.splits_total);
   U.T = t_end - U.t_begin;
   U.head0 = hg * 2 * p.cta_heads + (int)rank * p.cta_heads;
+  U.empty_from = p.usplits;  // the balanced schedule's fall-back leaves slots past usplits empty
   return U;
+}
+
+// Balanced schedule: the piece of (row, head group) v = g / nt that starts
+// at global tile g and ends at g_end or at the row's end.  Its partial slot
+// is its pair's rank among the pairs that cover the row; the pair covering
+// tile x is the largest q with floor(q G / P) <= x.
+__device__ __forceinline__ DecodeUnit stream_unit(const DecodeParams& p, int64_t g, int64_t g_end,
+                                                  int64_t pair, int64_t npairs, uint32_t rank) {
+  DecodeUnit U;
+  const int64_t v = g / p.nt;
+  const int hg = (int)(v % p.hgroups);
+  U.b = v / p.hgroups;
+  U.bs = U.b;
+  U.seqlen = p.seqlens[U.bs];
+  // the schedule covers max_len tokens a row: a longer sequence is cut there
+  if (U.seqlen > p.nt * kTile) raise_dev_error(p.err, QCAU_DEVERR_INDEX);
+  const int64_t row0 = v * p.nt, row1 = row0 + p.nt;
+  const int64_t first_pair = ((row0 + 1) * npairs - 1) / p.gtiles;
+  U.split = (int)(pair - first_pair);
+  U.t_begin = (int)(g - row0);
+  const int t_end = (int)((g_end < row1 ? g_end : row1) - row0);
+  const int ntiles = (U.seqlen + kTile - 1) / kTile;
+  U.T = (t_end < ntiles ? t_end : ntiles) - U.t_begin;
+  U.head0 = hg * 2 * p.cta_heads + (int)rank * p.cta_heads;
+  U.empty_from = row1 <= g_end ? U.split + 1 : p.splits;
+  return U;
+}
+
+// A pair's walk over its work: units pair, pair + npairs, ... or, in the
+// balanced schedule, the pieces of its tile range.  Every role of the pair
+// takes the same walk.
+struct UnitCursor {
+  int64_t pos, end;
+};
+
+__device__ __forceinline__ UnitCursor cursor_begin(const DecodeParams& p, bool balanced,
+                                                   int64_t pair, int64_t npairs) {
+  if (balanced) return {pair * p.gtiles / npairs, (pair + 1) * p.gtiles / npairs};
+  return {pair, p.units};
+}
+
+__device__ __forceinline__ DecodeUnit cursor_unit(const DecodeParams& p, bool balanced,
+                                                  const UnitCursor& c, int64_t pair,
+                                                  int64_t npairs, uint32_t rank) {
+  return balanced ? stream_unit(p, c.pos, c.end, pair, npairs, rank) : decode_unit(p, c.pos, rank);
+}
+
+__device__ __forceinline__ void cursor_next(const DecodeParams& p, bool balanced, UnitCursor& c,
+                                            int64_t npairs) {
+  c.pos = balanced ? (c.pos / p.nt + 1) * p.nt : c.pos + npairs;
 }
 
 // All lanes wait; the warp agrees on the outcome (timeouts are per lane).
@@ -225,10 +288,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int64_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  // partial row of (row U.b, split U.split, head) in its head block's destination
-  auto part_row = [&](const DecodeUnit& U, int head, int& blk) -> int64_t {
+  // partial row of (row b, split slot, head) in its head block's destination
+  auto part_row_at = [&](int64_t b, int slot, int head, int& blk) -> int64_t {
     blk = head / p.part_hblock;
-    return ((int64_t)U.b * p.splits + U.split) * p.part_hblock + (head - blk * p.part_hblock);
+    return ((int64_t)b * p.splits + slot) * p.part_hblock + (head - blk * p.part_hblock);
+  };
+  auto part_row = [&](const DecodeUnit& U, int head, int& blk) -> int64_t {
+    return part_row_at(U.b, U.split, head, blk);
   };
 
   // direct-mode output row of (row U.b, head)
@@ -261,11 +327,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     sh->abort = 0;
     fence_barrier_init();
   }
+  if (p.stream) {
+    // the batch's tiles at its own lengths, to check that it fills the
+    // balanced plan (every CTA counts the same, so all take one schedule)
+    long long n = 0;
+    for (int64_t r = threadIdx.x; r < p.rows; r += kThreads) {
+      const int64_t t = ((int64_t)p.seqlens[r] + kTile - 1) / kTile;
+      n += t < 0 ? 0 : (t > p.nt ? p.nt : t);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) n += __shfl_down_sync(0xffffffffu, n, o);
+    if (lane == 0) sh->tiles[warp] = n;
+  }
   if (warp == 1) tmem_alloc<2>(&sh->tmem_base, kTmemCols);
   tc_fence_before();
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
+  bool balanced = false;
+  if (p.stream) {
+    long long n = 0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; w++) n += sh->tiles[w];
+    balanced = n * 10 >= (long long)p.rows * p.nt * 9;
+  }
 
   // physical page of the unit's page pidx (units with T > 0 have seqlen >= 1)
   auto page_of = [&](const DecodeUnit& U, int pidx) -> int {
@@ -294,8 +379,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t q_full_l = mapa_shared(smem_u32(&sh->q_full), 0);
       int n = 0, nq = 0;  // ring copies issued; units whose Q was issued
       bool ok = true;
-      for (int64_t unit = pair; unit < p.units && ok; unit += npairs) {
-        const DecodeUnit U = decode_unit(p, unit, rank);
+      for (UnitCursor c = cursor_begin(p, balanced, pair, npairs); c.pos < c.end && ok;
+           cursor_next(p, balanced, c, npairs)) {
+        const DecodeUnit U = cursor_unit(p, balanced, c, pair, npairs, rank);
         if (U.T <= 0) continue;
         if (is_k) {
           // Q of the previous unit is free once its last QK has completed
@@ -352,8 +438,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (warp == 1) {
         const uint32_t idesc_qk = make_idesc(128, 128, kFmtBF16, kFmtBF16, false, false);
         int nk = 0, gt = 0, nu = 0;  // K boxes consumed, tiles, units
-        for (int64_t unit = pair; unit < p.units && ok; unit += npairs) {
-          const DecodeUnit U = decode_unit(p, unit, rank);
+        for (UnitCursor c = cursor_begin(p, balanced, pair, npairs); c.pos < c.end && ok;
+             cursor_next(p, balanced, c, npairs)) {
+          const DecodeUnit U = cursor_unit(p, balanced, c, pair, npairs, rank);
           if (U.T <= 0) continue;
           if (!(ok = mbar_wait(&sh->q_full, nu & 1, abort))) break;
           for (int it = 0; it < U.T && ok; it++, gt++) {
@@ -386,8 +473,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       } else {
         const uint32_t idesc_pv = make_idesc(128, 256, kFmtBF16, kFmtBF16, false, true);
         int nv = 0, gt = 0, nu = 0;  // V pages consumed, tiles, units
-        for (int64_t unit = pair; unit < p.units && ok; unit += npairs) {
-          const DecodeUnit U = decode_unit(p, unit, rank);
+        for (UnitCursor c = cursor_begin(p, balanced, pair, npairs); c.pos < c.end && ok;
+             cursor_next(p, balanced, c, npairs)) {
+          const DecodeUnit U = cursor_unit(p, balanced, c, pair, npairs, rank);
           if (U.T <= 0) continue;
           // the first PV of a unit overwrites O: the previous epilogue has read it
           if (nu > 0 && !(ok = mbar_wait<true>(&sh->o_free, (nu - 1) & 1, abort))) break;
@@ -438,10 +526,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                   mapa_shared(smem_u32(&sh->s_free[1]), 0)};
     const uint32_t p_full_l = mapa_shared(smem_u32(&sh->p_full), 0);
     const uint32_t o_free_l = mapa_shared(smem_u32(&sh->o_free), 0);
+    // the last piece of a row (balanced schedule) marks the row's slots after
+    // its own empty: weight zero in the combine
+    auto mark_empty = [&](const DecodeUnit& U) {
+      for (int slot = U.empty_from; slot < p.splits; slot++)
+        for (int i = et; i < p.cta_heads; i += 128) {
+          int blk;
+          const int64_t prow = part_row_at(U.b, slot, U.head0 + i, blk);
+          p.blk_ml[blk][prow * 2] = -INFINITY;
+          p.blk_ml[blk][prow * 2 + 1] = 0.f;
+        }
+    };
     int gt = 0, nu = 0;  // tiles, units with tiles
     bool ok = true;
-    for (int64_t unit = pair; unit < p.units && ok; unit += npairs) {
-      const DecodeUnit U = decode_unit(p, unit, rank);
+    for (UnitCursor c = cursor_begin(p, balanced, pair, npairs); c.pos < c.end && ok;
+         cursor_next(p, balanced, c, npairs)) {
+      const DecodeUnit U = cursor_unit(p, balanced, c, pair, npairs, rank);
       if (U.T <= 0) {
         if (p.direct) {  // no visible token: the output rows are zero
           for (int i = et; i < p.cta_heads * 64; i += 128)
@@ -454,6 +554,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             p.blk_ml[blk][prow * 2] = -INFINITY;
             p.blk_ml[blk][prow * 2 + 1] = 0.f;
           }
+          mark_empty(U);
         }
         continue;
       }
@@ -626,6 +727,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           p.blk_ml[blk][prow * 2] = m_run;
           p.blk_ml[blk][prow * 2 + 1] = l_tot;
         }
+        mark_empty(U);
       }
       // O is read: the next unit's first PV may overwrite it
       tc_fence_before();
@@ -707,6 +809,11 @@ bool decode_attn_sm100_supported(const AttnArgs& a) {
 
 cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   if (!decode_attn_sm100_supported(a)) return cudaErrorNotSupported;
+  // the balanced schedule: one query token per row, no fixed split range
+  if (a.stream && (a.s != 1 || a.splits_total > 0 || a.peer || a.stream_nt < 1 ||
+                   a.stream_usplits > a.splits ||
+                   a.stream_pairs < 1 || (a.splits > 1 && a.part_o == nullptr)))
+    return cudaErrorInvalidValue;
   if (a.b == 0) return cudaSuccess;
   // K and V are read through a 4-D view of the cache [pages][64 tokens][9
   // chunks][64 values], so that one box carries several chunks of a page: the
@@ -753,7 +860,9 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
   p.q_hblock = (int)qhb;
   p.q_box = q_box;
   p.split_base = a.splits_total > 0 ? a.split_base : 0;
-  p.splits_total = a.splits_total > 0 ? a.splits_total : a.splits;
+  const int usplits = a.stream && a.stream_usplits > 0 ? a.stream_usplits : (int)a.splits;
+  p.usplits = usplits;
+  p.splits_total = a.splits_total > 0 ? a.splits_total : usplits;
   p.part_hblock = a.part_hblock > 0 ? (int)a.part_hblock : (int)a.h;
   p.nblk = (int)(a.h / p.part_hblock);
   for (int j = 0; j < kMaxBlocks; j++) {
@@ -791,12 +900,17 @@ cudaError_t launch_decode_attn_sm100(const AttnArgs& a, cudaStream_t st) {
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSmemBytes);
   if (e != cudaSuccess) return e;
-  const int64_t units = a.b * a.s * a.splits * p.hgroups;
+  const int64_t units = a.b * a.s * usplits * p.hgroups;
   p.units = units;
   // one pair per unit; when the units outnumber the pairs that fit at once,
-  // one pair per slot, each looping over units (no pair waits for another)
+  // one pair per slot, each looping over units (no pair waits for another).
+  // The balanced schedule has its own pair count (its ranges depend on it).
   const int64_t slots = resident_pairs();
-  const int64_t pairs = (slots > 0 && units > slots) ? slots : units;
+  int64_t pairs = (slots > 0 && units > slots) ? slots : units;
+  p.stream = a.stream ? 1 : 0;
+  p.nt = a.stream_nt;
+  p.gtiles = a.stream ? rows * p.hgroups * a.stream_nt : 0;
+  if (a.stream) pairs = a.stream_pairs;
   decode_attn_sm100_kernel<<<(unsigned)(2 * pairs), kThreads, kSmemBytes, st>>>(tq, tk, tv, p);
   return cudaGetLastError();
 }

@@ -191,6 +191,47 @@ cudaError_t run_gather(const AttnArgs& a, cudaStream_t st) {
   return launch_attn_gather_sm100(a, st);
 }
 
+// Balanced decode schedule of the pair kernel (one query token per
+// sequence): the tiles of every (row, 128-head group) at max_len, row after
+// row, are cut into one equal range per CTA pair (74 on B200; small batches
+// keep the split count, see below).  A pair runs its range as pieces cut at row
+// ends, so no pair idles and none runs more than a few pieces; a row cut
+// into several pieces gets one partial slot per piece.  `splits` is the most
+// pieces of any row (the owner of tile x is the largest q with
+// floor(q G / P) <= x, as in the kernel).
+struct StreamPlan {
+  int64_t nt = 0, pairs = 0;
+  int splits = 0;  // 0: not applicable
+};
+
+StreamPlan sm100_stream_plan(int64_t rows, int64_t h, int64_t max_len) {
+  StreamPlan sp;
+  const int64_t hgroups = h >= 128 ? h / 128 : 1;
+  const int64_t nt = (max_len + 127) / 128;
+  const int64_t v = rows * hgroups;
+  if (v <= 0 || nt <= 0) return sp;
+  const int64_t g = v * nt;
+  int64_t pairs = kNumSms / 2;
+  if (pairs > g / 4) pairs = g / 4;
+  if (pairs < 1) pairs = 1;
+  // the plan's set-up and merge have to pay for themselves: under 32 tiles
+  // a pair they do not (32 x 4096 at 128 heads: 63.5 against 60.1 us), nor
+  // under 64 where the split count would run unsplit, with no merge at all
+  // (128 x 4096: 179 against 173 us; 64 x 32768, 221 tiles a pair: 0.697
+  // against 0.764 ms; 16 x 32768, split anyway: 164 against 171 us)
+  if (g < 32 * pairs || (sm100_splits(rows, h, max_len) <= 1 && g < 64 * pairs)) return sp;
+  int64_t most = 1;
+  for (int64_t i = 0; i < v; i++) {
+    const int64_t first = ((i * nt + 1) * pairs - 1) / g;
+    const int64_t last = ((i + 1) * nt * pairs - 1) / g;
+    if (last - first + 1 > most) most = last - first + 1;
+  }
+  sp.nt = nt;
+  sp.pairs = pairs;
+  sp.splits = (int)most;
+  return sp;
+}
+
 size_t attn_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int splits) {
   if (splits <= 1) return 0;
   return align256((size_t)rows * splits * h * d_v * 4) + align256((size_t)rows * splits * h * 2 * 4);
@@ -200,9 +241,14 @@ size_t attn_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int splits) {
 // the two-CTA kernel takes (with 576-wide keys and 64-token pages) are sized
 // for its split count; the gather kernel, which runs the other shapes, caps
 // its split count to the same size.
-size_t decode_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int64_t max_len) {
+size_t decode_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int64_t max_len, int64_t qlen) {
   const bool pair_heads = d_v == 512 && (h % 128 == 0 || h == 64 || h == 32 || h == 16);
-  if (pair_heads) return attn_ws_bytes(rows, h, d_v, sm100_splits(rows, h, max_len));
+  if (pair_heads) {
+    // decode rows (qlen 1) may take the balanced schedule's slots
+    const StreamPlan sp = qlen == 1 ? sm100_stream_plan(rows, h, max_len) : StreamPlan{};
+    const int rule = sm100_splits(rows, h, max_len);
+    return attn_ws_bytes(rows, h, d_v, sp.splits > rule ? sp.splits : rule);
+  }
   return attn_ws_bytes(rows, h, d_v,
                        std::max(gather_splits(rows, h, 576, max_len),
                                 gather_splits(rows, h, 512, max_len)));
@@ -215,11 +261,25 @@ size_t decode_ws_bytes(int64_t rows, int64_t h, int64_t d_v, int64_t max_len) {
 int run_decode_attn(AttnArgs a, void* ws, cudaStream_t st) {
   const bool sm100 = decode_attn_sm100_supported(a);
   const int64_t rows = a.b * a.s;
-  if (sm100) {
+  // decode rows of the pair kernel take the balanced schedule when their
+  // lengths fill it (the kernel checks), else the split count; the partial
+  // slots cover both.  Prefill rows and fixed split ranges take the split
+  // count; the gather kernel its own count, within the same workspace.
+  StreamPlan sp;
+  if (sm100 && a.s == 1 && a.splits_total <= 0 && !a.peer)
+    sp = sm100_stream_plan(rows, a.h, a.max_len);
+  if (sp.splits > 0) {
+    const int rule = sm100_splits(rows, a.h, a.max_len);
+    a.stream = 1;
+    a.stream_nt = sp.nt;
+    a.stream_pairs = sp.pairs;
+    a.stream_usplits = rule;  // the fall-back for batches that do not fill the plan
+    a.splits = sp.splits > rule ? sp.splits : rule;
+  } else if (sm100) {
     a.splits = sm100_splits(rows, a.h, a.max_len);
   } else {
     a.splits = gather_splits(rows, a.h, a.d_qk, a.max_len);
-    const size_t room = decode_ws_bytes(rows, a.h, a.d_v, a.max_len);
+    const size_t room = decode_ws_bytes(rows, a.h, a.d_v, a.max_len, a.s);
     while (a.splits > 1 && attn_ws_bytes(rows, a.h, a.d_v, a.splits) > room) a.splits--;
   }
   const bool partials = a.splits > 1;
@@ -436,7 +496,7 @@ int qcau_forward(const void* c_q, const void* wq_b, const void* wq_b_scale, int3
 }
 
 size_t qcau_decode_attn_workspace_size(int64_t b, int64_t h, int64_t d_v, int64_t max_seqlen) {
-  return decode_ws_bytes(b, h, d_v, max_seqlen);
+  return decode_ws_bytes(b, h, d_v, max_seqlen, 1);
 }
 
 int qcau_decode_attn_paged(const void* q, const void* cache, const int32_t* block_table,
@@ -569,7 +629,7 @@ int qcau_sparse_attn_fp8(const void* q, const void* kv_latent, const float* kv_s
 
 size_t qcau_prefill_attn_workspace_size(int64_t b, int64_t s, int64_t h, int64_t d_v,
                                         int64_t max_seqlen) {
-  return decode_ws_bytes(b * s, h, d_v, max_seqlen);
+  return decode_ws_bytes(b * s, h, d_v, max_seqlen, s);
 }
 
 int qcau_prefill_attn_paged(const void* q, const void* cache, const int32_t* block_table,
@@ -949,7 +1009,7 @@ static MlaWs mla_ws(const qcau_mla_dims* d) {
   w.ov = off; off += align256(B * H * d->d_v * 2);
   w.xo = off; off += align256(B * H * d->d_v);
   w.so = off; off += align256(B * ((H * d->d_v) / 128) * 4);
-  w.attn = off; off += decode_ws_bytes(d->batch, d->n_heads, d->kv_lora, d->max_seqlen);
+  w.attn = off; off += decode_ws_bytes(d->batch, d->n_heads, d->kv_lora, d->max_seqlen, 1);
   w.total = off;
   return w;
 }

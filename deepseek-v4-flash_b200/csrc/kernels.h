@@ -159,6 +159,15 @@ struct AttnArgs {
   uint32_t* peer_flag[16];
   unsigned int* done_counter;
   uint32_t epoch;
+  // Balanced decode schedule of the pair kernel (one query token per
+  // sequence), when stream != 0: the tiles of every (row, head group), row
+  // after row at max_len, are cut into stream_pairs equal ranges, one per
+  // CTA pair; the pieces of a row, in pair order, are its partial slots, and
+  // splits is the most pieces any row has.
+  int stream;
+  int64_t stream_nt;     // tiles of 128 tokens per row at max_len
+  int64_t stream_pairs;
+  int stream_usplits;    // the equal splits of the fall-back (<= splits; 0: splits)
 };
 
 // Wait (bounded, ~1 s) until flags[i] >= epoch (wrapping compare) for i < n;

@@ -55,7 +55,8 @@ typedef enum { QCAU_OUT_BF16 = 0, QCAU_OUT_F32 = 1 } qcau_out_dtype;
 
 /* Device error word bits (qcau_device_error). */
 #define QCAU_DEVERR_TIMEOUT 1   /* a bounded pipeline wait expired; the kernel returned early */
-#define QCAU_DEVERR_INDEX 2     /* a block-table entry was outside [0, num_pages) */
+#define QCAU_DEVERR_INDEX 2     /* a block-table entry was outside [0, num_pages), or a
+                                   decode sequence was longer than max_seqlen */
 
 /* Library version (major*10000 + minor*100 + patch). */
 int qcau_version(void);
@@ -164,10 +165,12 @@ int qcau_forward(const void* c_q, const void* wq_b, const void* wq_b_scale,
  * replaced by "all cached tokens"; same numerics as sparse_attn).
  *   q [b, h, d_qk] bf16; cache [num_pages, page_size, d_kv] bf16;
  *   block_table [b, max_pages] int32; seqlens [b] int32 (tokens per
- *   sequence, <= max_pages*page_size); attn_sink [h] or NULL;
+ *   sequence, <= max_seqlen <= max_pages*page_size); attn_sink [h] or NULL;
  *   o [b, h, d_v] bf16 (V = cache row[:d_v]).
  *   Split-KV: partial results go to the workspace and a combine kernel
- *   merges them (workspace >= qcau_decode_attn_workspace_size(...)).
+ *   merges them (workspace >= qcau_decode_attn_workspace_size(...)).  The
+ *   two-CTA kernel schedules every sequence at max_seqlen: a longer one is
+ *   cut there and raises QCAU_DEVERR_INDEX.
  *   On sm_100a with h a multiple of 128 or h in {16, 32, 64}, d_qk == 576,
  *   d_v == 512, page_size == 64
  *   this runs the tcgen05 two-CTA kernel; other shapes run the general

@@ -86,21 +86,36 @@ def test_sparse_attn_rejects_empty_kv():
     assert b"at least one latent row" in L.qcau_last_error()
 
 
+def _plan_slots(rows, max_len, rule, pairs=74):
+    """Partial slots of the balanced decode plan (128 heads): the most pieces
+    any row's 128-token tiles are cut into by 74 equal pair ranges, or 0 when
+    a pair would get fewer than 32 tiles, or fewer than 64 where the split
+    count `rule` is 1 (the split count runs then)."""
+    nt = (max_len + 127) // 128
+    g = rows * nt
+    pairs = max(1, min(pairs, g // 4))
+    if g < 32 * pairs or (rule <= 1 and g < 64 * pairs):
+        return 0
+    return max(((i + 1) * nt * pairs - 1) // g - ((i * nt + 1) * pairs - 1) // g + 1
+               for i in range(rows))
+
+
 def test_decode_split_counts_measured_best():
     """The two-CTA kernel's split counts at the shapes they were measured on
     (128 heads, 512-wide values, B200), read back from the workspace the
-    decode entry asks for (fp32 O and (max, sum) partials per split): 128
+    decode entry asks for (fp32 O and (max, sum) partials per slot): 128
     sequences x 32K in 4 splits, 64 x 32K and 128 x 4K unsplit (the faster
-    choices over 8 and 4 splits), 16 x 32K in 4."""
+    choices over 8 and 4 splits), 16 x 32K in 4; decode rows also get the
+    balanced plan's slots where it applies (the larger of the two counts)."""
     L = _lib.lib()
 
     def ws(b, splits):
         return b * splits * 128 * (512 + 2) * 4 if splits > 1 else 0
 
-    assert L.qcau_decode_attn_workspace_size(128, 128, 512, 32768) == ws(128, 4)
-    assert L.qcau_decode_attn_workspace_size(64, 128, 512, 32768) == 0
-    assert L.qcau_decode_attn_workspace_size(128, 128, 512, 4096) == 0
-    assert L.qcau_decode_attn_workspace_size(16, 128, 512, 32768) == ws(16, 4)
+    for b, ctx, rule in ((128, 32768, 4), (64, 32768, 1), (128, 4096, 1), (16, 32768, 4)):
+        assert L.qcau_decode_attn_workspace_size(b, 128, 512, ctx) == \
+            ws(b, max(rule, _plan_slots(b, ctx, rule))), (b, ctx)
+    assert _plan_slots(128, 32768, 4) == 2 and _plan_slots(128, 4096, 1) == 0
 
 
 @no_device
