@@ -204,18 +204,21 @@ def attn_only(batch: int, ctx: int, local: int):
     print(json.dumps({"attn_only": True, "batch": batch, "ctx": ctx}))
 
 
-def gemm_only(local: int):
+def gemm_only(local: int, m_rows: int = 0):
     """A small FP8 GEMM case for ncu and tuning: the decode layer's q-up
     ([128,1536] x [24576,1536]) and o-proj ([128,16384] x [7168,16384]) with
     fp32 128x128 block scales; 3 warm-up and 5 timed launches of each.  The
-    two weights (155 MB) exceed L2 and are read alternately."""
+    two weights (155 MB) exceed L2 and are read alternately.  m_rows > 0
+    gives both GEMMs that many rows (the prefill's 16384, or a smaller
+    profiling case)."""
     from qcau_b200 import _lib
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     gen = torch.Generator(device=dev).manual_seed(3)
     L = _lib.lib()
-    shapes = {"q_up": (BATCH, HEADS * 192, DC), "o_proj": (BATCH, DIM, HEADS * 128)}
+    m_ = m_rows if m_rows > 0 else BATCH
+    shapes = {"q_up": (m_, HEADS * 192, DC), "o_proj": (m_, DIM, HEADS * 128)}
     ops = {}
     for name, (m, n, k) in shapes.items():
         a = torch.randn(m, k, device=dev, generator=gen).to(torch.float8_e4m3fn)
@@ -293,6 +296,63 @@ def prefill_only(local: int):
     flops = 2.0 * B * HEADS * (S * (S + 1) / 2) * (WIDTH + 512)
     print(json.dumps({"prefill_only": True, "batch": B, "seq": S, "heads": HEADS, "ms": ms,
                       "TFLOP/s": flops / ms / 1e9, "workspace_bytes": need}))
+
+
+def prefill_layer(local: int, B: int = 4, S: int = 4096):
+    """The whole absorbed-MLA layer on a prefill: batch 4 x 4096 new tokens x
+    128 heads (q-up FP8 GEMM at M = 16384, RoPE, absorb, causal attention
+    over the paged cache, v-up, o-proj FP8 GEMM at M = 16384); device time of
+    the step and of each stage (CUDA events), with each stage's FLOPs."""
+    from qcau_b200 import _lib
+    from qcau_b200.mla import MLAConfig, MLADecodeLayer, make_paged_cache, precompute_freqs_cis
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = MLAConfig(n_heads=HEADS, dc=DC, dim=DIM)
+    layer = MLADecodeLayer(cfg, dev)
+    layer.random_weights(seed=0)
+    cache, table, sl = make_paged_cache(B, S, PAGE, WIDTH, dev, seed=0)
+    freqs = precompute_freqs_cis(64, S + 1, cfg.rope_theta, dev)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    q_lora = torch.randn(B, S, DC, device=dev, generator=gen)
+    q_lora = (q_lora * torch.rsqrt(q_lora.square().mean(-1, keepdim=True))).to(torch.bfloat16)
+    y = torch.empty(B, S, DIM, device=dev, dtype=torch.bfloat16)
+
+    def run():
+        layer.forward_prefill(q_lora, cache, table, sl, freqs, S, y)
+    ms = _time_ms(run, warmup=2, reps=3)
+    assert _lib.device_error() == 0
+    rows = B * S
+    fl = {"q_up_fp8": 2.0 * rows * HEADS * 192 * DC,
+          "absorb": 2.0 * rows * HEADS * 128 * 512,
+          "attention": 2.0 * B * HEADS * (S * (S + 1) / 2) * (WIDTH + 512),
+          "v_up": 2.0 * rows * HEADS * 512 * 128,
+          "o_proj_fp8": 2.0 * rows * DIM * HEADS * 128}
+    # per stage: the same calls one at a time between events
+    c = cfg
+    d = layer.dims(rows, table.size(1), cache.size(0), 1, freqs.size(0))
+    q2 = q_lora.reshape(rows, DC)
+    pos = (sl.to(torch.int64).view(B, 1) - S + 1 +
+           torch.arange(S, device=dev).view(1, S)).to(torch.int32).reshape(-1)
+    q_abs = torch.empty(rows, HEADS, WIDTH, device=dev, dtype=torch.bfloat16)
+    o_lat = torch.empty(rows, HEADS, 512, device=dev, dtype=torch.bfloat16)
+    L = _lib.lib()
+    need = L.qcau_prefill_attn_workspace_size(B, S, HEADS, 512, S)
+    ws = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+    st = {"q_up_rope_absorb": lambda: layer._q_stage(d, q2, pos, freqs, q_abs),
+          "attention": lambda: _lib.check(L.qcau_prefill_attn_paged(
+              q_abs.data_ptr(), cache.data_ptr(), table.data_ptr(), sl.data_ptr(), None,
+              o_lat.data_ptr(), B, S, HEADS, WIDTH, 512, WIDTH, PAGE, table.size(1),
+              cache.size(0), S, c.softmax_scale, ws.data_ptr(), need, _lib.stream_ptr(dev)),
+              "prefill"),
+          "v_up_o_proj": lambda: layer._out_stage(d, o_lat, y.view(rows, DIM))}
+    stages = {k: _time_ms(f, warmup=1, reps=3) for k, f in st.items()}
+    total = sum(fl.values())
+    _, tflops, kind = peaks()
+    print(json.dumps({"prefill_layer": True, "batch": B, "seq": S, "heads": HEADS, "ms": ms,
+                      "TFLOP/s": total / ms / 1e9, "flops": total, "stage_ms": stages,
+                      "stage_flops": fl, "bf16_peak_tflops": tflops, "peak_source": kind,
+                      "note": "FP8 GEMM FLOPs (q-up, o-proj) run at the FP8 rate, the rest bf16"}))
 
 
 def sparse_fp8_only(local: int, heads: int, rows: int = 131072):
@@ -381,6 +441,11 @@ def main():
                     help="profiling case: the layer's two FP8 GEMMs at batch 128")
     ap.add_argument("--prefill-only", action="store_true",
                     help="time the causal prefill attention, batch 4 x 4096 x 128 heads")
+    ap.add_argument("--gemm-m", type=int, default=0,
+                    help="rows of the --gemm-only GEMMs (default: the decode batch)")
+    ap.add_argument("--prefill-layer", action="store_true",
+                    help="time the whole layer on a prefill, batch 4 x 4096 x 128 heads, "
+                         "with its stages")
     ap.add_argument("--sparse-fp8-only", type=int, default=0, metavar="HEADS",
                     help="time the FP8-cache top-k sparse decode (batch 64, 131072 rows) at HEADS")
     ap.add_argument("--attn-split", default="rows", choices=["context", "rows", "heads"],
@@ -404,10 +469,13 @@ def main():
         attn_only(args.batch, args.ctx, local)
         return
     if args.gemm_only:
-        gemm_only(local)
+        gemm_only(local, args.gemm_m)
         return
     if args.prefill_only:
         prefill_only(local)
+        return
+    if args.prefill_layer:
+        prefill_layer(local)
         return
     if args.sparse_fp8_only:
         sparse_fp8_only(local, args.sparse_fp8_only, args.sparse_rows)

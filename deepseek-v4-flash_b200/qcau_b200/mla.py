@@ -134,6 +134,7 @@ class MLADecodeLayer:
         self.exchange = exchange
         self._cp = None
         self._rows = None
+        self._prefill = None
         self._peer = None
         # (stage name, CUDA event) marks of the split steps, recorded on the
         # compute stream when a caller sets this to a list (stage timing)
@@ -242,6 +243,54 @@ class MLADecodeLayer:
                                     positions.data_ptr(), freqs.data_ptr(), y.data_ptr(),
                                     ws.data_ptr(), ws.numel(), stream_ptr(self.device)),
               "mla_decode")
+        return y
+
+    def forward_prefill(self, q_lora, cache, block_table, seqlens, freqs, max_seqlen,
+                        y: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """A prefill (or chunked-prefill) step of the layer: y [B, S, dim] bf16.
+
+        q_lora [B, S, dc] holds the S new tokens of every sequence, whose
+        latent rows are already in the cache: seqlens[b] counts them, and
+        token t of sequence b attends causally over the first
+        seqlens[b] - S + 1 + t cached tokens and takes RoPE at that position
+        (the reference's prefill branch, model.py:517-528, on the paged
+        cache).  The stages are the decode layer's (q-up + RoPE + absorb; the
+        v-up and o-proj) on B * S rows, around the causal prefill attention;
+        across head shards y is all-reduced as in forward().
+        """
+        B, S = q_lora.shape[0], q_lora.shape[1]
+        rows = B * S
+        c = self.cfg
+        q2 = q_lora.reshape(rows, c.dc).contiguous()
+        pos = (seqlens.to(torch.int64).view(B, 1) - S + 1 +
+               torch.arange(S, device=self.device).view(1, S)).to(torch.int32).reshape(-1)
+        # the stage workspace holds no attention partials (max_seqlen 1)
+        d = self.dims(rows, block_table.size(1), cache.size(0), 1, freqs.size(0))
+        w = c.kv_lora + c.d_rope
+        need = lib().qcau_prefill_attn_workspace_size(B, S, self.n_local, c.kv_lora, max_seqlen)
+        pf = self._prefill
+        if pf is None or pf["rows"] != rows or pf["ws"].numel() < max(need, 1):
+            # the stage buffers, kept across steps (and readable by tests)
+            pf = self._prefill = {
+                "rows": rows,
+                "q_abs": torch.empty(rows, self.n_local, w, device=self.device,
+                                     dtype=torch.bfloat16),
+                "o_lat": torch.empty(rows, self.n_local, c.kv_lora, device=self.device,
+                                     dtype=torch.bfloat16),
+                "ws": torch.empty(max(need, 1), device=self.device, dtype=torch.uint8),
+            }
+        q_abs, o_lat, ws = pf["q_abs"], pf["o_lat"], pf["ws"]
+        self._q_stage(d, q2, pos, freqs, q_abs)
+        check(lib().qcau_prefill_attn_paged(
+            q_abs.data_ptr(), cache.data_ptr(), block_table.data_ptr(), seqlens.data_ptr(), None,
+            o_lat.data_ptr(), B, S, self.n_local, w, c.kv_lora, w, c.page_size,
+            block_table.size(1), cache.size(0), max_seqlen, c.softmax_scale, ws.data_ptr(),
+            need, stream_ptr(self.device)), "prefill_attn_paged")
+        if y is None:
+            y = torch.empty(B, S, c.dim, device=self.device, dtype=torch.bfloat16)
+        self._out_stage(d, o_lat, y.view(rows, c.dim))
+        if self.world_size > 1:
+            dist.all_reduce(y, group=self.group)
         return y
 
     def forward(self, q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen,
