@@ -87,9 +87,9 @@ constexpr uint32_t kTmemCols = 512;
 
 struct DecodeShared {
   uint64_t kfull[kKSlots];   // leader: K slot landed in both CTAs
-  uint64_t kempty[kKSlots];  // both: K slot consumed by QK
+  uint64_t kempty[kKSlots];  // both: K slot consumed by QK (the last slot: s_full)
   uint64_t vfull[kVSlots];   // leader: V slot landed in both CTAs
-  uint64_t vempty[kVSlots];  // both: V slot consumed by PV
+  uint64_t vempty[kVSlots];  // both: V slot consumed by PV (the last slot: p_free)
   uint64_t q_full;           // leader: Q landed in both CTAs
   uint64_t s_full[2];        // both: S(t) ready
   uint64_t s_free[2];        // leader: the 8 softmax warps have read S(t)
@@ -106,6 +106,9 @@ struct DecodeShared {
   int abort;
   long long tiles[8];  // per warp: the batch's tiles (the balanced schedule's check)
 };
+
+static_assert(kKSlots == kKPerTile && kVSlots == kVPerTile,
+              "each ring holds exactly one tile: slot i is box i of the tile");
 
 constexpr size_t kSmemBytes = 1024 + kQBytes + kPBytes + (size_t)kKSlots * kKSlot +
                               (size_t)kVSlots * kVSlot + sizeof(DecodeShared);
@@ -400,8 +403,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int it = 0; it < U.T && ok; it++) {
           const int t = U.t_begin + it;
           for (int i = 0; i < per_tile; i++, n++) {
+            // slot i of the ring holds box i of a tile (u = the tile's ordinal)
             const int slot = n % nslots, u = n / nslots;
-            if (!(ok = mbar_wait(&emptyb[slot], (u & 1) ^ 1, abort))) break;
+            // the tile's last box is released by the tile's completion commit
+            // (QK: s_full, PV: p_free); the others by their own empty barrier
+            if (slot == nslots - 1) {
+              if (u > 0 && !(ok = is_k ? mbar_wait(&sh->s_full[(u - 1) & 1], ((u - 1) >> 1) & 1, abort)
+                                       : mbar_wait(&sh->p_free, (u - 1) & 1, abort)))
+                break;
+            } else if (!(ok = mbar_wait(&emptyb[slot], (u & 1) ^ 1, abort))) {
+              break;
+            }
             if (leader) mbar_arrive_expect_tx(&fullb[slot], is_k ? 2 * kKSlot : 2 * kVSlot);
             last_use[slot] = u;
             const uint32_t fb = mapa_shared(smem_u32(&fullb[slot]), 0);
@@ -437,6 +449,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       bool ok = true;
       if (warp == 1) {
         const uint32_t idesc_qk = make_idesc(128, 128, kFmtBF16, kFmtBF16, false, false);
+        const uint64_t q_desc = make_sdesc(q_addr, 16, 1024), k_desc = make_sdesc(k_addr, 16, 1024);
         int nk = 0, gt = 0, nu = 0;  // K boxes consumed, tiles, units
         for (UnitCursor c = cursor_begin(p, balanced, pair, npairs); c.pos < c.end && ok;
              cursor_next(p, balanced, c, npairs)) {
@@ -449,22 +462,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               break;
             tc_fence_after();
             for (int g = 0; g < kKPerTile; g++, nk++) {
-              const int slot = nk % kKSlots, u = nk / kKSlots;
+              const int slot = g, u = gt;  // the ring holds one tile: box g in slot g
               if (!(ok = mbar_wait(&sh->kfull[slot], u & 1, abort))) break;
-              // chunk k = 3g + c: 4 MMAs of 16 dims, B = this CTA's 64 tokens (N = 128)
+              // chunk k = 3g + c: 4 MMAs of 16 dims, B = this CTA's 64 tokens (N = 128);
+              // descriptors advance by (byte offset >> 4) in their address field
+              const uint64_t qg = q_desc + (uint64_t)((3 * g * 8192) >> 4);
+              const uint64_t kg = k_desc + (uint64_t)((slot * kKSlot) >> 4);
 #pragma unroll
               for (int c = 0; c < 3; c++)
 #pragma unroll
                 for (int kk = 0; kk < 4; kk++)
-                  mma_bf16_pair(tmem + kTmemS + sb * 64,
-                                make_sdesc(q_addr + (3 * g + c) * 8192 + kk * 32, 16, 1024),
-                                make_sdesc(k_addr + slot * kKSlot + c * 8192 + kk * 32, 16, 1024),
-                                idesc_qk, (g | c | kk) != 0 ? 1u : 0u);
-              tc_commit_pair(&sh->kempty[slot], 3);
-              last_bar = &sh->kempty[slot];
-              last_phase = u & 1;
+                  mma_bf16_pair(tmem + kTmemS + sb * 64, qg + (uint64_t)((c * 8192 + kk * 32) >> 4),
+                                kg + (uint64_t)((c * 8192 + kk * 32) >> 4), idesc_qk,
+                                (g | c | kk) != 0 ? 1u : 0u);
+              if (g + 1 < kKPerTile) {  // the last box is released by s_full
+                tc_commit_pair(&sh->kempty[slot], 3);
+                last_bar = &sh->kempty[slot];
+                last_phase = u & 1;
+              }
             }
-            if (ok) tc_commit_pair(&sh->s_full[sb], 3);
+            if (ok) {
+              tc_commit_pair(&sh->s_full[sb], 3);
+              last_bar = &sh->s_full[sb];
+              last_phase = (gt >> 1) & 1;
+            }
           }
           // both CTAs' Q may be reloaded once the unit's QK MMAs have completed
           if (ok) tc_commit_pair(&sh->q_empty, 3);
@@ -472,6 +493,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       } else {
         const uint32_t idesc_pv = make_idesc(128, 256, kFmtBF16, kFmtBF16, false, true);
+        const uint64_t p_desc = make_sdesc(p_addr, 16, 1024), v_desc = make_sdesc(v_addr, 8192, 1024);
         int nv = 0, gt = 0, nu = 0;  // V pages consumed, tiles, units
         for (UnitCursor c = cursor_begin(p, balanced, pair, npairs); c.pos < c.end && ok;
              cursor_next(p, balanced, c, npairs)) {
@@ -483,7 +505,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (!(ok = mbar_wait<true>(&sh->p_full, gt & 1, abort))) break;
             tc_fence_after();
             for (int pg = 0; pg < kVPerTile; pg++, nv++) {
-              const int slot = nv % kVSlots, u = nv / kVSlots;
+              const int slot = pg, u = gt;  // the ring holds one tile: page pg in slot pg
               if (!(ok = mbar_wait(&sh->vfull[slot], u & 1, abort))) break;
               // PV MMA j takes chunks 2j, 2j+1 of each CTA's slot: its output
               // columns are dims 256r + 128j + [0, 128) of CTA r's half
@@ -492,17 +514,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int kk = 0; kk < 4; kk++) {
                   // 16 tokens of page pg: P chunk pg, V slot rows 16kk..16kk+15
-                  const uint64_t ad = make_sdesc(p_addr + pg * 8192 + kk * 32, 16, 1024);
+                  const uint64_t ad = p_desc + (uint64_t)((pg * 8192 + kk * 32) >> 4);
                   const uint64_t bd =
-                      make_sdesc(v_addr + slot * kVSlot + j * 16384 + kk * 2048, 8192, 1024);
+                      v_desc + (uint64_t)((slot * kVSlot + j * 16384 + kk * 2048) >> 4);
                   mma_bf16_pair(tmem + kTmemO + j * 128, ad, bd, idesc_pv,
                                 (it > 0 || pg > 0 || kk > 0) ? 1u : 0u);
                 }
-              tc_commit_pair(&sh->vempty[slot], 3);
-              last_bar = &sh->vempty[slot];
-              last_phase = u & 1;
+              if (pg + 1 < kVPerTile) {  // the last page is released by p_free
+                tc_commit_pair(&sh->vempty[slot], 3);
+                last_bar = &sh->vempty[slot];
+                last_phase = u & 1;
+              }
             }
-            if (ok) tc_commit_pair(&sh->p_free, 3);
+            if (ok) {
+              tc_commit_pair(&sh->p_free, 3);
+              last_bar = &sh->p_free;
+              last_phase = gt & 1;
+            }
           }
           if (ok) tc_commit_pair(&sh->o_full, 3);
           nu++;
