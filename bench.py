@@ -250,7 +250,8 @@ def gemm_only(local: int, m_rows: int = 0):
             times.append(ev[0].elapsed_time(ev[1]))
         t = sorted(times)[len(times) // 2] * 1e-3
         nbytes = n * k + m * k + m * n * 2 + (n // 128) * (k // 128) * 4 + m * (k // 128) * 4
-        res[name] = {"us": t * 1e6, "GB/s": nbytes / t / 1e9, "TFLOP/s": 2.0 * m * n * k / t / 1e12}
+        res[name] = {"us": t * 1e6, "GB/s": nbytes / t / 1e9, "frac_of_hbm": nbytes / t / 1e9 / peaks()[0],
+                     "TFLOP/s": 2.0 * m * n * k / t / 1e12}
     assert _lib.device_error() == 0
     print(json.dumps({"gemm_only": True, **res}))
 
