@@ -458,6 +458,8 @@ def main():
                          "stored by the attention kernel into the owning rank's memory")
     ap.add_argument("--sparse-rows", type=int, default=131072,
                     help="rows per sequence of the --sparse-fp8-only cache")
+    ap.add_argument("--no-graphs", action="store_true",
+                    help="run every decode step eagerly instead of replaying it from a CUDA graph")
     ap.add_argument("--stages", action="store_true",
                     help="after the timed steps, time the row-split step's stages (q-up, "
                          "all-to-alls, attention, out-projection, all-reduce) with CUDA "
@@ -497,7 +499,7 @@ def main():
                                 device_id=dev)
     cfg = MLAConfig(n_heads=HEADS, dc=DC, dim=DIM)
     layer = MLADecodeLayer(cfg, dev, rank=rank, world_size=ws, attn_split=args.attn_split,
-                           exchange=args.exchange)
+                           exchange=args.exchange, cuda_graphs=not args.no_graphs)
     cp = ws > 1 and args.attn_split == "context"
     rs = ws > 1 and args.attn_split == "rows"
     layer.random_weights(seed=0)
@@ -716,7 +718,10 @@ def main():
                                        if cp else
                                        f"head-shard tp{ws}, attention split by sequences "
                                        "(q and o all-to-all)" if rs else f"head-shard tp{ws}"),
-                       "l2": "inputs (4.83 GB cache) larger than L2; no flush"},
+                       "l2": "inputs (4.83 GB cache) larger than L2; no flush",
+                       "launch": ("eager launches" if args.no_graphs else
+                                  "each step replayed from a CUDA graph (kernels and "
+                                  "collectives), captured after one eager step")},
             "roofline": roof,
             "e2e": {"value": e2e_val, "unit": "tok/s",
                     "h2d_bytes_per_step": q_lora.numel() * 2,
@@ -738,6 +743,7 @@ def main():
     if ws > 1:
         dist.barrier()
         layer.close()   # peer receive buffers of the p2p exchange, if any (collective)
+        layer.release_graphs()
         dist.destroy_process_group()
 
 

@@ -123,7 +123,8 @@ class MLADecodeLayer:
     """Holds this rank's weight shards and runs one decode step per call."""
 
     def __init__(self, cfg: MLAConfig, device, rank: int = 0, world_size: int = 1,
-                 process_group=None, attn_split: str = "rows", exchange: str = "nccl"):
+                 process_group=None, attn_split: str = "rows", exchange: str = "nccl",
+                 cuda_graphs: bool = False):
         if cfg.n_heads % world_size:
             raise ValueError("n_heads must be divisible by the number of ranks")
         if attn_split not in ("heads", "context", "rows"):
@@ -139,6 +140,12 @@ class MLADecodeLayer:
         # (stage name, CUDA event) marks of the split steps, recorded on the
         # compute stream when a caller sets this to a list (stage timing)
         self.stage_events = None
+        # cuda_graphs: forward() replays each decode step from a CUDA graph
+        # (its kernels and collectives, captured after one eager step), one
+        # graph per set of tensors the step reads and writes; while
+        # stage_events is set, or without an output tensor, steps run eagerly
+        self.cuda_graphs = cuda_graphs
+        self._graphs = {}
         self.cfg = cfg
         self.device = torch.device(device)
         self.rank, self.world_size = rank, world_size
@@ -296,6 +303,32 @@ class MLADecodeLayer:
     def forward(self, q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen,
                 y: Optional[torch.Tensor] = None) -> torch.Tensor:
         """y [batch, dim] bf16, summed over the head shards."""
+        if self.cuda_graphs and y is not None and self.stage_events is None:
+            args = (q_lora, cache, block_table, seqlens, positions, freqs)
+            key = tuple((t.data_ptr(), tuple(t.shape)) for t in args) + (y.data_ptr(),
+                                                                          int(max_seqlen))
+            g = self._graphs.get(key)
+            if g is None:
+                # one eager step sets up the stage buffers and plans; the
+                # capture then records the same launches
+                self._step(q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen, y)
+                torch.cuda.synchronize(self.device)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self._step(q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen,
+                               y)
+                self._graphs[key] = g
+            g.replay()
+            return y
+        return self._step(q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen, y)
+
+    def release_graphs(self) -> None:
+        """Drop the captured steps (before the process group that their
+        collectives use is destroyed)."""
+        self._graphs.clear()
+
+    def _step(self, q_lora, cache, block_table, seqlens, positions, freqs, max_seqlen,
+              y: Optional[torch.Tensor] = None) -> torch.Tensor:
         rows = self.attn_split == "rows" and q_lora.size(0) % self.world_size == 0
         if self.world_size > 1 and rows:
             return self.forward_rows(q_lora, cache, block_table, seqlens, positions, freqs,
