@@ -204,6 +204,63 @@ def attn_only(batch: int, ctx: int, local: int):
     print(json.dumps({"attn_only": True, "batch": batch, "ctx": ctx}))
 
 
+def attn_sustained(local: int, seconds: float):
+    """The dominant kernel under sustained load: the decode attention of the
+    bench's workload (batch 128, 128 heads, ctx 32768, split-KV + combine)
+    launched back to back for `seconds`, timed with CUDA events on its
+    stream, with the SM clock and throttle reasons sampled during the loop.
+    time x clock compares it with the burst figure at another clock."""
+    from qcau_b200 import _lib
+    from qcau_b200.mla import make_paged_cache
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cache, table, seqlens = make_paged_cache(BATCH, CTX, PAGE, WIDTH, dev, seed=0)
+    gen = torch.Generator(device=dev).manual_seed(1)
+    q = torch.randn(BATCH, HEADS, WIDTH, device=dev, generator=gen).to(torch.bfloat16)
+    o = torch.empty(BATCH, HEADS, 512, device=dev, dtype=torch.bfloat16)
+    L = _lib.lib()
+    need = L.qcau_decode_attn_workspace_size(BATCH, HEADS, 512, CTX)
+    wsb = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+    stream = _lib.stream_ptr(dev)
+
+    def run():
+        _lib.check(L.qcau_decode_attn_paged(q.data_ptr(), cache.data_ptr(), table.data_ptr(),
+                                            seqlens.data_ptr(), None, o.data_ptr(), BATCH, HEADS,
+                                            WIDTH, 512, WIDTH, PAGE, table.size(1), cache.size(0),
+                                            CTX, 192 ** -0.5, wsb.data_ptr(), need, stream), "attn")
+
+    for _ in range(5):
+        run()
+    torch.cuda.synchronize(dev)
+    # launches per second, from a short burst: enough launches for `seconds`
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        run()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    n = max(10, int(seconds * 1000.0 / (e0.elapsed_time(e1) / 10)))
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0.record()
+    for _ in range(n):
+        run()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    assert _lib.device_error() == 0
+    ms = e0.elapsed_time(e1) / n
+    hbm, _, peak_kind = peaks()
+    nbytes = 4867751936
+    line = {"attn_sustained": True, "launches": n, "seconds": e0.elapsed_time(e1) / 1000.0,
+            "ms_per_launch": ms, "GB/s": nbytes / ms / 1e6, "frac_of_hbm": nbytes / ms / 1e6 / hbm,
+            "peak_source": peak_kind, "clocks": clk}
+    if clk.get("sm_mhz"):
+        line["ms_x_ghz"] = ms * clk["sm_mhz"] / 1000.0
+    print(json.dumps(line))
+
+
 def gemm_only(local: int, m_rows: int = 0):
     """A small FP8 GEMM case for ncu and tuning: the decode layer's q-up
     ([128,1536] x [24576,1536]) and o-proj ([128,16384] x [7168,16384]) with
@@ -458,6 +515,9 @@ def main():
                          "stored by the attention kernel into the owning rank's memory")
     ap.add_argument("--sparse-rows", type=int, default=131072,
                     help="rows per sequence of the --sparse-fp8-only cache")
+    ap.add_argument("--sustained", type=float, default=0.0, metavar="SECONDS",
+                    help="time the decode attention launched back to back for SECONDS, "
+                         "with clocks sampled (the sustained figure)")
     ap.add_argument("--no-graphs", action="store_true",
                     help="run every decode step eagerly instead of replaying it from a CUDA graph")
     ap.add_argument("--stages", action="store_true",
@@ -470,6 +530,9 @@ def main():
     ws, rank, local = dist_env()
     if args.attn_only:
         attn_only(args.batch, args.ctx, local)
+        return
+    if args.sustained > 0:
+        attn_sustained(local, args.sustained)
         return
     if args.gemm_only:
         gemm_only(local, args.gemm_m)
