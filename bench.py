@@ -450,6 +450,107 @@ def sparse_fp8_only(local: int, heads: int, rows: int = 131072):
                       "frac_of_hbm": nbytes / ms / 1e6 / hbm, "peak_source": peak_kind}))
 
 
+def _time_flushed_us(fn, flush, reps=7):
+    """Median device time (us) of fn(), each launch timed alone with CUDA
+    events after `flush` (a write larger than L2) evicted its inputs."""
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    fn()
+    fn()
+    times = []
+    for _ in range(reps):
+        flush.add_(1)
+        ev[0].record()
+        fn()
+        ev[1].record()
+        torch.cuda.synchronize()
+        times.append(ev[0].elapsed_time(ev[1]) * 1e3)
+    return sorted(times)[len(times) // 2]
+
+
+def producers_only(local: int):
+    """The producers either side of the decode attention, each at the model's
+    widths (V4-Flash: 64 heads of 512, index heads 64 x 128, top-512, ratio 4)
+    and a decode or prefill shape, timed per call with L2 flushed before it:
+
+    - kv_build: RMSNorm + RoPE + FP8 round trip of new 512-wide KV rows,
+      written into the cache by slot (decode: 128 rows; prefill: 4 x 4096);
+    - compressor: gated pooling of ratio-4 overlapping windows of the fp32
+      wkv / wgate projections, then kv_build into the cache (prefill 4 x 4096;
+      decode: 128 sequences, a step that closes a group);
+    - indexer: Hadamard + FP4 of the queries, q.k over the compressed keys,
+      ReLU x head weights, head sum, top-512 (decode: 128 sequences at 32768
+      tokens = 8192 compressed keys each);
+    - GOPU: grouped wo_a (8 groups x 1024 x 4096 bf16), act_quant, FP8 wo_b
+      [4096, 8192] (decode: 128 tokens).
+
+    Algorithmic bytes are the inputs read once and the outputs written once
+    (workspace round trips are not counted)."""
+    from qcau_b200 import _lib
+    from qcau_b200.cache import Compressor, kv_build
+    from qcau_b200.gopu import GOPU
+    from qcau_b200.indexer import Indexer
+    from qcau_b200.mla import precompute_freqs_cis, quantize_weight_fp8
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    flush = torch.zeros(64 << 20, device=dev, dtype=torch.float32)  # 256 MB > L2
+    hbm, _, peak_kind = peaks()
+    res = {}
+
+    def rec(name, us, nbytes, **kw):
+        res[name] = {"us": round(us, 2), "algorithmic_bytes": int(nbytes),
+                     "GB/s": round(nbytes / us / 1e3, 1),
+                     "frac_of_hbm": round(nbytes / us / 1e3 / hbm, 3), **kw}
+
+    d, rd = 512, 64
+    freqs = precompute_freqs_cis(rd, 32768 + 8, 10000.0, dev)
+    normw = torch.ones(d, device=dev)
+    for name, rows in (("kv_build_decode_b128", 128), ("kv_build_prefill_4x4096", 16384)):
+        x = torch.randn(rows, d, device=dev, generator=gen).to(torch.bfloat16)
+        pos = torch.arange(rows, device=dev, dtype=torch.int32) % 32768
+        cache = torch.zeros(rows + 64, d, device=dev, dtype=torch.bfloat16)
+        slots = torch.arange(rows, device=dev, dtype=torch.int32)
+        us = _time_flushed_us(lambda: kv_build(x, normw, freqs, pos, rope_dim=rd, cache=cache,
+                                               slots=slots, return_rows=False), flush)
+        rec(name, us, rows * (d * 2 * 2 + 8), rows=rows)
+
+    for name, b, s, sp in (("compressor_prefill_4x4096", 4, 4096, 0),
+                           ("compressor_decode_b128", 128, 1, 4095)):
+        comp = Compressor(d, 4, rd, max_batch=b, device=dev)
+        comp.kv_cache = torch.zeros(b, 1024, d, device=dev, dtype=torch.bfloat16)
+        comp.freqs_cis = torch.view_as_complex(freqs[:4104])
+        kv = torch.randn(b, s, 2 * d, device=dev, generator=gen)
+        sc = torch.randn(b, s, 2 * d, device=dev, generator=gen)
+        n_out = b * max(s // 4, 1)
+        us = _time_flushed_us(lambda: comp.forward(kv, sc, sp), flush)
+        state = 0 if s > 1 else comp.kv_state[:b].numel() * 4 * 2 * 2
+        rec(name, us, kv.numel() * 4 * 2 + n_out * d * 2 + state, batch=b, tokens=s)
+
+    b, h, t, k = 128, 64, 8192, 512
+    q = torch.randn(b, 1, h, 128, device=dev, generator=gen).to(torch.bfloat16)
+    keys = torch.randn(b, t, 128, device=dev, generator=gen).to(torch.bfloat16)
+    w = (torch.randn(b, 1, h, device=dev, generator=gen) * 0.01).to(torch.bfloat16)
+    ix = Indexer(n_heads=h, head_dim=128, index_topk=k, compress_ratio=4, device=dev)
+    us = _time_flushed_us(lambda: ix.forward(q, keys, w, 4 * t - 1, 0, rotate=True), flush)
+    rec("indexer_decode_b128_t8192", us, keys.numel() * 2 + q.numel() * 2 + w.numel() * 2
+        + b * k * 4, batch=b, heads=h, compressed_keys=t, topk=k,
+        score_workspace_bytes=b * h * t * 2)
+
+    rows, G, R, Dm = 128, 8, 1024, 4096
+    o = torch.randn(rows, 64, d, device=dev, generator=gen).to(torch.bfloat16)
+    wo_a = (torch.randn(G * R, 64 * d // G, device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+    wb, wbs = quantize_weight_fp8(torch.randn(Dm, G * R, device=dev, generator=gen) * 0.02, True)
+    m = GOPU(device=dev)
+    m.load_weights(wo_a, wb, wbs)
+    us = _time_flushed_us(lambda: m.forward_local(o), flush)
+    rec("gopu_decode_b128", us, wo_a.numel() * 2 + wb.numel() + wbs.numel() + o.numel() * 2
+        + rows * Dm * 2, rows=rows)
+    assert _lib.device_error() == 0
+    print(json.dumps({"producers_only": True, "peak_gbs": hbm, "peak_source": peak_kind,
+                      "l2": "flushed before each timed call", **res}))
+
+
 def stage_times(layer, q_lora, cache, table, seqlens, positions, freqs, y, dev, ws, steps):
     """Per-stage device time (us, mean over `steps` steps, max over ranks) of
     the row-split decode step: CUDA events recorded between its stages on the
@@ -506,6 +607,9 @@ def main():
                          "with its stages")
     ap.add_argument("--sparse-fp8-only", type=int, default=0, metavar="HEADS",
                     help="time the FP8-cache top-k sparse decode (batch 64, 131072 rows) at HEADS")
+    ap.add_argument("--producers", action="store_true",
+                    help="time the KV build, compressor, indexer top-k and GOPU at decode "
+                         "and prefill shapes, each with L2 flushed")
     ap.add_argument("--attn-split", default="rows", choices=["context", "rows", "heads"],
                     help="N > 1: split the attention of the head-sharded layer by context "
                          "(each rank 1/N of every sequence), by rows (each rank 1/N of the "
@@ -542,6 +646,9 @@ def main():
         return
     if args.prefill_layer:
         prefill_layer(local)
+        return
+    if args.producers:
+        producers_only(local)
         return
     if args.sparse_fp8_only:
         sparse_fp8_only(local, args.sparse_fp8_only, args.sparse_rows)
