@@ -22,7 +22,8 @@ CSRC = PKG_DIR / "csrc"
 BUILD = PKG_DIR / "_build"
 LIB = PKG_DIR / "qcau_b200" / "libqcau_b200.so"
 SOURCES = ["capi.cu", "act_quant.cu", "rope_norm.cu", "fp8_gemm.cu", "bmm.cu",
-           "attn_combine.cu", "attn_decode_sm100.cu", "attn_gather_sm100.cu", "kv_build.cu", "indexer.cu", "compress.cu"]
+           "attn_combine.cu", "attn_decode_sm100.cu", "attn_gather_sm100.cu", "kv_build.cu", "indexer.cu", "compress.cu",
+           "indexer_score_sm100.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
          "-I", str(REPO / "include")]

@@ -819,33 +819,23 @@ int qcau_rotate_fp4(void* x, int64_t rows, int64_t d, int32_t hadamard, int32_t 
 
 static int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
-static size_t indexer_raw_bytes(int64_t b, int64_t s, int64_t h, int64_t t) {
-  return align256((size_t)(b * s * h * round_up(t > 0 ? t : 1, 128) * 2));
-}
-
-size_t qcau_indexer_scores_workspace_size(int64_t b, int64_t s, int64_t h, int64_t t) {
-  return indexer_raw_bytes(b, s, h, t);
-}
+size_t qcau_indexer_scores_workspace_size(int64_t, int64_t, int64_t, int64_t) { return 0; }
 
 size_t qcau_indexer_topk_workspace_size(int64_t b, int64_t s, int64_t h, int64_t t) {
-  return indexer_raw_bytes(b, s, h, t) + align256((size_t)(b * s * t * 4));
+  (void)h;
+  return align256((size_t)(b * s * (t > 0 ? t : 0) * 4));
 }
 
-int qcau_indexer_scores(const void* q, const void* kv, const void* weights, float* score,
-                        int64_t b, int64_t s, int64_t h, int64_t d, int64_t t, int64_t kv_rows,
-                        void* workspace, size_t workspace_bytes, void* stream) {
-  QCAU_CHECK_ARG(q && kv && weights && score, "indexer_scores: NULL pointer");
+int qcau_indexer_raw_scores(const void* q, const void* kv, void* raw, int64_t b, int64_t s,
+                            int64_t h, int64_t d, int64_t t, int64_t kv_rows, void* stream) {
+  QCAU_CHECK_ARG(q && kv && raw, "indexer_raw_scores: NULL pointer");
   QCAU_CHECK_ARG(b >= 0 && s >= 0 && h > 0 && t >= 0 && kv_rows >= t,
-                 "indexer_scores: bad shape");
-  QCAU_CHECK_ARG(d % 64 == 0 && d > 0, "indexer_scores: head_dim must be a multiple of 64");
-  QCAU_CHECK_ARG(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kv)) & 15) == 0,
-                 "indexer_scores: q and kv must be 16-byte aligned");
-  const size_t need = indexer_raw_bytes(b, s, h, t);
-  if (workspace_bytes < need || !workspace)
-    return fail(QCAU_ERR_WORKSPACE,
-                "indexer_scores: workspace too small (need " + std::to_string(need) + " bytes)");
+                 "indexer_raw_scores: bad shape");
+  QCAU_CHECK_ARG(d % 64 == 0 && d > 0, "indexer_raw_scores: head_dim must be a multiple of 64");
+  QCAU_CHECK_ARG(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kv) |
+                   reinterpret_cast<uintptr_t>(raw)) & 15) == 0,
+                 "indexer_raw_scores: q, kv and raw must be 16-byte aligned");
   if (b * s == 0 || t == 0) return QCAU_OK;
-  cudaStream_t st = to_stream(stream);
   const int64_t tp = round_up(t, 128);
   // raw[b, (s, h), u] = q[b, s, h, :] . kv[b, u, :], the bf16 einsum
   // (model.py:518); the B tensor map holds the t rows that exist, the rest of
@@ -859,15 +849,33 @@ int qcau_indexer_scores(const void* q, const void* kv, const void* weights, floa
   m.b_rstride = d;
   m.b_kmajor = 1;
   m.b_rows = t;
-  m.c = workspace;
+  m.c = raw;
   m.c_bstride = s * h * tp;
   m.c_rstride = tp;
   m.batch = b;
   m.m = s * h;
   m.n = tp;
   m.k = d;
-  QCAU_CHECK_CUDA(launch_bf16_bmm(m, st));
-  QCAU_CHECK_CUDA(launch_index_score(workspace, weights, score, b * s, (int)h, t, tp, st));
+  QCAU_CHECK_CUDA(launch_bf16_bmm(m, to_stream(stream)));
+  return QCAU_OK;
+}
+
+int qcau_indexer_scores(const void* q, const void* kv, const void* weights, float* score,
+                        int64_t b, int64_t s, int64_t h, int64_t d, int64_t t, int64_t kv_rows,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  QCAU_CHECK_ARG(q && kv && weights && score, "indexer_scores: NULL pointer");
+  QCAU_CHECK_ARG(b >= 0 && s >= 0 && h > 0 && h <= 128 && t >= 0 && kv_rows >= t,
+                 "indexer_scores: bad shape (up to 128 heads a rank)");
+  QCAU_CHECK_ARG(d == 128, "indexer_scores: index_head_dim 128 is supported");
+  QCAU_CHECK_ARG(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(kv)) & 15) == 0,
+                 "indexer_scores: q and kv must be 16-byte aligned");
+  QCAU_CHECK_ARG((b * s * h) < (int64_t(1) << 31) && t < (int64_t(1) << 31),
+                 "indexer_scores: too many query heads or keys");
+  if (b * s == 0 || t == 0) return QCAU_OK;
+  QCAU_CHECK_CUDA(launch_indexer_score_sm100(q, kv, weights, score, b, s, h, t, kv_rows,
+                                             to_stream(stream)));
   return QCAU_OK;
 }
 
@@ -893,11 +901,9 @@ int qcau_indexer_topk(const void* q, const void* kv, const void* weights, int32_
   if (workspace_bytes < need || !workspace)
     return fail(QCAU_ERR_WORKSPACE,
                 "indexer_topk: workspace too small (need " + std::to_string(need) + " bytes)");
-  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-  const size_t raw_bytes = indexer_raw_bytes(b, s, h, t);
-  float* score = reinterpret_cast<float*>(ws + raw_bytes);
-  const int rc =
-      qcau_indexer_scores(q, kv, weights, score, b, s, h, d, t, kv_rows, ws, raw_bytes, stream);
+  float* score = reinterpret_cast<float*>(workspace);
+  const int rc = qcau_indexer_scores(q, kv, weights, score, b, s, h, d, t, kv_rows, nullptr, 0,
+                                     stream);
   if (rc != QCAU_OK) return rc;
   return qcau_topk(score, topk_idxs, b * s, t, k, s, start_pos == 0 ? ratio : 0, offset, stream);
 }
@@ -988,6 +994,76 @@ int qcau_kv_build(const void* kv_in, void* kv_out, int64_t rows, int64_t d,
   a.slots = cache ? cache_slots : nullptr;
   a.cache_rows = cache_rows;
   QCAU_CHECK_CUDA(launch_kv_build(a, to_stream(stream)));
+  return QCAU_OK;
+}
+
+int qcau_compressor_step(const float* kv, const float* score, const float* ape, float* kv_state,
+                         float* score_state, int64_t bsz, int64_t seqlen, int64_t d,
+                         int64_t ratio, int32_t overlap, int64_t start_pos,
+                         const float* norm_weight, float eps, const float* freqs, int64_t npos,
+                         int64_t rope_dim, int32_t rotate, int32_t round_scale, void* cache,
+                         int64_t cache_seq_rows, int64_t cache_offset, void* rows_out,
+                         void* stream) {
+  QCAU_CHECK_ARG(bsz >= 0 && seqlen >= 0 && ratio > 0 && start_pos >= 0,
+                 "compressor_step: bad shape");
+  QCAU_CHECK_ARG(d > 0 && d % 64 == 0 && d <= 1024 && rope_dim >= 0 && rope_dim % 2 == 0 &&
+                     rope_dim <= d, "compressor_step: bad head_dim or rope_dim");
+  QCAU_CHECK_ARG(rotate ? d == 128 : (d - rope_dim) % 64 == 0,
+                 "compressor_step: the rotated rows must be 128 wide, the others have a "
+                 "multiple of 64 values below the rope part");
+  QCAU_CHECK_ARG(start_pos == 0 || seqlen == 1, "compressor_step: decode steps have one token");
+  QCAU_CHECK_ARG(kv_state && score_state, "compressor_step: the state is NULL");
+  QCAU_CHECK_ARG(rope_dim == 0 || (freqs && npos > 0), "compressor_step: RoPE needs freqs");
+  const int64_t n = start_pos == 0 ? seqlen / ratio : ((start_pos + 1) % ratio == 0 ? 1 : 0);
+  const int64_t first = start_pos == 0 ? 0 : start_pos / ratio;
+  QCAU_CHECK_ARG(bsz * seqlen == 0 || (kv && score && ape), "compressor_step: NULL input");
+  QCAU_CHECK_ARG(bsz * n == 0 || rows_out, "compressor_step: rows_out is NULL");
+  QCAU_CHECK_ARG(cache == nullptr || (cache_seq_rows > 0 && cache_offset >= 0 &&
+                                      cache_offset + first + n <= cache_seq_rows),
+                 "compressor_step: the compressed rows do not fit the cache rows of a sequence");
+  QCAU_CHECK_ARG(((reinterpret_cast<uintptr_t>(rows_out) | reinterpret_cast<uintptr_t>(cache)) &
+                  15) == 0, "compressor_step: rows_out and cache must be 16-byte aligned");
+  if (bsz * seqlen == 0) return QCAU_OK;
+  cudaStream_t st = to_stream(stream);
+  // pooled rows [bsz, n, d] bf16 into rows_out, then built there in place
+  QCAU_CHECK_CUDA(launch_compress(kv, score, ape, kv_state, score_state, rows_out, bsz, seqlen,
+                                  (int)d, (int)ratio, overlap ? 1 : 0, start_pos, st));
+  if (n == 0) return QCAU_OK;
+  KvBuildArgs a{};
+  a.in = rows_out;
+  a.out = rows_out;
+  a.rows = bsz * n;
+  a.d = d;
+  a.norm_weight = norm_weight;
+  a.norm_dim = (int)d;
+  a.eps = eps;
+  a.freqs = freqs;
+  a.npos = npos;
+  a.rope_dim = (int)rope_dim;
+  a.quant_dims = rotate ? 0 : (int)(d - rope_dim);
+  a.round_scale = round_scale ? 1 : 0;
+  // compressed row i of sequence b: position (first + i) * ratio, cache row
+  // b * cache_seq_rows + cache_offset + first + i (model.py:459-476)
+  a.seq_rows = n;
+  a.pos_base = first * ratio;
+  a.pos_step = ratio;
+  a.slot_seq_stride = cache_seq_rows;
+  a.slot_base = cache_offset + first;
+  if (!rotate) {
+    a.cache = cache;
+    a.cache_rows = cache ? bsz * cache_seq_rows : 0;
+  }
+  QCAU_CHECK_CUDA(launch_kv_build(a, st));
+  if (rotate) {
+    QCAU_CHECK_CUDA(launch_rotate_fp4(rows_out, bsz * n, 1, 1, st));
+    if (cache) {
+      const size_t row_bytes = (size_t)d * 2;
+      QCAU_CHECK_CUDA(cudaMemcpy2DAsync(
+          reinterpret_cast<uint8_t*>(cache) + (size_t)(cache_offset + first) * row_bytes,
+          (size_t)cache_seq_rows * row_bytes, rows_out, (size_t)n * row_bytes,
+          (size_t)n * row_bytes, (size_t)bsz, cudaMemcpyDeviceToDevice, st));
+    }
+  }
   return QCAU_OK;
 }
 

@@ -31,6 +31,7 @@ constexpr int kMaxWin = 2 * 128;  // entries of one window (2 * ratio with overl
 template <class Entry>
 __device__ __forceinline__ float pool_window(Entry entry, int w) {
   float m = -INFINITY;
+#pragma unroll 8
   for (int j = 0; j < w; j++) {
     float k, sc;
     entry(j, k, sc);
@@ -38,12 +39,14 @@ __device__ __forceinline__ float pool_window(Entry entry, int w) {
   }
   if (m == -INFINITY) return 0.f;  // cannot happen: the current group's scores are finite
   float sum = 0.f;
+#pragma unroll 8
   for (int j = 0; j < w; j++) {
     float k, sc;
     entry(j, k, sc);
     sum += expf(sc - m);
   }
   float acc = 0.f;
+#pragma unroll 8
   for (int j = 0; j < w; j++) {
     float k, sc;
     entry(j, k, sc);
@@ -52,7 +55,43 @@ __device__ __forceinline__ float pool_window(Entry entry, int w) {
   return acc;
 }
 
-// One thread per (sequence, group, channel c < d).
+// The same pooling with the window's W entries loaded into registers first,
+// so their loads are in flight together instead of one after another (the
+// ratio-4 compressors: W = 8 with overlap, 4 without).  Same arithmetic, in
+// the same order, as pool_window.
+template <int W, class Entry>
+__device__ __forceinline__ float pool_window_regs(Entry entry) {
+  float k[W], sc[W];
+#pragma unroll
+  for (int j = 0; j < W; j++) entry(j, k[j], sc[j]);
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < W; j++) m = fmaxf(m, sc[j]);
+  if (m == -INFINITY) return 0.f;
+  float e[W], sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < W; j++) {
+    e[j] = expf(sc[j] - m);
+    sum += e[j];
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < W; j++) acc += k[j] * (e[j] / sum);
+  return acc;
+}
+
+template <int W, class Entry>
+__device__ __forceinline__ float pool(Entry entry, int w) {
+  if constexpr (W > 0) {
+    return pool_window_regs<W>(entry);
+  } else {
+    return pool_window(entry, w);
+  }
+}
+
+// One thread per (sequence, group, channel c < d); W = the window's entries
+// when known at compile time, else 0.
+template <int W>
 __global__ void compress_prefill_kernel(const float* __restrict__ kv, const float* __restrict__ score,
                                         const float* __restrict__ ape, __nv_bfloat16* __restrict__ out,
                                         int64_t bsz, int64_t seqlen, int d, int ratio, int overlap) {
@@ -83,7 +122,7 @@ __global__ void compress_prefill_kernel(const float* __restrict__ kv, const floa
     k = kvb[t * cw + ch];
     sc = scb[t * cw + ch] + ape[jj * cw + ch];
   };
-  const float v = pool_window(entry, overlap ? 2 * ratio : ratio);
+  const float v = pool<W>(entry, overlap ? 2 * ratio : ratio);
   out[(b * groups + g) * d + c] = __float2bfloat16_rn(v);
 }
 
@@ -128,6 +167,7 @@ __global__ void compress_state_prefill_kernel(const float* __restrict__ kv,
 
 // One decode token per sequence (model.py:441-457): one thread per
 // (sequence, channel c < d), which owns channels c and d + c of the state.
+template <int W>
 __global__ void compress_decode_kernel(const float* __restrict__ kv, const float* __restrict__ score,
                                        const float* __restrict__ ape, float* __restrict__ kv_state,
                                        float* __restrict__ score_state,
@@ -157,8 +197,9 @@ __global__ void compress_decode_kernel(const float* __restrict__ kv, const float
     k = ks[j * cw + ch];
     sc = ss[j * cw + ch];
   };
-  out[b * d + c] = __float2bfloat16_rn(pool_window(entry, overlap ? 2 * ratio : ratio));
+  out[b * d + c] = __float2bfloat16_rn(pool<W>(entry, overlap ? 2 * ratio : ratio));
   if (overlap) {  // state[:ratio] = state[ratio:] (model.py:451-452)
+#pragma unroll 4
     for (int j = 0; j < ratio; j++)
       for (int h = 0; h < 2; h++) {
         const int ch = c + h * d;
@@ -173,14 +214,18 @@ __global__ void compress_decode_kernel(const float* __restrict__ kv, const float
 cudaError_t launch_compress(const float* kv, const float* score, const float* ape, float* kv_state,
                             float* score_state, void* out, int64_t bsz, int64_t seqlen, int d,
                             int ratio, int overlap, int64_t start_pos, cudaStream_t st) {
-  if (ratio <= 0 || (overlap ? 2 * ratio : ratio) > kMaxWin) return cudaErrorInvalidValue;
+  const int w = overlap ? 2 * ratio : ratio;
+  if (ratio <= 0 || w > kMaxWin) return cudaErrorInvalidValue;
   __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
   if (start_pos == 0) {
     const int64_t n = bsz * (seqlen / ratio) * d;
-    if (n > 0)
-      compress_prefill_kernel<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(kv, score, ape, o, bsz,
-                                                                           seqlen, d, ratio, overlap);
-    const int64_t ns = bsz * (int64_t)(overlap ? 2 * ratio : ratio) * (overlap ? 2 * d : d);
+    if (n > 0) {
+      const unsigned grid = (unsigned)((n + 127) / 128);
+      auto kern = w == 8 ? compress_prefill_kernel<8>
+                  : w == 4 ? compress_prefill_kernel<4> : compress_prefill_kernel<0>;
+      kern<<<grid, 128, 0, st>>>(kv, score, ape, o, bsz, seqlen, d, ratio, overlap);
+    }
+    const int64_t ns = bsz * (int64_t)w * (overlap ? 2 * d : d);
     if (ns > 0 && kv_state)
       compress_state_prefill_kernel<<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(
           kv, score, ape, kv_state, score_state, bsz, seqlen, d, ratio, overlap);
@@ -188,9 +233,12 @@ cudaError_t launch_compress(const float* kv, const float* score, const float* ap
   }
   if (seqlen != 1) return cudaErrorInvalidValue;
   const int64_t n = bsz * d;
-  if (n > 0)
-    compress_decode_kernel<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(
-        kv, score, ape, kv_state, score_state, o, bsz, d, ratio, overlap, start_pos);
+  if (n > 0) {
+    auto kern = w == 8 ? compress_decode_kernel<8>
+                : w == 4 ? compress_decode_kernel<4> : compress_decode_kernel<0>;
+    kern<<<(unsigned)((n + 127) / 128), 128, 0, st>>>(kv, score, ape, kv_state, score_state, o,
+                                                      bsz, d, ratio, overlap, start_pos);
+  }
   return cudaGetLastError();
 }
 

@@ -106,33 +106,6 @@ __global__ void __launch_bounds__(256) rotate_fp4_kernel(__nv_bfloat16* __restri
       make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
 }
 
-// ---------------------------------------------------------------- weighted ReLU sum
-
-// raw [R, H, Tp] bf16 (the einsum, Tp >= T; R = B * S query rows),
-// w [R, H] bf16, score [R, T] fp32 holding the bf16 sums.  A warp per
-// (row, 32 positions); the heads are summed in order, in fp32, each product
-// rounded to bf16 first as the reference's bf16 tensors are.
-__global__ void __launch_bounds__(256) index_score_kernel(const __nv_bfloat16* __restrict__ raw,
-                                                          const __nv_bfloat16* __restrict__ w,
-                                                          float* __restrict__ score, int64_t rows,
-                                                          int h, int64_t t_len, int64_t t_pad) {
-  const int64_t task = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const int64_t tiles = (t_len + 31) / 32;
-  if (task >= rows * tiles) return;
-  const int64_t row = task / tiles;
-  const int64_t t = (task % tiles) * 32 + lane;
-  if (t >= t_len) return;
-  const __nv_bfloat16* rp = raw + row * h * t_pad + t;
-  const __nv_bfloat16* wp = w + row * h;
-  float acc = 0.f;
-  for (int hh = 0; hh < h; hh++) {
-    const float rv = fmaxf(__bfloat162float(rp[(int64_t)hh * t_pad]), 0.f);
-    acc += bf16_round(__fmul_rn(rv, __bfloat162float(wp[hh])));
-  }
-  score[row * t_len + t] = bf16_round(acc);
-}
-
 // ---------------------------------------------------------------- top-k
 
 constexpr int kTopkThreads = 1024;
@@ -360,16 +333,6 @@ cudaError_t launch_rotate_fp4(void* x, int64_t rows, int hadamard, int fp4, cuda
   if (rows == 0) return cudaSuccess;
   rotate_fp4_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
       reinterpret_cast<__nv_bfloat16*>(x), rows, hadamard, fp4);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_index_score(const void* raw, const void* w, float* score, int64_t rows, int h,
-                               int64_t t_len, int64_t t_pad, cudaStream_t st) {
-  const int64_t tasks = rows * ((t_len + 31) / 32);
-  if (tasks == 0) return cudaSuccess;
-  index_score_kernel<<<(unsigned)((tasks + 7) / 8), 256, 0, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(raw), reinterpret_cast<const __nv_bfloat16*>(w),
-      score, rows, h, t_len, t_pad);
   return cudaGetLastError();
 }
 

@@ -60,6 +60,10 @@ struct KvBuildArgs {
   void* cache;         // [cache_rows, d] bf16 or nullptr
   const int32_t* slots;  // [rows]: destination cache row, -1 to skip
   int64_t cache_rows;
+  // seq_rows > 0 replaces positions and slots by arithmetic: row r is new row
+  // i = r % seq_rows of sequence r / seq_rows, at position pos_base + i *
+  // pos_step and cache row (r / seq_rows) * slot_seq_stride + slot_base + i
+  int64_t seq_rows, pos_base, pos_step, slot_seq_stride, slot_base;
 };
 cudaError_t launch_kv_build(const KvBuildArgs& args, cudaStream_t st);
 
@@ -87,8 +91,13 @@ cudaError_t launch_bf16_bmm(const BmmArgs& args, cudaStream_t st);
 // of the raw scores with the prefill mask, the top-k selection, and the
 // window / compressed index lists.
 cudaError_t launch_rotate_fp4(void* x, int64_t rows, int hadamard, int fp4, cudaStream_t st);
-cudaError_t launch_index_score(const void* raw, const void* w, float* score, int64_t rows, int h,
-                               int64_t t_len, int64_t t_pad, cudaStream_t st);
+
+// The indexer's score rows score[r, u] = bf16(sum_h bf16(relu(bf16(q[r, h] .
+// kv[r / s, u])) * w[r, h])), fp32 [b * s, t], fused on tcgen05 (head_dim
+// 128, h <= 128).
+cudaError_t launch_indexer_score_sm100(const void* q, const void* kv, const void* w, float* score,
+                                       int64_t b, int64_t s, int64_t h, int64_t t,
+                                       int64_t kv_rows, cudaStream_t st);
 cudaError_t launch_topk(const float* score, int64_t rows, int64_t t_len, int k, int32_t* out,
                         int64_t offset, int64_t s_len, int mask_ratio, cudaStream_t st);
 // KV compressor gated pooling (compress.cu): prefill rows of the complete

@@ -61,8 +61,10 @@ __global__ void __launch_bounds__(256) kv_build_kernel(KvBuildArgs p, int* err) 
   }
 
   // RoPE of the last rope_dim values at this row's position
+  const int64_t seq = p.seq_rows > 0 ? r / p.seq_rows : 0;
+  const int64_t i_new = p.seq_rows > 0 ? r - seq * p.seq_rows : 0;
   if (p.rope_dim > 0) {
-    const int64_t pos = p.positions[r];
+    const int64_t pos = p.seq_rows > 0 ? p.pos_base + i_new * p.pos_step : p.positions[r];
     if (pos < 0 || pos >= p.npos) {
       if (lane == 0) raise_dev_error(err, QCAU_DEVERR_INDEX);
     } else {
@@ -87,15 +89,27 @@ __global__ void __launch_bounds__(256) kv_build_kernel(KvBuildArgs p, int* err) 
     if (64 * k < p.quant_dims) {
       const float amax = warp_max(fmaxf(fabsf(v[k].x), fabsf(v[k].y)));
       const float sc = act_scale(amax, p.round_scale);
-      float q0 = fminf(fmaxf(__fdiv_rn(v[k].x, sc), -448.f), 448.f);
-      float q1 = fminf(fmaxf(__fdiv_rn(v[k].y, sc), -448.f), 448.f);
+      float q0, q1;
+      if (p.round_scale) {
+        // sc = 2^e with -22 <= e <= 120: x * 2^-e is the exact quotient
+        // rounded once, the same number __fdiv_rn gives
+        const float inv = __uint_as_float((uint32_t)(254 - (int)(__float_as_uint(sc) >> 23)) << 23);
+        q0 = __fmul_rn(v[k].x, inv);
+        q1 = __fmul_rn(v[k].y, inv);
+      } else {
+        q0 = __fdiv_rn(v[k].x, sc);
+        q1 = __fdiv_rn(v[k].y, sc);
+      }
+      q0 = fminf(fmaxf(q0, -448.f), 448.f);
+      q1 = fminf(fmaxf(q1, -448.f), 448.f);
       v[k].x = bf16_round(__fmul_rn(e4m3_to_f32(f32_to_e4m3(q0)), sc));
       v[k].y = bf16_round(__fmul_rn(e4m3_to_f32(f32_to_e4m3(q1)), sc));
     }
   }
 
   __nv_bfloat162* out = p.out ? reinterpret_cast<__nv_bfloat162*>(p.out) + r * (p.d / 2) : nullptr;
-  int64_t slot = p.slots ? (int64_t)p.slots[r] : -1;
+  int64_t slot = p.seq_rows > 0 && p.cache ? seq * p.slot_seq_stride + p.slot_base + i_new
+                 : p.slots ? (int64_t)p.slots[r] : -1;
   if (slot >= p.cache_rows) {
     if (lane == 0) raise_dev_error(err, QCAU_DEVERR_INDEX);
     slot = -1;

@@ -105,6 +105,8 @@ SIGNATURES = {
     "qcau_kv_build": ([_P, _P, _I64, _I64, _P, _I64, _F, _P, _P, _I64, _I64, _I64, _I32, _P, _P,
                        _I64, _P], ctypes.c_int),
     "qcau_compress": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I64, _P], ctypes.c_int),
+    "qcau_compressor_step": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I64, _P, _F, _P,
+                              _I64, _I64, _I32, _I32, _P, _I64, _I64, _P, _P], ctypes.c_int),
     "qcau_rotate_fp4": ([_P, _I64, _I64, _I32, _I32, _P], ctypes.c_int),
     "qcau_indexer_topk_workspace_size": ([_I64, _I64, _I64, _I64], _SZ),
     "qcau_indexer_topk": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
@@ -112,6 +114,8 @@ SIGNATURES = {
     "qcau_indexer_scores_workspace_size": ([_I64, _I64, _I64, _I64], _SZ),
     "qcau_indexer_scores": ([_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P],
                             ctypes.c_int),
+    "qcau_indexer_raw_scores": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P],
+                                ctypes.c_int),
     "qcau_topk": ([_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P], ctypes.c_int),
     "qcau_index_lists_width": ([_I64, _I64, _I64, _I64, _I64], _I64),
     "qcau_index_lists": ([_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _I64, _P], ctypes.c_int),

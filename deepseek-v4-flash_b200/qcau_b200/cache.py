@@ -243,39 +243,30 @@ class Compressor:
         kv, score = kv.contiguous(), score.contiguous()
         if start_pos == 0:
             n = s // ratio
-            positions = torch.arange(n, device=kv.device, dtype=torch.int32) * ratio
-            first = 0
         else:
             if s != 1:
                 raise ValueError("decode steps have one token")
             n = 1 if (start_pos + 1) % ratio == 0 else 0
-            positions = torch.full((1,), start_pos + 1 - ratio, device=kv.device, dtype=torch.int32)
-            first = start_pos // ratio
-        pooled = torch.empty(b, max(n, 1), d, device=kv.device, dtype=torch.bfloat16)
+        first = 0 if start_pos == 0 else start_pos // ratio
+        if n and self.cache_offset + first + n > self.kv_cache.size(1):
+            raise ValueError("the compressed rows do not fit the cache")
+        freqs = self.freqs_cis
+        freqs = torch.view_as_real(freqs) if freqs.is_complex() else freqs
+        freqs = freqs.to(device=kv.device, dtype=torch.float32).contiguous()
+        w = self.norm_weight.to(device=kv.device, dtype=torch.float32).contiguous()
+        ape = self.ape.to(device=kv.device, dtype=torch.float32).contiguous()
+        rows = torch.empty(b, max(n, 1), d, device=kv.device, dtype=torch.bfloat16)
         # the state of the first b sequences (the reference's state[:bsz]) is
         # contiguous because the state rows of a sequence are
         ks, ss = self.kv_state[:b], self.score_state[:b]
-        check(lib().qcau_compress(kv.data_ptr(), score.data_ptr(), self.ape.data_ptr(),
-                                  ks.data_ptr(), ss.data_ptr(), pooled.data_ptr(), b, s, d, ratio,
-                                  int(self.overlap), start_pos, stream_ptr(kv.device)), "compress")
+        check(lib().qcau_compressor_step(
+            kv.data_ptr(), score.data_ptr(), ape.data_ptr(), ks.data_ptr(), ss.data_ptr(), b, s, d,
+            ratio, int(self.overlap), start_pos, w.data_ptr(), self.eps, freqs.data_ptr(),
+            freqs.size(0), self.rd, int(self.rotate),
+            1 if self.scale_fmt == "ue8m0" else 0, self.kv_cache.data_ptr(), self.kv_cache.size(1),
+            self.cache_offset, rows.data_ptr(), stream_ptr(kv.device)), "compressor_step")
         if n == 0:
             return None
-        pooled = pooled[:, :n]
-        rows_per_seq = self.kv_cache.size(1)
-        slots = (torch.arange(b, device=kv.device, dtype=torch.int32).unsqueeze(1) * rows_per_seq
-                 + self.cache_offset + first
-                 + torch.arange(n, device=kv.device, dtype=torch.int32).unsqueeze(0)).reshape(-1)
-        pos = positions.repeat(b)
-        if not self.rotate:
-            out = kv_build(pooled.reshape(-1, d), self.norm_weight, self.freqs_cis, pos,
-                           rope_dim=self.rd, norm_dim=d, quant_dims=d - self.rd,
-                           scale_fmt=self.scale_fmt, eps=self.eps, cache=self.kv_cache, slots=slots)
-            return out.view(b, n, d)
-        from .indexer import rotate_fp4_
-        out = kv_build(pooled.reshape(-1, d), self.norm_weight, self.freqs_cis, pos,
-                       rope_dim=self.rd, norm_dim=d, quant_dims=0, eps=self.eps)
-        rotate_fp4_(out)
-        self.kv_cache.view(-1, d).index_copy_(0, slots.long(), out)
-        return out.view(b, n, d)
+        return rows[:, :n]
 
     __call__ = forward

@@ -111,6 +111,26 @@ def get_compress_topk_idxs(ratio: int, bsz: int, seqlen: int, start_pos: int, of
     return w[..., 1:].contiguous()  # drop the one-wide window part
 
 
+def raw_scores(q: torch.Tensor, kv_cache: torch.Tensor, t: int) -> torch.Tensor:
+    """The indexer's einsum alone (model.py:518): raw [b, s, h, t] bf16 =
+    q[b, s, h, :] . kv_cache[b, u, :] for u < t.  Indexer.forward keeps this
+    intermediate on chip; this is for inspection."""
+    require_cuda(q, kv_cache)
+    b, s, h, d = q.shape
+    if q.dtype != torch.bfloat16 or kv_cache.dtype != torch.bfloat16:
+        raise ValueError("q and kv_cache must be bf16")
+    if kv_cache.dim() != 3 or kv_cache.size(2) != d or kv_cache.stride(2) != 1 \
+            or kv_cache.stride(1) != d or kv_cache.size(1) < t:
+        raise ValueError("kv_cache must be [>= b, >= t, head_dim] with contiguous rows")
+    q = q.contiguous()
+    tp = (t + 127) // 128 * 128
+    raw = torch.empty(b, s, h, tp, dtype=torch.bfloat16, device=q.device)
+    check(lib().qcau_indexer_raw_scores(q.data_ptr(), kv_cache.data_ptr(), raw.data_ptr(), b, s,
+                                        h, d, t, kv_cache.stride(0) // d, stream_ptr(q.device)),
+          "indexer_raw_scores")
+    return raw[..., :t]
+
+
 def topk(score: torch.Tensor, k: int, offset: int = 0, seqlen: Optional[int] = None,
          mask_ratio: int = 0) -> torch.Tensor:
     """Indices [..., k] int32 of the k largest of each row of score [..., T]
@@ -148,6 +168,8 @@ class Indexer:
             raise ValueError("the heads must divide over the ranks")
         if head_dim != 128:
             raise ValueError("index_head_dim 128 is supported")
+        if n_heads // world_size > 128:
+            raise ValueError("up to 128 index heads a rank are supported")
         self.n_heads, self.head_dim = n_heads, head_dim
         self.n_local_heads = n_heads // world_size
         self.index_topk, self.compress_ratio = index_topk, compress_ratio

@@ -358,6 +358,33 @@ int qcau_compress(const float* kv, const float* score, const float* ape, float* 
                   int64_t ratio, int32_t overlap, int64_t start_pos, void* stream);
 
 /* ------------------------------------------------------------------------
+ * compressor_step -- one whole Compressor.forward after its projections
+ * (QCAU/QCAU_inference/inference/model.py:415-476; Deepseek_origin/inference/
+ * model.py:317-377): qcau_compress's pooling, then on the compressed rows the
+ * kv_norm RMSNorm over all d values (fp32 norm_weight, NULL = ones), RoPE of
+ * the last rope_dim values at each row's first position, and either the FP8
+ * round trip of the values below the rope part (rotate 0, the attention's
+ * compressor) or the Hadamard rotation and FP4 round trip of qcau_rotate_fp4
+ * (rotate 1, the indexer's, d = 128); the rows are written to rows_out
+ * [bsz, n, d] bf16 and, when cache is not NULL, to the caller's cache
+ * [>= bsz, cache_seq_rows, d] bf16 at rows cache_offset + first + i of each
+ * sequence (model.py:472-475; the attention's compressed rows follow its
+ * window ring, cache_offset = window_size).  n = seqlen / ratio and first =
+ * 0 at a prefill (start_pos 0); at a decode step n = 1 when (start_pos + 1)
+ * % ratio == 0, else 0 (only the state is updated), and first = start_pos /
+ * ratio.  Row i sits at position (first + i) * ratio of freqs [npos,
+ * rope_dim/2, 2] fp32.  Positions and cache rows are computed on the device,
+ * so a decode step is two or three launches and no host-side tensors.
+ * ---------------------------------------------------------------------- */
+int qcau_compressor_step(const float* kv, const float* score, const float* ape, float* kv_state,
+                         float* score_state, int64_t bsz, int64_t seqlen, int64_t d,
+                         int64_t ratio, int32_t overlap, int64_t start_pos,
+                         const float* norm_weight, float eps, const float* freqs, int64_t npos,
+                         int64_t rope_dim, int32_t rotate, int32_t round_scale, void* cache,
+                         int64_t cache_seq_rows, int64_t cache_offset, void* rows_out,
+                         void* stream);
+
+/* ------------------------------------------------------------------------
  * Index-list producers: what the sparse attention's topk_idxs come from.
  *
  * qcau_rotate_fp4 -- in place on rows of 128 bf16 values: the Walsh-Hadamard
@@ -381,13 +408,15 @@ int qcau_compress(const float* kv, const float* score, const float* ape, float* 
  *   then topk_idxs [b, s, k] int32 = the k largest per row (score
  *   descending, equal scores by index ascending) + offset; entries past a
  *   row's finite scores are -1, as the reference's mask makes them.  k is
- *   min(index_topk, t) in the reference (<= 2048 here); d a multiple of 64.
- *   The workspace holds the raw scores and the score rows:
+ *   min(index_topk, t) in the reference (<= 2048 here); d must be 128 (the
+ *   model's index_head_dim) and h <= 128.  The score rows are computed in
+ *   one pass over the keys: the einsum's [b, s, h, t] output stays on chip.
+ *   The workspace holds the score rows:
  *   qcau_indexer_topk_workspace_size(b, s, h, t) bytes.
  *   Its two halves, for head-sharded ranks that all-reduce the score rows
  *   between them (model.py:520-521):
  *   qcau_indexer_scores -- score [b, s, t] fp32 (bf16 values), unmasked;
- *     workspace qcau_indexer_scores_workspace_size(b, s, h, t) bytes.
+ *     qcau_indexer_scores_workspace_size(b, s, h, t) is 0 (no workspace).
  *   qcau_topk -- topk_idxs [rows, k] of score [rows, t]: the k largest of a
  *     row, score descending then index ascending, + offset, -1 past the
  *     row's candidates; -inf is never taken, and with mask_ratio > 0 (a
@@ -408,6 +437,12 @@ int qcau_rotate_fp4(void* x, int64_t rows, int64_t d, int32_t hadamard, int32_t 
                     void* stream);
 size_t qcau_indexer_topk_workspace_size(int64_t b, int64_t s, int64_t h, int64_t t);
 size_t qcau_indexer_scores_workspace_size(int64_t b, int64_t s, int64_t h, int64_t t);
+/* qcau_indexer_raw_scores -- the einsum alone, raw [b, s * h, round_up(t,
+ *   128)] bf16 = q[b, s, h, :] . kv[b, u, :] (model.py:518; columns past t
+ *   are zero): the intermediate the fused score pass keeps on chip, for
+ *   inspection; d a multiple of 64, any h. */
+int qcau_indexer_raw_scores(const void* q, const void* kv, void* raw, int64_t b, int64_t s,
+                            int64_t h, int64_t d, int64_t t, int64_t kv_rows, void* stream);
 int qcau_indexer_scores(const void* q, const void* kv, const void* weights, float* score,
                         int64_t b, int64_t s, int64_t h, int64_t d, int64_t t, int64_t kv_rows,
                         void* workspace, size_t workspace_bytes, void* stream);

@@ -84,3 +84,73 @@ def test_compressor_rejects_bad_shapes():
     # a prefill shorter than the ratio compresses nothing but keeps its tokens
     assert comp(torch.ones(2, 3, 1024, device="cuda"), torch.zeros(2, 3, 1024, device="cuda"), 0) is None
     assert bool((comp.kv_state[:2, 4:7] == 1).all())
+
+
+def _unfused_step(comp, kv, score, start_pos, state):
+    """The same compressor step composed from qcau_compress, kv_build with
+    explicit positions and slots, and rotate_fp4: what qcau_compressor_step
+    computes on the device in one call."""
+    from qcau_b200.cache import kv_build
+    from qcau_b200.indexer import rotate_fp4_
+    b, s, _ = kv.shape
+    ratio, d = comp.ratio, comp.d
+    ks, ss = state
+    n = s // ratio if start_pos == 0 else int((start_pos + 1) % ratio == 0)
+    first = 0 if start_pos == 0 else start_pos // ratio
+    pooled = torch.empty(b, max(n, 1), d, device="cuda", dtype=torch.bfloat16)
+    _lib.check(_lib.lib().qcau_compress(kv.data_ptr(), score.data_ptr(), comp.ape.data_ptr(),
+                                        ks.data_ptr(), ss.data_ptr(), pooled.data_ptr(), b, s, d,
+                                        ratio, int(comp.overlap), start_pos,
+                                        _lib.stream_ptr(kv.device)), "compress")
+    if n == 0:
+        return None
+    rows_per_seq = comp.kv_cache.size(1)
+    i = torch.arange(n, device="cuda", dtype=torch.int32)
+    slots = (torch.arange(b, device="cuda", dtype=torch.int32).view(b, 1) * rows_per_seq
+             + comp.cache_offset + first + i.view(1, n)).reshape(-1)
+    pos = ((first + i) * ratio).repeat(b)
+    cache = comp.kv_cache.clone()
+    if not comp.rotate:
+        out = kv_build(pooled[:, :n].reshape(-1, d), comp.norm_weight, comp.freqs_cis, pos,
+                       rope_dim=comp.rd, quant_dims=d - comp.rd, cache=cache, slots=slots)
+    else:
+        out = kv_build(pooled[:, :n].reshape(-1, d), comp.norm_weight, comp.freqs_cis, pos,
+                       rope_dim=comp.rd, quant_dims=0)
+        rotate_fp4_(out)
+        cache.view(-1, d).index_copy_(0, slots.long(), out)
+    return out.view(b, n, d), cache
+
+
+@pytest.mark.parametrize("d,rotate,b,s,start_pos", [
+    (512, False, 4, 1024, 0),      # attention compressor, prefill
+    (512, False, 128, 1, 4095),    # decode step closing a group, bench batch
+    (512, False, 128, 1, 4093),    # decode step closing none: state only
+    (128, True, 8, 512, 0),        # indexer compressor (rotated), prefill
+    (128, True, 64, 1, 2047),      # indexer compressor, decode
+])
+def test_compressor_step_equals_unfused_chain(d, rotate, b, s, start_pos):
+    """qcau_compressor_step (one call: pooling, norm, RoPE, FP8 or rotation
+    and FP4, cache rows computed on the device) against the chain of the
+    separate entry points, bit for bit, cache included."""
+    gen = torch.Generator(device="cuda").manual_seed(d + b + s)
+    comp = Compressor(d, 4, 64, rotate=rotate, max_batch=b)
+    comp.ape.copy_(torch.randn(comp.ape.shape, device="cuda", generator=gen) * 0.1)
+    comp.norm_weight.copy_(1 + 0.1 * torch.randn(d, device="cuda", generator=gen))
+    comp.kv_cache = torch.zeros(b, 1200, d, dtype=torch.bfloat16, device="cuda")
+    comp.cache_offset = 128
+    comp.freqs_cis = torch.polar(torch.ones(8192, 32), torch.rand(8192, 32) * 6).cuda()
+    comp.kv_state.normal_(generator=gen)
+    comp.score_state.normal_(generator=gen)
+    kv = torch.randn(b, s, 2 * d, device="cuda", generator=gen)
+    sc = torch.randn(b, s, 2 * d, device="cuda", generator=gen)
+    state = (comp.kv_state[:b].clone(), comp.score_state[:b].clone())
+    want = _unfused_step(comp, kv, sc, start_pos, state)
+    got = comp(kv, sc, start_pos)
+    torch.cuda.synchronize()
+    assert torch.equal(comp.kv_state[:b], state[0]) and torch.equal(comp.score_state[:b], state[1])
+    if want is None:
+        assert got is None
+    else:
+        assert torch.equal(got, want[0])
+        assert torch.equal(comp.kv_cache, want[1])
+    assert _lib.device_error() == 0

@@ -86,10 +86,11 @@ def test_index_lists_bit_exact_with_reference(g):
     _ok()
 
 
-def _raw_from_workspace(ix, b, s, h, t):
-    tp = (t + 127) // 128 * 128
-    raw = ix._ws[: b * s * h * tp * 2].view(torch.bfloat16).view(b, s, h, tp)[..., :t]
-    return n_bf16(raw.contiguous())
+def _raw(q, kv, t):
+    """The einsum the indexer's fused score pass keeps on chip, from the
+    separate raw-score entry (the tcgen05 bmm): the scores below are checked
+    against the oracle's head sum of exactly these values."""
+    return n_bf16(I.raw_scores(q, kv, t).contiguous())
 
 
 def _check_topk_rows(got, want, score):
@@ -121,7 +122,7 @@ def test_indexer_forward_vs_reference_steps(g):
         got = got.cpu().numpy()
         want = g[f"step{i}/idx"]
         assert got.shape == want.shape
-        raw = _raw_from_workspace(ix, b, s, h, t)
+        raw = _raw(t_bf16(q), cache, t)
         ref_raw = IO.raw_scores(q, kv)
         d = np.abs(O.bf16_to_f32(raw) - O.bf16_to_f32(ref_raw))
         assert np.all(d <= np.spacing(np.abs(O.bf16_to_f32(ref_raw))) * 65536 + 0), i
@@ -153,7 +154,7 @@ def test_indexer_chain_bit_exact_with_oracle(b, s, start_pos, t, k):
     kk = min(k, t)
     assert got.shape == (b, s, kk)
     qr = IO.fp4_quant(IO.hadamard_rotate(n_bf16(q)))
-    raw = _raw_from_workspace(ix, b, s, h, t)
+    raw = _raw(I.rotate_fp4_(q.clone()), kv, t)
     ref_raw = IO.raw_scores(qr, n_bf16(kv))
     rf, gf = O.bf16_to_f32(ref_raw), O.bf16_to_f32(raw)
     assert np.all(np.abs(rf - gf) <= np.spacing(np.abs(rf)) * 65536)
@@ -186,3 +187,33 @@ def test_topk_prefill_mask_and_empty_rows():
     assert np.array_equal(got.cpu().numpy(), IO.topk(sc.cpu().numpy(), 8, 5, 33, 4))
     assert I.topk(torch.empty(3, 0, device="cuda"), 4).cpu().tolist() == [[-1] * 4] * 3
     _ok()
+
+
+@pytest.mark.parametrize("b,s,h,t,kv_rows", [
+    (128, 1, 64, 8192, 8192),    # the decode batch of 128 sequences at 32768 tokens (ratio 4)
+    (3, 1, 8, 300, 333),         # one rank of eight (64 heads / 8), ragged last tile, longer rows
+    (2, 5, 16, 129, 129),        # several query rows a sequence, one key past a tile
+    (2, 3, 48, 1000, 1024),      # heads padded to 64 in the MMA
+    (1, 2, 128, 640, 700),       # 128 heads a rank
+])
+def test_fused_score_rows_bit_exact_with_oracle(b, s, h, t, kv_rows):
+    """qcau_indexer_scores (one pass: the einsum in TMEM, ReLU x weight and the
+    head sum in the epilogue) against the oracle's head sum of the einsum's
+    bf16 values, bit for bit, on every row (sampled sequences at the decode
+    batch)."""
+    gen = torch.Generator(device="cuda").manual_seed(b * 7 + s * 5 + h + t)
+    q = torch.randn(b, s, h, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    kv = torch.randn(b, kv_rows, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    w = (torch.randn(b, s, h, device="cuda", generator=gen) * 0.01).to(torch.bfloat16)
+    score = torch.full((b * s, t), float("nan"), device="cuda")
+    L = _lib.lib()
+    _lib.check(L.qcau_indexer_scores(q.data_ptr(), kv.data_ptr(), w.data_ptr(), score.data_ptr(),
+                                     b, s, h, 128, t, kv_rows, None, 0,
+                                     _lib.stream_ptr(q.device)), "indexer_scores")
+    raw = I.raw_scores(q, kv, t)
+    _ok()
+    seqs = range(b) if b <= 8 else [0, 1, 37, 64, 100, 126, 127]
+    got = score.view(b, s, t)
+    for bi in seqs:
+        want = IO.index_scores(n_bf16(raw[bi].contiguous()), n_bf16(w[bi]))
+        assert np.array_equal(got[bi].cpu().numpy(), want.astype(np.float32)), bi

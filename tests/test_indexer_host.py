@@ -150,7 +150,13 @@ def test_library_rejects_bad_indexer_arguments():
     assert lib.qcau_topk(buf, buf, 1, 8, 4096, 0, 0, 0, None) == _lib.QCAU_ERR_INVALID
     assert lib.qcau_topk(buf, buf, 1, 8, 4, 0, 4, 0, None) == _lib.QCAU_ERR_INVALID  # mask, no seqlen
     need = lib.qcau_indexer_topk_workspace_size(2, 3, 8, 17)
-    assert need >= 2 * 3 * 8 * 128 * 2 + 2 * 3 * 17 * 4
+    assert need >= 2 * 3 * 17 * 4
+    assert lib.qcau_indexer_scores_workspace_size(2, 3, 8, 17) == 0
+    # the fused score pass: head_dim 128 and up to 128 heads a rank
+    assert lib.qcau_indexer_scores(buf, buf, buf, buf, 1, 1, 129, 128, 8, 8, None, 0,
+                                   None) == _lib.QCAU_ERR_INVALID
+    assert lib.qcau_indexer_scores(buf, buf, buf, buf, 1, 1, 8, 64, 8, 8, None, 0,
+                                   None) == _lib.QCAU_ERR_INVALID
     rc = lib.qcau_indexer_topk(buf, buf, buf, buf, 2, 3, 8, 128, 17, 17, 8, 0, 4, 0, buf, need - 1,
                                None)
     assert rc == _lib.QCAU_ERR_WORKSPACE
