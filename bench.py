@@ -871,7 +871,9 @@ def main():
     e2e_val = BATCH * args.steps / (float(te.item()) / 1000.0)
     assert _lib.device_error() == 0, "device error during the timed region"
 
-    launches_per_step = 8 + 1  # act_quant, gemm, rope, bmm, attention, combine, bmm, act_quant, gemm
+    # act_quant, gemm, bmm (absorb, with the query's RoPE in its epilogue),
+    # attention, combine, bmm (v-up, with the act_quant of its output), gemm
+    launches_per_step = 7
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws,

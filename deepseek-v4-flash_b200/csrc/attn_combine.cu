@@ -102,7 +102,7 @@ __global__ void attn_combine_kernel(AttnArgs p) {
 // The same merge for 512-wide outputs (the latent width), with the loads of
 // a split issued together: lane l holds dims 4l + 128k (k < 4), each
 // split's weight is computed once, and all four loads of a split precede its
-// arithmetic (two splits in flight).  An empty split (max -inf, its O never
+// arithmetic (four splits in flight).  An empty split (max -inf, its O never
 // written) is not loaded (the predicate is the same for the whole warp) and
 // adds zeros, so stale values never enter the sums.  The arithmetic and its
 // order are attn_combine_kernel's.
@@ -118,12 +118,25 @@ __global__ void __launch_bounds__(256) attn_combine512_kernel(AttnArgs p) {
   const int64_t pstride = p.part_split_major ? rows * p.h : p.h;  // between splits, in rows
   const float* ml = p.part_ml + prow0 * 2;
   const int64_t ml_stride = pstride * 2;
+  const int ns = p.splits;
+  // Up to 32 splits: lane i loads (m_i, l_i) of split i, so the warp's
+  // softmax states arrive in one round trip and are read back by shuffles in
+  // split order (the sums below are the same, term for term).
+  const bool lanes = ns <= 32;
+  float2 mine = make_float2(-INFINITY, 0.f);
+  if (lanes && lane < ns) mine = *reinterpret_cast<const float2*>(ml + lane * ml_stride);
+  auto m_of = [&](int i) {
+    return lanes ? __shfl_sync(0xffffffffu, mine.x, i) : ml[i * ml_stride];
+  };
+  auto l_of = [&](int i) {
+    return lanes ? __shfl_sync(0xffffffffu, mine.y, i) : ml[i * ml_stride + 1];
+  };
   float M = -INFINITY;
-  for (int i = 0; i < p.splits; i++) M = fmaxf(M, ml[i * ml_stride]);
+  for (int i = 0; i < ns; i++) M = fmaxf(M, m_of(i));
   float L = 0.f;
-  for (int i = 0; i < p.splits; i++) {
-    const float mi = ml[i * ml_stride];
-    if (mi != -INFINITY) L += ml[i * ml_stride + 1] * exp2f(mi - M);
+  for (int i = 0; i < ns; i++) {
+    const float mi = m_of(i), li = l_of(i);
+    if (mi != -INFINITY) L += li * exp2f(mi - M);
   }
   const float sk = p.sink ? p.sink[hh] * kLog2e : -INFINITY;
   if (M != -INFINITY)
@@ -137,9 +150,9 @@ __global__ void __launch_bounds__(256) attn_combine512_kernel(AttnArgs p) {
   for (int j = 0; j < 16; j++) a[j] = 0.f;
   const int64_t base = prow0 * 512 + lane * 4;
   const int64_t po_stride = pstride * 512;
-#pragma unroll 2
-  for (int i = 0; i < p.splits; i++) {
-    const float mi = ml[i * ml_stride];
+#pragma unroll 4
+  for (int i = 0; i < ns; i++) {
+    const float mi = m_of(i), li = l_of(i);
     const bool live = mi != -INFINITY;
     const int64_t e = base + i * po_stride;
     float v[16];
@@ -150,7 +163,7 @@ __global__ void __launch_bounds__(256) attn_combine512_kernel(AttnArgs p) {
 #pragma unroll
       for (int k = 0; k < 4; k++)
         u[k] = live ? *reinterpret_cast<const uint2*>(src + 128 * k) : make_uint2(0u, 0u);
-      w = live ? exp2f(mi - M) * ml[i * ml_stride + 1] : 0.f;
+      w = live ? exp2f(mi - M) * li : 0.f;
 #pragma unroll
       for (int k = 0; k < 4; k++) {
         const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u[k].x));

@@ -1125,12 +1125,27 @@ static int mla_q_stage(const qcau_mla_dims* d, const void* q_lora, const void* w
   QCAU_CHECK_CUDA(launch_fp8_gemm(ws + w.xq, ws + w.sq, wq_b, wq_b_scale, ws + w.q, B, H * dq,
                                   d->dc, a_e8, w_e8, 0, st));
   // RoPE on q_rope (last 64 of each head) at each sequence's position, in
-  // place and into the rope slot of q_abs (q_abs[:, :, kv_lora:])
+  // place and into the rope slot of q_abs (q_abs[:, :, kv_lora:]): done by
+  // the absorb's epilogue threads for the 64-dim rope of the 512-wide
+  // latent, by its own launch otherwise
   uint8_t* qa = reinterpret_cast<uint8_t*>(qabs);
-  QCAU_CHECK_CUDA(launch_rope_pairs(ws + w.q + d->d_nope * 2, dq, qa + d->kv_lora * 2, dabs,
-                                    freqs, positions, B, 1, H, (int)d->d_rope, 0, 0, st));
+  auto al16 = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  const bool fused_rope = d->d_rope == 64 && d->kv_lora % 256 == 0 && d->d_nope == 128 &&
+                          dq % 8 == 0 && dabs % 8 == 0 && al16(ws + w.q) && al16(qa) &&
+                          al16(freqs);
+  if (!fused_rope)
+    QCAU_CHECK_CUDA(launch_rope_pairs(ws + w.q + d->d_nope * 2, dq, qa + d->kv_lora * 2, dabs,
+                                      freqs, positions, B, 1, H, (int)d->d_rope, 0, 0, st));
   // q_abs[:, :, :512] = q_nope . W_UK ;  q_abs[:, :, 512:] = q_rope
   BmmArgs m{};
+  if (fused_rope) {
+    m.rope_x = ws + w.q + d->d_nope * 2;
+    m.rope_x_stride = dq;
+    m.rope_copy = qa + d->kv_lora * 2;
+    m.rope_copy_stride = dabs;
+    m.rope_freqs = freqs;
+    m.rope_pos = positions;
+  }
   m.a = ws + w.q;
   m.a_bstride = dq;
   m.a_rstride = H * dq;
@@ -1172,10 +1187,20 @@ static int mla_out_stage(const qcau_mla_dims* d, const void* olat, const void* w
   m.m = B;
   m.n = d->d_v;
   m.k = d->kv_lora;
+  // act_quant(o_v) in 1 x 128 blocks (one head's d_v values a block) comes
+  // out of the same epilogue: FP8 codes at x_o, scales at s_o
+  const bool fused_quant = d->d_v == 128;
+  if (fused_quant) {
+    m.q_codes = ws + w.xo;
+    m.q_scales = ws + w.so;
+    m.q_round_scale = d->act_round_scale;
+    m.q_scale_e8m0 = a_e8;
+  }
   QCAU_CHECK_CUDA(launch_bf16_bmm(m, st));
   // y = wo(act_quant(o_v))   (row-parallel partial; the caller all-reduces)
-  QCAU_CHECK_CUDA(launch_act_quant(ws + w.ov, ws + w.xo, ws + w.so, B, H * d->d_v, 128,
-                                   d->act_round_scale, a_e8, 0, st));
+  if (!fused_quant)
+    QCAU_CHECK_CUDA(launch_act_quant(ws + w.ov, ws + w.xo, ws + w.so, B, H * d->d_v, 128,
+                                     d->act_round_scale, a_e8, 0, st));
   QCAU_CHECK_CUDA(launch_fp8_gemm(ws + w.xo, ws + w.so, wo, wo_scale, y, B, d->dim, H * d->d_v,
                                   a_e8, w_e8, d->out_dtype == QCAU_OUT_F32, st));
   return QCAU_OK;

@@ -83,6 +83,24 @@ struct BmmArgs {
   int64_t c_bstride, c_rstride;
   int64_t batch, m, n, k;
   int64_t b_rows;  // rows of B that exist (0: n); TMA zero-fills the rest
+  // Optional act_quant of C in 1 x 128 blocks (act_quant.cu's arithmetic on
+  // the bf16 values of C): codes at q_codes with C's element strides, scales
+  // [m][c_rstride / 128] (fp32, or UE8M0 bytes with q_scale_e8m0).  Needs
+  // n == 128 and c_bstride, c_rstride multiples of 128.
+  void* q_codes;
+  void* q_scales;
+  int q_round_scale, q_scale_e8m0;
+  // Optional RoPE of a 64-value rope slice per (row r of batch entry g),
+  // done by the epilogue threads while the MMAs run (rope_norm.cu's
+  // rope_pairs arithmetic): the slice at rope_x + (r * batch + g) *
+  // rope_x_stride is rotated by rope_freqs[rope_pos[r]] (32 complex fp32),
+  // written back in place and to rope_copy + (r * batch + g) *
+  // rope_copy_stride.  Strides in elements, multiples of 8.
+  void* rope_x;
+  void* rope_copy;
+  int64_t rope_x_stride, rope_copy_stride;
+  const float* rope_freqs;
+  const int32_t* rope_pos;
 };
 cudaError_t launch_bf16_bmm(const BmmArgs& args, cudaStream_t st);
 

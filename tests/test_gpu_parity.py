@@ -629,3 +629,46 @@ def test_mla_decode_layer_128_heads_stagewise():
     assert np.array_equal(v["so"].cpu().numpy(), so)
     ref = O.f32_to_bf16(O.fp8_gemm(xo, so, n_u8(wo), wos.numpy()))
     assert_close_attn(f32(n_bf16(y)), f32(ref), "o-proj")
+
+
+@pytest.mark.parametrize("round_scale", [False, True])
+def test_mla_vup_fused_act_quant_bit_exact(round_scale):
+    """The v-up's epilogue quantises its own bf16 output (1 x 128 blocks, one
+    head's d_v values a block): codes and scales are bit for bit the
+    reference act_quant of the o_v it wrote, with fp32 and UE8M0 scales."""
+    import dataclasses
+    cfg = dataclasses.replace(MLAConfig(n_heads=16), act_round_scale=round_scale)
+    layer = MLADecodeLayer(cfg, "cuda")
+    layer.random_weights(seed=9, e8m0=round_scale)
+    B, ctx = 70, 256
+    cache, table, seqlens = make_paged_cache(B, ctx, 64, 576, "cuda", seed=10)
+    freqs = precompute_freqs_cis(64, 512, cfg.rope_theta, "cuda")
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    q_lora = torch.randn(B, cfg.dc, device="cuda", generator=gen).to(torch.bfloat16)
+    layer.forward(q_lora, cache, table, seqlens, seqlens.clone(), freqs, ctx)
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    v = _mla_ws_views(layer, B)
+    H = layer.n_local
+    xo, so = O.act_quant(n_bf16(v["ov"]), 128, round_scale)
+    assert np.array_equal(n_u8(v["xo"]), xo)
+    if round_scale:
+        got = layer._ws[_ws_offset(layer, B, "so"):][:B * H].cpu().numpy().reshape(B, H)
+        assert np.array_equal(np.ldexp(1.0, got.astype(np.int32) - 127).astype(np.float32), so)
+    else:
+        assert np.array_equal(v["so"].cpu().numpy(), so)
+
+
+def _ws_offset(layer, B, name):
+    """Byte offset of one intermediate in the decode layer's workspace."""
+    H, c = layer.n_local, layer.cfg
+    al = lambda n: (n + 255) // 256 * 256
+    sizes = [("xq", B * c.dc), ("sq", B * (c.dc // 128) * 4), ("q", B * H * 192 * 2),
+             ("qabs", B * H * 576 * 2), ("olat", B * H * 512 * 2), ("ov", B * H * 128 * 2),
+             ("xo", B * H * 128), ("so", B * H * 4)]
+    off = 0
+    for n_, sz in sizes:
+        if n_ == name:
+            return off
+        off += al(sz)
+    raise KeyError(name)
