@@ -13,10 +13,14 @@
 //   warp 0 TMA producer, warp 1 TMEM allocator + MMA issuer,
 //   warps 2-5 epilogue (TMEM -> bf16 rows).
 // BN is 128, or 256 for the absorb (B MN-major, K = 128, N = 512): there
-// 128 tiles of 128 columns took two waves of three CTAs per SM, each CTA a
-// load, a short MMA chain and an epilogue in series; 256-column tiles read
-// the shared A tile once for twice the weight bytes and fit one wave of two
-// CTAs per SM.
+// 512 CTAs of 128 columns (128 heads x 4) took two waves of three CTAs per
+// SM, each CTA a load, a short MMA chain and an epilogue in series; 256
+// columns read the shared A tile once for twice the weight bytes and fit
+// one wave of two CTAs per SM.
+// Epilogue options: the act_quant of C in 1 x 128 blocks (the v-up, whose
+// output rows are one head's 128 values), and the RoPE of a 64-value slice
+// of another tensor per (row, batch entry) done under the MMAs (the absorb,
+// for the query's rope part).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -30,8 +34,9 @@ constexpr int kThreads = 192;
 template <int BN>
 constexpr int stage_bytes() { return kTileBytes + BN * BK * 2; }
 
-// Stages of the TMA ring: 2 (66 KB, three CTAs per SM) when K fits in two
-// steps, as in the absorb (K = 128); 4 for longer K (the v-up, K = 512).
+// Stages of the TMA ring: 2 when K fits in two steps (66 KB and three CTAs
+// per SM at BN = 128; 98 KB and two CTAs per SM at BN = 256, the absorb);
+// 4 for longer K (the v-up, K = 512).
 template <int kStages>
 struct BmmShared {
   uint64_t full[kStages];
